@@ -1,0 +1,474 @@
+// api.cpp - the emugemm C ABI: handles, workspace and the emugemm_sgemm executor
+// (emugemm-cdna src/emugemm.cpp:75-87 workspace, :185-213 rho estimate, :285-358 executor).
+//
+// Every compute path runs CUDA kernels built for sm_100a; there is no CPU fallback. A handle refuses to
+// be created on any device other than compute capability 10.0.
+#include "emugemm_internal.h"
+
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+namespace emu {
+
+std::string live_arch_string();
+void tune_clear();
+int tc_gemm_bn(int fp16);
+size_t rho_ws_bytes(int M, int N, long K, int P, int sms);
+int launch_rho(const float* A, long lda, const float* B, long ldb, int M, int N, long K, int P, void* ws, int sms,
+               double* out2, void* stream);
+
+static std::atomic<unsigned long long> g_launches{0};
+void count_launch(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+static emugemm_status_t from_cuda(int e) {
+    if (e == 0) return EMUGEMM_STATUS_SUCCESS;
+    if (e == (int)cudaErrorMemoryAllocation) return EMUGEMM_STATUS_MEMORY_ERROR;
+    if (e == (int)cudaErrorInvalidValue) return EMUGEMM_STATUS_INVALID_VALUE;
+    return EMUGEMM_STATUS_INTERNAL_ERROR;
+}
+
+// Grow-only workspace slot (src/emugemm.cpp:79-87, but per handle and with an optional cap).
+void* ws_get(Handle* h, int slot, size_t bytes) {
+    if (bytes == 0) bytes = 256;
+    if (h->ws_size[slot] >= bytes) return h->ws[slot];
+    size_t total = 0;
+    for (int i = 0; i < kWsCount; ++i) total += (i == slot) ? 0 : h->ws_size[i];
+    if (h->ws_limit && total + bytes > h->ws_limit) return nullptr;
+    if (h->ws[slot]) {
+        cudaStreamSynchronize((cudaStream_t)h->stream);
+        cudaFree(h->ws[slot]);
+    }
+    h->ws[slot] = nullptr;
+    h->ws_size[slot] = 0;
+    if (cudaMalloc(&h->ws[slot], bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    h->ws_size[slot] = bytes;
+    return h->ws[slot];
+}
+
+// Runs `fn` with the handle's device current and restores the caller's device afterwards.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) { ok = false; return; }
+        if (prev != dev && cudaSetDevice(dev) != cudaSuccess) ok = false;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+static emugemm_status_t take_device_error(Handle* h) {
+    unsigned e = *reinterpret_cast<volatile unsigned*>(h->err_host);
+    if (e) {
+        *reinterpret_cast<volatile unsigned*>(h->err_host) = 0;
+        std::fprintf(stderr, "emugemm: a device-side wait timed out (flags 0x%x)\n", e);
+        return EMUGEMM_STATUS_TIMEOUT;
+    }
+    return EMUGEMM_STATUS_SUCCESS;
+}
+
+static emugemm_status_t sync_check(Handle* h) {
+    cudaError_t e = cudaStreamSynchronize((cudaStream_t)h->stream);
+    emugemm_status_t d = take_device_error(h);
+    if (d != EMUGEMM_STATUS_SUCCESS) return d;
+    return from_cuda((int)e);
+}
+
+// max|x| of a rows x cols matrix, read back to the host (synchronises the stream).
+static emugemm_status_t absmax(Handle* h, const float* X, long rows, long cols, long ld, float* out) {
+    float* d = (float*)ws_get(h, kWsScalar, 64);
+    if (!d) return EMUGEMM_STATUS_MEMORY_ERROR;
+    int e;
+    {
+        ProfScope ps(h, kProfScan);
+        e = launch_absmax(X, rows, cols, ld, d, h->stream);
+    }
+    if (e) return from_cuda(e);
+    float v = 0.f;
+    e = (int)cudaMemcpyAsync(&v, d, sizeof(float), cudaMemcpyDeviceToHost, (cudaStream_t)h->stream);
+    if (e) return from_cuda(e);
+    emugemm_status_t s = sync_check(h);
+    if (s != EMUGEMM_STATUS_SUCCESS) return s;
+    *out = v;
+    return EMUGEMM_STATUS_SUCCESS;
+}
+
+// src/emugemm.cpp:185-213. Returns < 0 on failure.
+static double estimate_rho(Handle* h, int M, int N, long K, const float* A, long lda, const float* B, long ldb,
+                           int P) {
+    if (P <= 0) P = 64;
+    if (M <= 0 || N <= 0 || K <= 0) return -1.0;
+    void* ws = ws_get(h, kWsRhoT1, rho_ws_bytes(M, N, K, P, h->num_sms));
+    double* out2 = (double*)ws_get(h, kWsRhoPart, 2 * sizeof(double));
+    if (!ws || !out2) return -1.0;
+    {
+        ProfScope ps(h, kProfRho);
+        if (launch_rho(A, lda, B, ldb, M, N, K, P, ws, h->num_sms, out2, h->stream)) return -1.0;
+    }
+    double v[2] = {0, 0};
+    if (cudaMemcpyAsync(v, out2, sizeof v, cudaMemcpyDeviceToHost, (cudaStream_t)h->stream) != cudaSuccess) return -1.0;
+    if (sync_check(h) != EMUGEMM_STATUS_SUCCESS) return -1.0;
+    const double num = std::sqrt(v[0] / (double)P), den = std::sqrt(v[1] / (double)P);
+    if (num < 0 || !(den > 0)) return -1.0;
+    return num / den;
+}
+
+ProfScope::ProfScope(Handle* h_, int kind_) : h(h_), kind(kind_) {
+    if (!h->profiling) return;
+    if (h->prof_n == h->prof_cap) {
+        int cap = h->prof_cap ? 2 * h->prof_cap : 64;
+        ProfRec* p = new ProfRec[cap];
+        for (int i = 0; i < h->prof_n; ++i) p[i] = h->prof[i];
+        delete[] h->prof;
+        h->prof = p;
+        h->prof_cap = cap;
+    }
+    cudaEvent_t a, b;
+    if (cudaEventCreate(&a) != cudaSuccess) return;
+    if (cudaEventCreate(&b) != cudaSuccess) { cudaEventDestroy(a); return; }
+    rec = &h->prof[h->prof_n++];
+    rec->a = a;
+    rec->b = b;
+    rec->kind = kind;
+    cudaEventRecord(a, (cudaStream_t)h->stream);
+}
+
+ProfScope::~ProfScope() {
+    if (rec) cudaEventRecord((cudaEvent_t)rec->b, (cudaStream_t)h->stream);
+}
+
+static void prof_clear(Handle* h) {
+    for (int i = 0; i < h->prof_n; ++i) {
+        cudaEventDestroy((cudaEvent_t)h->prof[i].a);
+        cudaEventDestroy((cudaEvent_t)h->prof[i].b);
+    }
+    h->prof_n = 0;
+}
+
+static long round_up(long x, long m) { return (x + m - 1) / m * m; }
+
+// bf16x3 / fp16x3 through the tensor-core kernel over pre-split slices.
+static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, long lda, const float* B, long ldb,
+                               float* C, long ldc, double* C64, long ldc64, bool fp16) {
+    const int BN = tc_gemm_bn(fp16 ? 1 : 0);
+    const long Mp = round_up(M, 128), Np = round_up(N, BN), Kp = round_up(K, 64);
+    if (Mp > 0x7fffffffL || Np > 0x7fffffffL || Kp > 0x7fffffffL) return EMUGEMM_STATUS_INVALID_SIZE;
+    uint16_t* a0 = (uint16_t*)ws_get(h, kWsSplitA0, (size_t)Mp * Kp * 2);
+    uint16_t* a1 = (uint16_t*)ws_get(h, kWsSplitA1, (size_t)Mp * Kp * 2);
+    uint16_t* b0 = (uint16_t*)ws_get(h, kWsSplitB0, (size_t)Np * Kp * 2);
+    uint16_t* b1 = (uint16_t*)ws_get(h, kWsSplitB1, (size_t)Np * Kp * 2);
+    if (!a0 || !a1 || !b0 || !b1) return EMUGEMM_STATUS_MEMORY_ERROR;
+    int* rexp = nullptr;
+    int* cexp = nullptr;
+    if (fp16) {
+        rexp = (int*)ws_get(h, kWsScaleA, (size_t)M * 4);
+        cexp = (int*)ws_get(h, kWsScaleB, (size_t)N * 8);
+        if (!rexp || !cexp) return EMUGEMM_STATUS_MEMORY_ERROR;
+        ProfScope ps(h, kProfScan);
+        int e = launch_row_exponents(A, M, K, lda, rexp, h->stream);
+        if (!e) e = launch_col_exponents(B, K, N, ldb, cexp, reinterpret_cast<unsigned*>(cexp + N), h->stream);
+        if (e) return from_cuda(e);
+    }
+    int e;
+    {
+        ProfScope ps(h, kProfSplit);
+        e = launch_split_rows(A, M, K, lda, (int)Mp, Kp, fp16 ? 1 : 0, rexp, a0, a1, h->stream);
+        if (!e) e = launch_split_cols(B, K, N, ldb, (int)Np, Kp, fp16 ? 1 : 0, cexp, b0, b1, h->stream);
+    }
+    if (e) return from_cuda(e);
+    TcGemmArgs t;
+    t.a_hi = a0; t.a_lo = a1; t.b_hi = b0; t.b_lo = b1;
+    t.M = M; t.N = N; t.Mp = (int)Mp; t.Np = (int)Np; t.Kp = Kp;
+    t.C = C; t.ldc = ldc; t.C64 = C64; t.ldc64 = ldc64;
+    t.fp16 = fp16 ? 1 : 0;
+    t.row_exp = rexp; t.col_exp = cexp;
+    t.err = h->err_dev;
+    t.num_sms = h->num_sms;
+    ProfScope ps(h, kProfTcGemm);
+    return from_cuda(launch_tc_gemm(t, h->stream));
+}
+
+static emugemm_status_t run_fp32(Handle* h, int M, int N, long K, const float* A, long lda, const float* B, long ldb,
+                                 float* C, long ldc, double* C64, long ldc64, int chunks) {
+    Fp32GemmArgs f;
+    f.A = A; f.lda = lda; f.B = B; f.ldb = ldb;
+    f.C = C; f.ldc = ldc; f.C64 = C64; f.ldc64 = ldc64;
+    f.M = M; f.N = N; f.K = K;
+    f.chunks = chunks < 1 ? 1 : chunks;
+    f.num_sms = h->num_sms;
+    f.bm = lookup_tile(M, N, K / f.chunks, 0).fp32_bm;
+    f.ws64 = nullptr;
+    size_t wsb = fp32_gemm_ws_bytes(f);
+    if (wsb) {
+        f.ws64 = (double*)ws_get(h, kWsF64Acc, wsb);
+        if (!f.ws64) return EMUGEMM_STATUS_MEMORY_ERROR;
+    }
+    ProfScope ps(h, kProfFp32Gemm);
+    return from_cuda(launch_fp32_gemm(f, h->stream));
+}
+
+// Zero an M x N output (K == 0).
+static emugemm_status_t zero_out(Handle* h, int M, int N, float* C, long ldc, double* C64, long ldc64) {
+    cudaError_t e;
+    if (C64)
+        e = cudaMemset2DAsync(C64, (size_t)ldc64 * 8, 0, (size_t)N * 8, (size_t)M, (cudaStream_t)h->stream);
+    else
+        e = cudaMemset2DAsync(C, (size_t)ldc * 4, 0, (size_t)N * 4, (size_t)M, (cudaStream_t)h->stream);
+    return from_cuda((int)e);
+}
+
+static emugemm_status_t dispatch(Handle* h, emu_scheme_t s, int chunks, int M, int N, long K, const float* A,
+                                 long lda, const float* B, long ldb, float* C, long ldc, double* C64, long ldc64) {
+    if (M == 0 || N == 0) return EMUGEMM_STATUS_SUCCESS;
+    if (K == 0) return zero_out(h, M, N, C, ldc, C64, ldc64);
+    switch (s) {
+        case EMU_SCHEME_NATIVE_FP32: return run_fp32(h, M, N, K, A, lda, B, ldb, C, ldc, C64, ldc64, 1);
+        case EMU_SCHEME_FP32_CHUNKED: return run_fp32(h, M, N, K, A, lda, B, ldb, C, ldc, C64, ldc64, chunks);
+        // A forced BF16X6 runs the bf16x3 kernel, as the reference does (src/emugemm.cpp:331).
+        case EMU_SCHEME_BF16X3:
+        case EMU_SCHEME_BF16X6: return run_tc(h, M, N, K, A, lda, B, ldb, C, ldc, C64, ldc64, false);
+        case EMU_SCHEME_FP16X3: return run_tc(h, M, N, K, A, lda, B, ldb, C, ldc, C64, ldc64, true);
+        default: return EMUGEMM_STATUS_NOT_IMPLEMENTED;
+    }
+}
+
+static bool is_sm100(int dev) {
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return false;
+    if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) return false;
+    return major == 10 && minor == 0;
+}
+
+}  // namespace emu
+
+using emu::Handle;
+
+extern "C" {
+
+emugemm_status_t emugemm_create_handle(emugemm_handle_t* out) {
+    if (!out) return EMUGEMM_STATUS_INVALID_POINTER;
+    *out = nullptr;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return EMUGEMM_STATUS_INTERNAL_ERROR; }
+    if (!emu::is_sm100(dev)) return EMUGEMM_STATUS_ARCH_MISMATCH;
+    Handle* h = new Handle();
+    h->device = dev;
+    cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaHostAlloc((void**)&h->err_host, sizeof(unsigned), cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer((void**)&h->err_dev, h->err_host, 0) != cudaSuccess) {
+        cudaGetLastError();
+        if (h->err_host) cudaFreeHost(h->err_host);
+        delete h;
+        return EMUGEMM_STATUS_MEMORY_ERROR;
+    }
+    *h->err_host = 0;
+    *out = reinterpret_cast<emugemm_handle_t>(h);
+    return EMUGEMM_STATUS_SUCCESS;
+}
+
+emugemm_status_t emugemm_destroy_handle(emugemm_handle_t handle) {
+    Handle* h = reinterpret_cast<Handle*>(handle);
+    if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
+    emu::DeviceGuard g(h->device);
+    cudaStreamSynchronize((cudaStream_t)h->stream);
+    for (int i = 0; i < emu::kWsCount; ++i)
+        if (h->ws[i]) cudaFree(h->ws[i]);
+    emu::prof_clear(h);
+    delete[] h->prof;
+    if (h->err_host) cudaFreeHost(h->err_host);
+    delete h;
+    return EMUGEMM_STATUS_SUCCESS;
+}
+
+emugemm_status_t emugemm_set_stream(emugemm_handle_t handle, void* stream) {
+    Handle* h = reinterpret_cast<Handle*>(handle);
+    if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
+    h->stream = stream;
+    return EMUGEMM_STATUS_SUCCESS;
+}
+
+emugemm_status_t emugemm_set_workspace_limit(emugemm_handle_t handle, size_t bytes) {
+    Handle* h = reinterpret_cast<Handle*>(handle);
+    if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
+    h->ws_limit = bytes;
+    return EMUGEMM_STATUS_SUCCESS;
+}
+
+emugemm_status_t emugemm_sync(emugemm_handle_t handle) {
+    Handle* h = reinterpret_cast<Handle*>(handle);
+    if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
+    emu::DeviceGuard g(h->device);
+    return emu::sync_check(h);
+}
+
+void emugemm_shutdown(void) { emu::tune_clear(); }
+
+emugemm_status_t emugemm_sgemm_ex(emugemm_handle_t handle, int M, int N, long K, const float* A, long lda,
+                                  const float* B, long ldb, float* C, long ldc, const emu_request_t* req,
+                                  emu_hints_t* hints, emu_plan_t* out_plan) {
+    Handle* h = reinterpret_cast<Handle*>(handle);
+    if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
+    if (M < 0 || N < 0 || K < 0) return EMUGEMM_STATUS_INVALID_SIZE;
+    if (lda < (K > 0 ? K : 1) || ldb < (N > 0 ? N : 1) || ldc < (N > 0 ? N : 1)) return EMUGEMM_STATUS_INVALID_SIZE;
+    if ((M > 0 && N > 0) && (!C || (K > 0 && (!A || !B)))) return EMUGEMM_STATUS_INVALID_POINTER;
+    emu::DeviceGuard g(h->device);
+    if (!g.ok) return EMUGEMM_STATUS_INTERNAL_ERROR;
+
+    // src/emugemm.cpp:288-294: hints are in/out; NULL means measure everything with 64 probes.
+    emu_hints_t local = hints ? *hints : emu_hints_t{-1.f, -1.f, 0, -1.f, 0};
+    const bool have_a = (long)M * K > 0, have_b = K * (long)N > 0;
+    if (local.a_absmax < 0) {
+        float v = 0.f;
+        if (have_a) {
+            emugemm_status_t s = emu::absmax(h, A, M, K, lda, &v);
+            if (s != EMUGEMM_STATUS_SUCCESS) return s;
+        }
+        local.a_absmax = v;
+    }
+    if (local.b_absmax < 0) {
+        float v = 0.f;
+        if (have_b) {
+            emugemm_status_t s = emu::absmax(h, B, K, N, ldb, &v);
+            if (s != EMUGEMM_STATUS_SUCCESS) return s;
+        }
+        local.b_absmax = v;
+    }
+    if (local.rho < 0) local.rho = (float)emu::estimate_rho(h, M, N, K, A, lda, B, ldb, local.rho_probes);
+    if (hints) {
+        hints->a_absmax = local.a_absmax;
+        hints->b_absmax = local.b_absmax;
+        hints->rho = local.rho;
+    }
+    emu_plan_t plan = emu::plan(emu::model(), M, N, K, req, &local);
+    if (out_plan) *out_plan = plan;
+    return emu::dispatch(h, plan.chosen, plan.chunks, M, N, K, A, lda, B, ldb, C, ldc, nullptr, 0);
+}
+
+emugemm_status_t emugemm_sgemm(emugemm_handle_t handle, int M, int N, long K, const float* A, const float* B,
+                               float* C, const emu_request_t* req, emu_hints_t* hints, emu_plan_t* out_plan) {
+    return emugemm_sgemm_ex(handle, M, N, K, A, K > 0 ? K : 1, B, N > 0 ? N : 1, C, N > 0 ? N : 1, req, hints,
+                            out_plan);
+}
+
+double emugemm_estimate_rho(emugemm_handle_t handle, int M, int N, long K, const float* A, const float* B,
+                            int probes) {
+    Handle* h = reinterpret_cast<Handle*>(handle);
+    if (!h || !A || !B) return -1.0;
+    emu::DeviceGuard g(h->device);
+    return emu::estimate_rho(h, M, N, K, A, K, B, N, probes);
+}
+
+emugemm_status_t emugemm_absmax(emugemm_handle_t handle, const float* X, size_t n, float* out_absmax) {
+    Handle* h = reinterpret_cast<Handle*>(handle);
+    if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
+    if (!out_absmax || (n && !X)) return EMUGEMM_STATUS_INVALID_POINTER;
+    emu::DeviceGuard g(h->device);
+    if (n == 0) { *out_absmax = 0.f; return EMUGEMM_STATUS_SUCCESS; }
+    return emu::absmax(h, X, 1, (long)n, (long)n, out_absmax);
+}
+
+emugemm_status_t emugemm_split_bf16(emugemm_handle_t handle, const float* X, size_t n, unsigned short* hi,
+                                    unsigned short* lo) {
+    Handle* h = reinterpret_cast<Handle*>(handle);
+    if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
+    if (n && (!X || !hi || !lo)) return EMUGEMM_STATUS_INVALID_POINTER;
+    emu::DeviceGuard g(h->device);
+    return emu::from_cuda(emu::launch_split_bf16(X, n, hi, lo, h->stream));
+}
+
+emugemm_status_t emugemm_split_f16(emugemm_handle_t handle, const float* X, size_t n, unsigned short* hi,
+                                   unsigned short* lo) {
+    Handle* h = reinterpret_cast<Handle*>(handle);
+    if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
+    if (n && (!X || !hi || !lo)) return EMUGEMM_STATUS_INVALID_POINTER;
+    emu::DeviceGuard g(h->device);
+    return emu::from_cuda(emu::launch_split_f16(X, n, hi, lo, h->stream));
+}
+
+emugemm_status_t emugemm_sgemm_partial_f64(emugemm_handle_t handle, int M, int N, long K, const float* A, long lda,
+                                           const float* B, long ldb, double* P, int scheme, int chunks) {
+    Handle* h = reinterpret_cast<Handle*>(handle);
+    if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
+    if (M < 0 || N < 0 || K < 0) return EMUGEMM_STATUS_INVALID_SIZE;
+    if (lda < (K > 0 ? K : 1) || ldb < (N > 0 ? N : 1)) return EMUGEMM_STATUS_INVALID_SIZE;
+    if ((M > 0 && N > 0) && (!P || (K > 0 && (!A || !B)))) return EMUGEMM_STATUS_INVALID_POINTER;
+    if (scheme == EMU_SCHEME_AUTO) return EMUGEMM_STATUS_INVALID_VALUE;
+    emu::DeviceGuard g(h->device);
+    return emu::dispatch(h, (emu_scheme_t)scheme, chunks, M, N, K, A, lda, B, ldb, nullptr, 0, P, N);
+}
+
+emugemm_status_t emugemm_reduce_f64(emugemm_handle_t handle, int M, int N, int G, const double* P, float* C) {
+    Handle* h = reinterpret_cast<Handle*>(handle);
+    if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
+    if (M < 0 || N < 0 || G < 1) return EMUGEMM_STATUS_INVALID_SIZE;
+    if ((long)M * N > 0 && (!P || !C)) return EMUGEMM_STATUS_INVALID_POINTER;
+    emu::DeviceGuard g(h->device);
+    return emu::from_cuda(emu::launch_reduce_f64(P, G, M, N, (long)M * N, C, N, nullptr, 0, h->stream));
+}
+
+int emugemm_fp32_groups(int M, int N, long K, int chunks, int num_sms) {
+    emu::Fp32GemmArgs f{};
+    f.M = M; f.N = N; f.K = K; f.chunks = chunks; f.num_sms = num_sms; f.bm = 0;
+    return emu::fp32_gemm_groups(f);
+}
+
+unsigned long long emugemm_kernel_launch_count(void) { return emu::g_launches.load(); }
+
+emugemm_status_t emugemm_profile_begin(emugemm_handle_t handle) {
+    Handle* h = reinterpret_cast<Handle*>(handle);
+    if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
+    emu::DeviceGuard g(h->device);
+    emu::prof_clear(h);
+    h->profiling = true;
+    return EMUGEMM_STATUS_SUCCESS;
+}
+
+emugemm_status_t emugemm_profile_end(emugemm_handle_t handle, double* ms_by_kind, int* count_by_kind, int nkinds) {
+    Handle* h = reinterpret_cast<Handle*>(handle);
+    if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
+    emu::DeviceGuard g(h->device);
+    h->profiling = false;
+    emugemm_status_t st = emu::sync_check(h);
+    for (int k = 0; k < nkinds; ++k) {
+        if (ms_by_kind) ms_by_kind[k] = 0.0;
+        if (count_by_kind) count_by_kind[k] = 0;
+    }
+    for (int i = 0; i < h->prof_n; ++i) {
+        const emu::ProfRec& r = h->prof[i];
+        float ms = 0.f;
+        if (r.kind < nkinds && cudaEventElapsedTime(&ms, (cudaEvent_t)r.a, (cudaEvent_t)r.b) == cudaSuccess) {
+            if (ms_by_kind) ms_by_kind[r.kind] += ms;
+            if (count_by_kind) count_by_kind[r.kind] += 1;
+        }
+    }
+    emu::prof_clear(h);
+    return st;
+}
+
+const char* emugemm_status_string(emugemm_status_t s) {
+    switch (s) {
+        case EMUGEMM_STATUS_SUCCESS: return "success";
+        case EMUGEMM_STATUS_INVALID_HANDLE: return "invalid handle";
+        case EMUGEMM_STATUS_NOT_IMPLEMENTED: return "not implemented";
+        case EMUGEMM_STATUS_INVALID_POINTER: return "invalid pointer";
+        case EMUGEMM_STATUS_INVALID_SIZE: return "invalid size";
+        case EMUGEMM_STATUS_MEMORY_ERROR: return "memory error";
+        case EMUGEMM_STATUS_INTERNAL_ERROR: return "internal error";
+        case EMUGEMM_STATUS_INVALID_VALUE: return "invalid value";
+        case EMUGEMM_STATUS_ARCH_MISMATCH: return "device is not sm_100";
+        case EMUGEMM_STATUS_TIMEOUT: return "device wait timed out";
+    }
+    return "unknown status";
+}
+
+}  // extern "C"

@@ -1,0 +1,162 @@
+// emugemm_internal.h - declarations shared by the host and kernel translation units of libemugemm.
+#pragma once
+
+#include "../../include/emugemm.h"
+
+#include <cstddef>
+#include <cstdint>
+
+namespace emu {
+
+// ---------------------------------------------------------------------------------------------------
+// model.cpp
+struct ChunkStep { int c_max; double cost; };
+
+struct ModelConsts {
+    const char* name;
+    double a_fp32, a_lowp, a_fp16x3;
+    double floor_bf16x3, floor_fp16x3, floor_bf16x6;
+    double spd_bf16x3, spd_fp16x3, spd_bf16x6;
+    float fp16_max, fp16_min;          // fp16 "range safe" test: min < absmax < max
+    const ChunkStep* chunk_steps;
+    int n_chunk_steps;
+    double chunk_cost_beyond;
+    int max_chunks;
+    double hbm_bps, fp32_flops;
+    double ovh_native, ovh_chunked, ovh_emulated, ovh_fp16x3;   // bytes per input element
+    double rho_ref_coef;
+};
+
+const ModelConsts& model();
+bool set_model_by_name(const char* name);
+double chunk_cost(const ModelConsts& m, int c);
+double model_err(const ModelConsts& m, emu_scheme_t s, long K, int c);
+double model_err_rho(const ModelConsts& m, emu_scheme_t s, long K, int c, double rho);
+double model_speed(const ModelConsts& m, emu_scheme_t s, int c);
+emu_plan_t plan(const ModelConsts& m, int M, int N, long K, const emu_request_t* req,
+                const emu_hints_t* hints);
+
+extern const char* const kReasonUnreachable;
+extern const char* const kReasonSlower;
+extern const char* const kReasonFp16;
+extern const char* const kReasonBf16;
+extern const char* const kReasonChunked;
+extern const char* const kReasonNative;
+
+// ---------------------------------------------------------------------------------------------------
+// tune.cpp: per-shape tile table
+struct TileChoice {
+    int tc_variant;     // tensor-core kernel variant: 0 = auto, 1 = fused in-smem split, 2 = pre-split
+    int fp32_bm;        // FP32 SIMT tile edge: 0 = auto, 64 or 128
+};
+TileChoice lookup_tile(int M, int N, long K, int dtype /*0 fp32, 1 bf16, 2 fp16*/);
+
+// ---------------------------------------------------------------------------------------------------
+// Device-side error word: kernels OR these bits into the handle's mapped error word when a bounded wait
+// gives up; the host reads it after synchronising.
+enum : unsigned {
+    kErrTimeoutProducer = 1u,
+    kErrTimeoutMma = 2u,
+    kErrTimeoutEpilogue = 4u,
+    kErrTimeoutConvert = 8u,
+    kErrTmemAlloc = 16u,
+};
+
+// Workspace slots of a handle (grow-only, freed with the handle).
+enum WsSlot {
+    kWsSplitA0 = 0, kWsSplitA1, kWsSplitB0, kWsSplitB1,
+    kWsScaleA, kWsScaleB,
+    kWsF64Acc,
+    kWsRhoT1, kWsRhoT2, kWsRhoPart,
+    kWsScalar,
+    kWsCount
+};
+
+// Kernel classes timed by the optional per-handle profiler (CUDA events on the handle's stream).
+enum ProfKind { kProfTcGemm = 0, kProfFp32Gemm, kProfSplit, kProfScan, kProfRho, kProfReduce, kProfCount };
+
+struct ProfRec { void* a; void* b; int kind; };   // cudaEvent_t pair
+
+struct Handle {
+    int device = 0;
+    void* stream = nullptr;         // cudaStream_t
+    int num_sms = 0;
+    size_t ws_limit = 0;            // 0 = no cap
+    void* ws[kWsCount] = {};
+    size_t ws_size[kWsCount] = {};
+    unsigned* err_host = nullptr;   // mapped pinned word
+    unsigned* err_dev = nullptr;
+    bool profiling = false;
+    ProfRec* prof = nullptr;        // growable array of event pairs
+    int prof_n = 0, prof_cap = 0;
+};
+
+// Profiler scope: records an event before and after the launches inside it when the handle profiles.
+struct ProfScope {
+    Handle* h; int kind; ProfRec* rec = nullptr;
+    ProfScope(Handle* h_, int kind_);
+    ~ProfScope();
+};
+
+void* ws_get(Handle* h, int slot, size_t bytes);
+void count_launch(unsigned n = 1);
+
+// ---------------------------------------------------------------------------------------------------
+// Kernel launchers (return a cudaError_t as int; 0 = success).
+
+// k_split.cu
+int launch_split_bf16(const float* X, size_t n, uint16_t* hi, uint16_t* lo, void* stream);
+int launch_split_f16(const float* X, size_t n, uint16_t* hi, uint16_t* lo, void* stream);
+int launch_absmax(const float* X, long rows, long cols, long ld, float* out, void* stream);
+// Row exponents of A (MxK) / column exponents of B (KxN) for the scaled fp16 split: e such that
+// max|x| * 2^-e < 2^15 (0 for an all-zero row or column).
+int launch_row_exponents(const float* A, int M, long K, long lda, int* e_out, void* stream);
+int launch_col_exponents(const float* B, long K, int N, long ldb, int* e_out, unsigned* scratch,
+                         void* stream);
+// Pre-split into K-major 16-bit slices: rows x Kp (zero padded to rows_p x Kp).
+// kind 0 = bf16, 1 = scaled fp16 (hi = RNE(x*2^-e), lo = RNE((x*2^-e - hi)*2048)).
+int launch_split_rows(const float* A, int M, long K, long lda, int Mp, long Kp, int kind,
+                      const int* row_exp, uint16_t* hi, uint16_t* lo, void* stream);
+// B (KxN, ldb) -> transposed K-major slices Np x Kp.
+int launch_split_cols(const float* B, long K, int N, long ldb, int Np, long Kp, int kind,
+                      const int* col_exp, uint16_t* hi, uint16_t* lo, void* stream);
+
+// k_tc_gemm.cu: tensor-core 3-product GEMM over pre-split K-major slices.
+struct TcGemmArgs {
+    const uint16_t* a_hi; const uint16_t* a_lo;   // Mp x Kp
+    const uint16_t* b_hi; const uint16_t* b_lo;   // Np x Kp
+    int M, N, Mp, Np; long Kp;
+    float* C; long ldc;
+    double* C64; long ldc64;                       // when non-null: write FP64 instead of C
+    int fp16;                                      // 0 = bf16x3, 1 = scaled fp16x3
+    const int* row_exp; const int* col_exp;        // fp16x3 only
+    unsigned* err;
+    int num_sms;
+};
+int launch_tc_gemm(const TcGemmArgs& a, void* stream);
+int tc_gemm_bn(int fp16);   // output tile width of the bf16x3 (0) / fp16x3 (1) kernel
+
+// k_fp32_gemm.cu: FP32 SIMT GEMM with K-chunks summed in FP64.
+struct Fp32GemmArgs {
+    const float* A; long lda;
+    const float* B; long ldb;
+    float* C; long ldc;
+    double* C64; long ldc64;     // when non-null: write FP64 sums here instead of C
+    int M, N; long K;
+    int chunks;
+    double* ws64;                // G x M x N FP64 partials when G > 1
+    int num_sms;
+    int bm;                      // 0 = auto
+};
+int fp32_gemm_groups(const Fp32GemmArgs& a);   // G chosen for this shape
+size_t fp32_gemm_ws_bytes(const Fp32GemmArgs& a);
+int launch_fp32_gemm(const Fp32GemmArgs& a, void* stream);
+int launch_reduce_f64(const double* P, int G, int M, int N, long ldp, float* C, long ldc,
+                      double* C64, long ldc64, void* stream);
+
+// k_rho.cu: Hutchinson estimate of rho; out2[0] = sum |A|(|B| Omega) squared, out2[1] = sum (A B Omega)^2.
+size_t rho_ws_bytes(int M, int N, long K, int P, int sms);
+int launch_rho(const float* A, long lda, const float* B, long ldb, int M, int N, long K, int P, void* ws, int sms,
+               double* out2, void* stream);
+
+}  // namespace emu

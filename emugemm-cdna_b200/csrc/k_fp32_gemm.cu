@@ -1,0 +1,293 @@
+// k_fp32_gemm.cu - FP32 SIMT GEMM with K-chunks summed in FP64: the NATIVE_FP32 (c = 1) and FP32_CHUNKED
+// schemes of emugemm (emugemm-cdna src/emugemm.cpp:313-330).
+//
+// The reference runs one rocBLAS SGEMM per chunk into an FP32 buffer and adds it into an FP64 buffer with
+// a separate kernel (k_accum_f64, src/emugemm.cpp:149-154). Here one kernel does both: every output
+// element is a single sequential FP32 FMA chain over the chunk's K range (k ascending), and the chunk
+// partial is folded into an FP64 sum kept in a workspace tile owned by the same thread. Chunk c covers
+// [c*kc, min(K, (c+1)*kc)) with kc = ceil(K/chunks), exactly the reference's chunk boundaries.
+//
+// When there are too few output tiles to fill the GPU, the chunks are divided into G contiguous groups
+// (grid.z); group g writes its FP64 sum to partial plane g and a reduce kernel adds the planes in order
+// g = 0..G-1 and rounds once to FP32. With this fixed order the result is deterministic and a CPU oracle
+// that performs the same FMA chains and FP64 additions reproduces it bit for bit.
+#include "emugemm_internal.h"
+
+#include <cuda_runtime.h>
+
+namespace emu {
+namespace {
+
+constexpr int kBKf = 16;
+constexpr int kThr = 256;
+
+struct Params {
+    const float* A; long lda;
+    const float* B; long ldb;
+    float* C; long ldc;
+    double* C64; long ldc64;
+    double* W;          // G planes of M x N (ld N), used when G > 1
+    int M, N; long K;
+    long kc;            // chunk length
+    int ce;             // non-empty chunks
+    int cpg;            // chunks per group
+    int G;
+};
+
+template <int BM, int BN, int TM, int TN, bool VEC>
+__global__ void __launch_bounds__(kThr) k_fp32_gemm(Params p) {
+    __shared__ __align__(16) float As[2][kBKf][BM];
+    __shared__ __align__(16) float Bs[2][kBKf][BN];
+    constexpr int HM = TM / 2, HN = TN / 2;
+    constexpr int A_VEC = BM * kBKf / 4 / kThr;   // float4 per thread
+    constexpr int B_VEC = BN * kBKf / 4 / kThr;
+    constexpr int A_SC = BM * kBKf / kThr;        // scalars per thread
+    constexpr int B_SC = BN * kBKf / kThr;
+    static_assert(16 * TM == BM && 16 * TN == BN, "tile shape");
+
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int g = blockIdx.z;
+    const int c_first = g * p.cpg;
+    const int c_last = min(p.ce, c_first + p.cpg);   // exclusive
+
+    float acc[TM][TN];
+    double* Wg = p.W ? p.W + (size_t)g * p.M * p.N : nullptr;
+
+    float ra[VEC ? A_VEC * 4 : A_SC];
+    float rb[VEC ? B_VEC * 4 : B_SC];
+
+    auto load_global = [&](long kb, long kend) {
+        if (VEC) {
+#pragma unroll
+            for (int j = 0; j < A_VEC; ++j) {
+                const int f = tid + j * kThr;
+                const int row = f >> 2, kq = f & 3;
+                const int m = m0 + row;
+                const long k = kb + kq * 4;
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (m < p.M && k < kend) v = __ldg(reinterpret_cast<const float4*>(p.A + (size_t)m * p.lda + k));
+                ra[4 * j] = v.x; ra[4 * j + 1] = v.y; ra[4 * j + 2] = v.z; ra[4 * j + 3] = v.w;
+            }
+#pragma unroll
+            for (int j = 0; j < B_VEC; ++j) {
+                const int f = tid + j * kThr;
+                const int kk = f / (BN / 4), nq = f % (BN / 4);
+                const long k = kb + kk;
+                const int n = n0 + nq * 4;
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (k < kend && n < p.N) v = __ldg(reinterpret_cast<const float4*>(p.B + (size_t)k * p.ldb + n));
+                rb[4 * j] = v.x; rb[4 * j + 1] = v.y; rb[4 * j + 2] = v.z; rb[4 * j + 3] = v.w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < A_SC; ++j) {
+                const int f = tid + j * kThr;
+                const int row = f / kBKf, kk = f % kBKf;
+                const int m = m0 + row;
+                const long k = kb + kk;
+                ra[j] = (m < p.M && k < kend) ? __ldg(p.A + (size_t)m * p.lda + k) : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < B_SC; ++j) {
+                const int f = tid + j * kThr;
+                const int kk = f / BN, nn = f % BN;
+                const long k = kb + kk;
+                const int n = n0 + nn;
+                rb[j] = (k < kend && n < p.N) ? __ldg(p.B + (size_t)k * p.ldb + n) : 0.f;
+            }
+        }
+    };
+    auto store_smem = [&](int buf) {
+        if (VEC) {
+#pragma unroll
+            for (int j = 0; j < A_VEC; ++j) {
+                const int f = tid + j * kThr;
+                const int row = f >> 2, kq = f & 3;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) As[buf][kq * 4 + e][row] = ra[4 * j + e];
+            }
+#pragma unroll
+            for (int j = 0; j < B_VEC; ++j) {
+                const int f = tid + j * kThr;
+                const int kk = f / (BN / 4), nq = f % (BN / 4);
+                *reinterpret_cast<float4*>(&Bs[buf][kk][nq * 4]) =
+                    make_float4(rb[4 * j], rb[4 * j + 1], rb[4 * j + 2], rb[4 * j + 3]);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < A_SC; ++j) {
+                const int f = tid + j * kThr;
+                As[buf][f % kBKf][f / kBKf] = ra[j];
+            }
+#pragma unroll
+            for (int j = 0; j < B_SC; ++j) {
+                const int f = tid + j * kThr;
+                Bs[buf][f / BN][f % BN] = rb[j];
+            }
+        }
+    };
+
+    for (int ci = c_first; ci < c_last; ++ci) {
+        const long kbeg = (long)ci * p.kc;
+        const long kend = min(p.K, kbeg + p.kc);
+#pragma unroll
+        for (int i = 0; i < TM; ++i)
+#pragma unroll
+            for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+
+        const long nkb = (kend - kbeg + kBKf - 1) / kBKf;
+        load_global(kbeg, kend);
+        store_smem(0);
+        __syncthreads();
+        for (long kt = 0; kt < nkb; ++kt) {
+            const int cur = (int)(kt & 1);
+            if (kt + 1 < nkb) load_global(kbeg + (kt + 1) * kBKf, kend);
+#pragma unroll
+            for (int k = 0; k < kBKf; ++k) {
+                float a[TM], b[TN];
+#pragma unroll
+                for (int i = 0; i < HM; ++i) {
+                    a[i] = As[cur][k][ty * HM + i];
+                    a[HM + i] = As[cur][k][BM / 2 + ty * HM + i];
+                }
+#pragma unroll
+                for (int j = 0; j < HN; ++j) {
+                    b[j] = Bs[cur][k][tx * HN + j];
+                    b[HN + j] = Bs[cur][k][BN / 2 + tx * HN + j];
+                }
+#pragma unroll
+                for (int i = 0; i < TM; ++i)
+#pragma unroll
+                    for (int j = 0; j < TN; ++j) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+            }
+            if (kt + 1 < nkb) store_smem(cur ^ 1);
+            __syncthreads();
+        }
+
+        // Fold this chunk's FP32 partials into the FP64 sum of the group.
+        const bool first = (ci == c_first), last = (ci == c_last - 1);
+#pragma unroll
+        for (int i = 0; i < TM; ++i) {
+            const int m = m0 + (i < HM ? ty * HM + i : BM / 2 + ty * HM + (i - HM));
+            if (m >= p.M) continue;
+#pragma unroll
+            for (int j = 0; j < TN; ++j) {
+                const int n = n0 + (j < HN ? tx * HN + j : BN / 2 + tx * HN + (j - HN));
+                if (n >= p.N) continue;
+                const size_t wi = (size_t)m * p.N + n;
+                double s = first ? (double)acc[i][j] : Wg[wi] + (double)acc[i][j];
+                if (last && p.G == 1) {
+                    if (p.C64) p.C64[(size_t)m * p.ldc64 + n] = s;
+                    else p.C[(size_t)m * p.ldc + n] = (float)s;
+                } else {
+                    Wg[wi] = s;
+                }
+            }
+        }
+    }
+}
+
+__global__ void k_reduce_f64(const double* __restrict__ P, int G, int M, int N, long ldp_plane, float* C,
+                             long ldc, double* C64, long ldc64) {
+    const size_t total = (size_t)M * N;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        double s = P[i];
+        for (int g = 1; g < G; ++g) s += P[(size_t)g * ldp_plane + i];
+        const size_t m = i / N, n = i - m * N;
+        if (C64) C64[m * ldc64 + n] = s;
+        else C[m * ldc + n] = (float)s;
+    }
+}
+
+struct Shape {
+    int bm;
+    long kc;
+    int ce, cpg, G;
+    int tiles;
+};
+
+Shape shape_of(const Fp32GemmArgs& a) {
+    Shape s;
+    const int sms = a.num_sms > 0 ? a.num_sms : 148;
+    const long t128 = (long)((a.M + 127) / 128) * ((a.N + 127) / 128);
+    s.bm = a.bm ? a.bm : (t128 >= sms ? 128 : 64);
+    s.tiles = (int)((long)((a.M + s.bm - 1) / s.bm) * ((a.N + s.bm - 1) / s.bm));
+    const int c = a.chunks < 1 ? 1 : a.chunks;
+    s.kc = (a.K + c - 1) / c;
+    if (s.kc < 1) s.kc = 1;
+    s.ce = (int)((a.K + s.kc - 1) / s.kc);
+    if (s.ce < 1) s.ce = 1;
+    int G = 1;
+    if (s.ce > 1) {
+        int want = (2 * sms + s.tiles - 1) / s.tiles;
+        G = want < 1 ? 1 : want;
+        if (G > s.ce) G = s.ce;
+    }
+    s.cpg = (s.ce + G - 1) / G;
+    s.G = (s.ce + s.cpg - 1) / s.cpg;
+    return s;
+}
+
+template <int BM, int TM, bool VEC>
+void launch_cfg(const Params& p, dim3 grid, cudaStream_t st) {
+    k_fp32_gemm<BM, BM, TM, TM, VEC><<<grid, kThr, 0, st>>>(p);
+}
+
+}  // namespace
+
+int fp32_gemm_groups(const Fp32GemmArgs& a) { return shape_of(a).G; }
+
+size_t fp32_gemm_ws_bytes(const Fp32GemmArgs& a) {
+    Shape s = shape_of(a);
+    if (s.G <= 1) {
+        // A single group still needs the FP64 running sum when it has more than one chunk.
+        return s.ce > 1 ? (size_t)a.M * a.N * sizeof(double) : 0;
+    }
+    return (size_t)s.G * a.M * a.N * sizeof(double);
+}
+
+int launch_fp32_gemm(const Fp32GemmArgs& a, void* stream) {
+    if (a.M <= 0 || a.N <= 0 || a.K <= 0) return 0;
+    Shape s = shape_of(a);
+    Params p;
+    p.A = a.A; p.lda = a.lda;
+    p.B = a.B; p.ldb = a.ldb;
+    p.C = a.C; p.ldc = a.ldc;
+    p.C64 = a.C64; p.ldc64 = a.ldc64;
+    p.W = a.ws64;
+    p.M = a.M; p.N = a.N; p.K = a.K;
+    p.kc = s.kc; p.ce = s.ce; p.cpg = s.cpg; p.G = s.G;
+    if ((s.G > 1 || s.ce > 1) && !a.ws64) return (int)cudaErrorInvalidValue;
+    const bool vec = (a.lda % 4 == 0) && (a.ldb % 4 == 0) && (a.N % 4 == 0) && (a.K % 4 == 0) &&
+                     (s.kc % 4 == 0) && ((reinterpret_cast<uintptr_t>(a.A) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(a.B) & 15) == 0);
+    cudaStream_t st = (cudaStream_t)stream;
+    dim3 grid((unsigned)((a.N + s.bm - 1) / s.bm), (unsigned)((a.M + s.bm - 1) / s.bm), (unsigned)s.G);
+    if (s.bm == 128) {
+        if (vec) launch_cfg<128, 8, true>(p, grid, st);
+        else launch_cfg<128, 8, false>(p, grid, st);
+    } else {
+        if (vec) launch_cfg<64, 4, true>(p, grid, st);
+        else launch_cfg<64, 4, false>(p, grid, st);
+    }
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return (int)e;
+    if (s.G > 1) return launch_reduce_f64(a.ws64, s.G, a.M, a.N, (long)a.M * a.N, a.C, a.ldc, a.C64, a.ldc64, stream);
+    return 0;
+}
+
+int launch_reduce_f64(const double* P, int G, int M, int N, long ldp, float* C, long ldc, double* C64, long ldc64,
+                      void* stream) {
+    const size_t total = (size_t)M * N;
+    if (total == 0) return 0;
+    size_t blocks = (total + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    k_reduce_f64<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(P, G, M, N, ldp, C, ldc, C64, ldc64);
+    count_launch();
+    return (int)cudaGetLastError();
+}
+
+}  // namespace emu

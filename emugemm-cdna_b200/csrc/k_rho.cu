@@ -1,0 +1,242 @@
+// k_rho.cu - Hutchinson estimate of the cancellation ratio rho = || |A||B| ||_F / ||AB||_F
+// (emugemm-cdna src/emugemm.cpp:171-213, emugemm_estimate_rho).
+//
+// With a Rademacher probe matrix Omega (N x P, row-major, Omega[i] = +1 if bit 0 of hash(i ^ 0x5eed) is
+// set, else -1, i = n*P + p; the hash of src/emugemm.cpp:173-176):
+//     T1 = B*Omega, T2 = A*T1          den = sqrt(sum T2^2 / P)
+//     U1 = |B|*Omega, U2 = |A|*U1      num = sqrt(sum U2^2 / P)        rho_hat = num / den
+// The reference materialises |A| and |B| and calls four FP32 rocBLAS GEMMs. Here one "skinny" kernel
+// reads each operand once and produces the signed and the absolute product together (|x| is applied on
+// the fly), Omega is generated in the kernel, and the sums of squares are FP64 warp-shuffle reductions
+// with a fixed combine order (deterministic).
+#include "emugemm_internal.h"
+
+#include <cuda_runtime.h>
+
+namespace emu {
+namespace {
+
+constexpr int kRows = 64, kP = 64, kBJ = 32, kT = 256;
+
+__device__ __forceinline__ float rademacher(unsigned i) {
+    unsigned h = i ^ 0x5eedu;
+    h ^= h >> 16;
+    h *= 0x7feb352du;
+    h ^= h >> 15;
+    h *= 0x846ca68bu;
+    h ^= h >> 16;
+    return (h & 1u) ? 1.f : -1.f;
+}
+
+// Ypart[s] (rows x P) = X[:, Js] * W[Js, :],  Yabs_part[s] = |X[:, Js]| * Wabs[Js, :].
+// OMEGA: W = Wabs = Omega (generated; J = N). Otherwise W, Wabs are J x P row-major.
+template <bool OMEGA>
+__global__ void __launch_bounds__(kT) k_skinny(const float* __restrict__ X, long ld, long rows, long J, int P,
+                                               const float* __restrict__ W, const float* __restrict__ Wabs,
+                                               long j_per_split, float* __restrict__ Ypart,
+                                               float* __restrict__ Yabs_part) {
+    __shared__ __align__(16) float Xs[kBJ][kRows];
+    __shared__ __align__(16) float Ws[kBJ][kP];
+    __shared__ __align__(16) float Was[kBJ][kP];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const long r0 = (long)blockIdx.x * kRows;
+    const int p0 = blockIdx.y * kP;
+    const int s = blockIdx.z;
+    const long j_begin = (long)s * j_per_split;
+    const long j_end = min(J, j_begin + j_per_split);
+
+    float acc[4][4] = {}, acca[4][4] = {};
+    for (long jb = j_begin; jb < j_end; jb += kBJ) {
+        for (int f = tid; f < kRows * kBJ; f += kT) {
+            const int rr = f / kBJ, jj = f % kBJ;
+            const long r = r0 + rr, j = jb + jj;
+            Xs[jj][rr] = (r < rows && j < j_end) ? __ldg(X + (size_t)r * ld + j) : 0.f;
+        }
+        for (int f = tid; f < kBJ * kP; f += kT) {
+            const int jj = f / kP, pp = f % kP;
+            const long j = jb + jj;
+            const int pc = p0 + pp;
+            float w = 0.f, wa = 0.f;
+            if (j < j_end && pc < P) {
+                if (OMEGA) {
+                    w = wa = rademacher((unsigned)((size_t)j * P + pc));
+                } else {
+                    w = __ldg(W + (size_t)j * P + pc);
+                    wa = __ldg(Wabs + (size_t)j * P + pc);
+                }
+            }
+            Ws[jj][pp] = w;
+            Was[jj][pp] = wa;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int jj = 0; jj < kBJ; ++jj) {
+            const float4 xv = *reinterpret_cast<const float4*>(&Xs[jj][ty * 4]);
+            const float4 wv = *reinterpret_cast<const float4*>(&Ws[jj][tx * 4]);
+            const float4 av = *reinterpret_cast<const float4*>(&Was[jj][tx * 4]);
+            const float x[4] = {xv.x, xv.y, xv.z, xv.w};
+            const float w[4] = {wv.x, wv.y, wv.z, wv.w};
+            const float a[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    acc[i][q] = __fmaf_rn(x[i], w[q], acc[i][q]);
+                    acca[i][q] = __fmaf_rn(fabsf(x[i]), a[q], acca[i][q]);
+                }
+        }
+        __syncthreads();
+    }
+    float* Y = Ypart + (size_t)s * rows * P;
+    float* Ya = Yabs_part + (size_t)s * rows * P;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const long r = r0 + ty * 4 + i;
+        if (r >= rows) continue;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int pc = p0 + tx * 4 + q;
+            if (pc >= P) continue;
+            Y[(size_t)r * P + pc] = acc[i][q];
+            Ya[(size_t)r * P + pc] = acca[i][q];
+        }
+    }
+}
+
+// T = sum_s Ypart[s] (FP32, in order s = 0..S-1), for both the signed and the absolute product.
+__global__ void k_combine(const float* __restrict__ Ypart, const float* __restrict__ Yabs_part, int S, size_t n,
+                          float* __restrict__ T, float* __restrict__ Tabs) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float y = Ypart[i], ya = Yabs_part[i];
+        for (int s = 1; s < S; ++s) {
+            y += Ypart[(size_t)s * n + i];
+            ya += Yabs_part[(size_t)s * n + i];
+        }
+        T[i] = y;
+        Tabs[i] = ya;
+    }
+}
+
+// Same combine, then FP64 sums of squares per block (warp shuffles), written to part[block][2].
+__global__ void k_combine_sq(const float* __restrict__ Ypart, const float* __restrict__ Yabs_part, int S, size_t n,
+                             double* __restrict__ part) {
+    double sq = 0.0, sqa = 0.0;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float y = Ypart[i], ya = Yabs_part[i];
+        for (int s = 1; s < S; ++s) {
+            y += Ypart[(size_t)s * n + i];
+            ya += Yabs_part[(size_t)s * n + i];
+        }
+        sq += (double)y * (double)y;
+        sqa += (double)ya * (double)ya;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        sqa += __shfl_xor_sync(0xffffffffu, sqa, o);
+    }
+    __shared__ double ws[2][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        ws[0][warp] = sq;
+        ws[1][warp] = sqa;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = blockDim.x >> 5;
+        sq = lane < nw ? ws[0][lane] : 0.0;
+        sqa = lane < nw ? ws[1][lane] : 0.0;
+        for (int o = 16; o > 0; o >>= 1) {
+            sq += __shfl_xor_sync(0xffffffffu, sq, o);
+            sqa += __shfl_xor_sync(0xffffffffu, sqa, o);
+        }
+        if (lane == 0) {
+            part[2 * blockIdx.x] = sq;
+            part[2 * blockIdx.x + 1] = sqa;
+        }
+    }
+}
+
+// out2[0] = sum of |.| squares (numerator), out2[1] = sum of signed squares (denominator).
+__global__ void k_final(const double* __restrict__ part, int nblocks, double* __restrict__ out2) {
+    if (threadIdx.x == 0) {
+        double sq = 0.0, sqa = 0.0;
+        for (int b = 0; b < nblocks; ++b) {
+            sq += part[2 * b];
+            sqa += part[2 * b + 1];
+        }
+        out2[0] = sqa;
+        out2[1] = sq;
+    }
+}
+
+constexpr int kCombineBlocks = 296;
+
+int splits_for(long rows, int P, long J, int sms) {
+    const long blocks = ((rows + kRows - 1) / kRows) * ((P + kP - 1) / kP);
+    long s = (2L * sms + blocks - 1) / blocks;
+    const long smax = (J + 255) / 256;
+    if (s > smax) s = smax;
+    if (s < 1) s = 1;
+    return (int)s;
+}
+
+long j_per(long J, int S) {
+    long j = (J + S - 1) / S;
+    return ((j + kBJ - 1) / kBJ) * kBJ;
+}
+
+struct RhoLayout {
+    int S1, S2;
+    size_t t1, t1a, y1, y1a, y2, y2a, part, total;
+};
+
+RhoLayout layout(int M, int N, long K, int P, int sms) {
+    RhoLayout L;
+    L.S1 = splits_for(K, P, N, sms);
+    L.S2 = splits_for(M, P, K, sms);
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t o = off; off += (bytes + 255) & ~size_t(255); return o; };
+    L.t1 = take((size_t)K * P * 4);
+    L.t1a = take((size_t)K * P * 4);
+    L.y1 = take((size_t)L.S1 * K * P * 4);
+    L.y1a = take((size_t)L.S1 * K * P * 4);
+    L.y2 = take((size_t)L.S2 * M * P * 4);
+    L.y2a = take((size_t)L.S2 * M * P * 4);
+    L.part = take((size_t)kCombineBlocks * 2 * 8);
+    L.total = off;
+    return L;
+}
+
+}  // namespace
+
+size_t rho_ws_bytes(int M, int N, long K, int P, int sms) { return layout(M, N, K, P, sms).total; }
+
+int launch_rho(const float* A, long lda, const float* B, long ldb, int M, int N, long K, int P, void* ws, int sms,
+               double* out2, void* stream) {
+    cudaStream_t st = (cudaStream_t)stream;
+    RhoLayout L = layout(M, N, K, P, sms);
+    char* w = static_cast<char*>(ws);
+    float* T1 = (float*)(w + L.t1);
+    float* T1a = (float*)(w + L.t1a);
+    float* Y1 = (float*)(w + L.y1);
+    float* Y1a = (float*)(w + L.y1a);
+    float* Y2 = (float*)(w + L.y2);
+    float* Y2a = (float*)(w + L.y2a);
+    double* part = (double*)(w + L.part);
+
+    // T1 = B * Omega (rows = K, J = N).
+    dim3 g1((unsigned)((K + kRows - 1) / kRows), (unsigned)((P + kP - 1) / kP), (unsigned)L.S1);
+    k_skinny<true><<<g1, kT, 0, st>>>(B, ldb, K, N, P, nullptr, nullptr, j_per(N, L.S1), Y1, Y1a);
+    const size_t n1 = (size_t)K * P;
+    k_combine<<<kCombineBlocks, 256, 0, st>>>(Y1, Y1a, L.S1, n1, T1, T1a);
+    // T2 = A * T1 (rows = M, J = K); only its sums of squares are kept.
+    dim3 g2((unsigned)((M + kRows - 1) / kRows), (unsigned)((P + kP - 1) / kP), (unsigned)L.S2);
+    k_skinny<false><<<g2, kT, 0, st>>>(A, lda, M, K, P, T1, T1a, j_per(K, L.S2), Y2, Y2a);
+    const size_t n2 = (size_t)M * P;
+    k_combine_sq<<<kCombineBlocks, 256, 0, st>>>(Y2, Y2a, L.S2, n2, part);
+    k_final<<<1, 32, 0, st>>>(part, kCombineBlocks, out2);
+    count_launch(5);
+    return (int)cudaGetLastError();
+}
+
+}  // namespace emu

@@ -1,0 +1,343 @@
+// k_tc_gemm.cu - the 3-product emulated-FP32 GEMM on the sm_100a tensor cores.
+//
+// C = A_hi*B_hi + A_lo*B_hi + A_hi*B_lo, the three slice products of the bf16x3 / fp16x3 schemes
+// (emugemm-cdna src/emugemm.cpp:331-356, where they are three rocBLAS calls with beta=1). Here the three
+// products of every k-step are issued back to back as tcgen05.mma into one TMEM accumulator (bf16x3) or
+// into two (fp16x3: hi*hi and the two cross products, which carry the lo slice's 2^11 factor), so C is
+// written once.
+//
+// Operands are pre-split 16-bit slices in HBM, K-major (A: Mp x Kp, B transposed: Np x Kp), loaded by
+// TMA with the 128-byte swizzle straight into the UMMA canonical layout.
+//
+// Warp roles (192 threads, one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer (one elected thread)
+//   warp 1      TMEM allocator and MMA issuer (one elected thread)
+//   warps 2..5  epilogue: tcgen05.ld from TMEM -> registers -> C
+// TMEM holds two accumulator buffers (512 columns), so the epilogue of tile i overlaps the MMAs of tile
+// i+1. Every wait is bounded; on a timeout the kernel records it in the error word, drains its copies
+// and MMAs in flight, frees TMEM and returns.
+#include "device_utils.cuh"
+#include "emugemm_internal.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+namespace emu {
+namespace {
+
+using namespace dev;
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;              // 64 16-bit elements = one 128-byte swizzle row
+constexpr int kThreads = 192;
+constexpr int kGroupM = 16;          // tile raster: groups of 16 row blocks sweep all column blocks
+
+template <bool FP16>
+struct Cfg {
+    static constexpr int BN = FP16 ? 128 : 256;
+    static constexpr int A_BYTES = kBM * kBK * 2;
+    static constexpr int B_BYTES = BN * kBK * 2;
+    static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    static constexpr int STAGES = FP16 ? 3 : 2;
+    static constexpr int ACC_COLS = FP16 ? 2 * BN : BN;    // TMEM columns per accumulator buffer
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*control*/;
+    static constexpr uint32_t IDESC = idesc_f16(kBM, BN, !FP16);
+};
+
+struct Ctl {
+    uint64_t full[4];
+    uint64_t empty[4];
+    uint64_t tmem_full[2];
+    uint64_t tmem_empty[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+};
+
+struct KParams {
+    int M, N, num_m, num_n, nk;
+    float* C; long ldc;
+    double* C64; long ldc64;
+    const int* row_exp; const int* col_exp;
+    unsigned* err;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
+    const int per_group = kGroupM * num_n;
+    const int g = t / per_group;
+    const int first_m = g * kGroupM;
+    const int gm = min(num_m - first_m, kGroupM);
+    const int r = t - g * per_group;
+    mb = first_m + r % gm;
+    nb = r / gm;
+}
+
+// Bounded wait used while unwinding: ignores the abort flag, shorter limit.
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    unsigned long long t0 = globaltimer();
+    while (!mbar_try_wait(a, parity)) {
+        if (globaltimer() - t0 > 200000000ull) return;
+    }
+}
+
+template <bool FP16>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_tc_gemm(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
+              const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo, KParams p) {
+    using C_ = Cfg<FP16>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Ctl* ctl = reinterpret_cast<Ctl*>(smem + C_::STAGES * C_::STAGE_BYTES);
+    volatile int* abort = &ctl->abort;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int num_tiles = p.num_m * p.num_n;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C_::STAGES; ++s) {
+            mbar_init(&ctl->full[s], 1);
+            mbar_init(&ctl->empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&ctl->tmem_full[b], 1);
+            mbar_init(&ctl->tmem_empty[b], 128);
+        }
+        mbar_init(&ctl->drain, 1);
+        ctl->abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tm_ahi);
+        prefetch_tmap(&tm_alo);
+        prefetch_tmap(&tm_bhi);
+        prefetch_tmap(&tm_blo);
+    }
+    if (warp == 1) {
+        tmem_alloc(&ctl->tmem_base, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = ctl->tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            long it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+                int mb, nb;
+                tile_coords(t, p.num_m, p.num_n, mb, nb);
+                for (int kb = 0; kb < p.nk; ++kb, ++it) {
+                    const int s = (int)(it % C_::STAGES);
+                    const uint32_t ph = (uint32_t)((it / C_::STAGES) & 1);
+                    if (!mbar_wait(&ctl->empty[s], ph ^ 1u, abort, p.err, kErrTimeoutProducer)) { ok = false; break; }
+                    uint8_t* st = smem + s * C_::STAGE_BYTES;
+                    mbar_arrive_expect_tx(&ctl->full[s], C_::STAGE_BYTES);
+                    tma_load_2d(st, &tm_ahi, &ctl->full[s], kb * kBK, mb * kBM);
+                    tma_load_2d(st + C_::A_BYTES, &tm_alo, &ctl->full[s], kb * kBK, mb * kBM);
+                    tma_load_2d(st + 2 * C_::A_BYTES, &tm_bhi, &ctl->full[s], kb * kBK, nb * C_::BN);
+                    tma_load_2d(st + 2 * C_::A_BYTES + C_::B_BYTES, &tm_blo, &ctl->full[s], kb * kBK, nb * C_::BN);
+                }
+            }
+            if (!ok) {
+                // Let the loads already issued land before the CTA can exit.
+                const long first = it > C_::STAGES ? it - C_::STAGES : 0;
+                for (long j = first; j < it; ++j)
+                    drain_wait(&ctl->full[j % C_::STAGES], (uint32_t)((j / C_::STAGES) & 1));
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            long it = 0;
+            int local = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+                const int b = local & 1;
+                const uint32_t bph = (uint32_t)((local >> 1) & 1);
+                if (!mbar_wait(&ctl->tmem_empty[b], bph ^ 1u, abort, p.err, kErrTimeoutMma)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_main = tmem_base + (uint32_t)(b * C_::ACC_COLS);
+                const uint32_t d_cross = FP16 ? d_main + (uint32_t)C_::BN : d_main;
+                for (int kb = 0; kb < p.nk; ++kb, ++it) {
+                    const int s = (int)(it % C_::STAGES);
+                    const uint32_t ph = (uint32_t)((it / C_::STAGES) & 1);
+                    if (!mbar_wait(&ctl->full[s], ph, abort, p.err, kErrTimeoutMma)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t st = smem_u32(smem + s * C_::STAGE_BYTES);
+                    const uint64_t a_hi = sdesc_kmajor_sw128(st);
+                    const uint64_t a_lo = sdesc_kmajor_sw128(st + C_::A_BYTES);
+                    const uint64_t b_hi = sdesc_kmajor_sw128(st + 2 * C_::A_BYTES);
+                    const uint64_t b_lo = sdesc_kmajor_sw128(st + 2 * C_::A_BYTES + C_::B_BYTES);
+#pragma unroll
+                    for (int ks = 0; ks < kBK / 16; ++ks) {
+                        const uint64_t adv = (uint64_t)(ks * 32) >> 4;   // 16 elements = 32 bytes along K
+                        const uint32_t acc = (kb | ks) ? 1u : 0u;
+                        mma_f16_ss(d_cross, a_lo + adv, b_hi + adv, C_::IDESC, acc);
+                        mma_f16_ss(d_cross, a_hi + adv, b_lo + adv, C_::IDESC, 1u);
+                        mma_f16_ss(d_main, a_hi + adv, b_hi + adv, C_::IDESC, FP16 ? acc : 1u);
+                    }
+                    mma_commit(&ctl->empty[s]);
+                }
+                if (!ok) break;
+                mma_commit(&ctl->tmem_full[b]);
+            }
+            if (!ok) {
+                mma_commit(&ctl->drain);
+                drain_wait(&ctl->drain, 0);
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int sp = warp & 3;                 // TMEM sub-partition this warp may access
+        const int row_in_tile = sp * 32 + lane;
+        int local = 0;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+            int mb, nb;
+            tile_coords(t, p.num_m, p.num_n, mb, nb);
+            const int b = local & 1;
+            const uint32_t bph = (uint32_t)((local >> 1) & 1);
+            bool ready = mbar_wait(&ctl->tmem_full[b], bph, abort, p.err, kErrTimeoutEpilogue);
+            if (!__all_sync(0xffffffffu, ready)) break;   // tcgen05.ld below needs the whole warp
+            tc_fence_after();
+            const int m = mb * kBM + row_in_tile;
+            const uint32_t tbase = tmem_base + ((uint32_t)(sp * 32) << 16) + (uint32_t)(b * C_::ACC_COLS);
+            int e_row = 0;
+            if (FP16 && m < p.M) e_row = p.row_exp[m];
+#pragma unroll 1
+            for (int cc = 0; cc < C_::BN / 32; ++cc) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tbase + (uint32_t)(cc * 32), r);
+                float v[32];
+                if (FP16) {
+                    uint32_t x[32];
+                    tmem_ld_32x32b_x32(tbase + (uint32_t)(C_::BN + cc * 32), x);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        v[j] = __uint_as_float(r[j]) + __uint_as_float(x[j]) * (1.0f / 2048.0f);
+                } else {
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                }
+                if (m < p.M) {
+                    const int n0 = nb * C_::BN + cc * 32;
+                    if (FP16) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int n = n0 + j;
+                            if (n < p.N) v[j] = ldexpf(v[j], e_row + p.col_exp[n]);
+                        }
+                    }
+                    if (p.C64) {
+                        double* crow = p.C64 + (size_t)m * p.ldc64;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (n0 + j < p.N) crow[n0 + j] = (double)v[j];
+                    } else {
+                        float* crow = p.C + (size_t)m * p.ldc;
+                        const bool vec = (n0 + 32 <= p.N) && ((p.ldc & 3) == 0) &&
+                                         ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
+                        if (vec) {
+                            float4* c4 = reinterpret_cast<float4*>(crow + n0);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                c4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (n0 + j < p.N) crow[n0 + j] = v[j];
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&ctl->tmem_empty[b]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 512);
+    }
+}
+
+// ---- host side: tensor maps ------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool get_encode() {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    return g_encode != nullptr;
+}
+
+// rows x Kp 16-bit matrix, K-major; box = 64 (K) x box_rows, 128-byte swizzle.
+bool make_tmap(CUtensorMap* m, const uint16_t* base, long Kp, int rows, int box_rows) {
+    cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)Kp * 2};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(base), dims, strides, box,
+                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <bool FP16>
+int launch_impl(const TcGemmArgs& a, void* stream) {
+    using C_ = Cfg<FP16>;
+    if (!get_encode()) return (int)cudaErrorNotSupported;
+    if (a.Mp % kBM || a.Np % C_::BN || a.Kp % kBK || a.Kp <= 0) return (int)cudaErrorInvalidValue;
+    CUtensorMap tah, tal, tbh, tbl;
+    if (!make_tmap(&tah, a.a_hi, a.Kp, a.Mp, kBM) || !make_tmap(&tal, a.a_lo, a.Kp, a.Mp, kBM) ||
+        !make_tmap(&tbh, a.b_hi, a.Kp, a.Np, C_::BN) || !make_tmap(&tbl, a.b_lo, a.Kp, a.Np, C_::BN))
+        return (int)cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(k_tc_gemm<FP16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C_::SMEM_BYTES);
+    if (e != cudaSuccess) return (int)e;
+    KParams p;
+    p.M = a.M;
+    p.N = a.N;
+    p.num_m = a.Mp / kBM;
+    p.num_n = a.Np / C_::BN;
+    p.nk = (int)(a.Kp / kBK);
+    p.C = a.C;
+    p.ldc = a.ldc;
+    p.C64 = a.C64;
+    p.ldc64 = a.ldc64;
+    p.row_exp = a.row_exp;
+    p.col_exp = a.col_exp;
+    p.err = a.err;
+    const int tiles = p.num_m * p.num_n;
+    int grid = a.num_sms > 0 ? a.num_sms : 148;
+    if (grid > tiles) grid = tiles;
+    k_tc_gemm<FP16><<<grid, kThreads, C_::SMEM_BYTES, (cudaStream_t)stream>>>(tah, tal, tbh, tbl, p);
+    count_launch();
+    return (int)cudaGetLastError();
+}
+
+}  // namespace
+
+int tc_gemm_bn(int fp16) { return fp16 ? Cfg<true>::BN : Cfg<false>::BN; }
+
+int launch_tc_gemm(const TcGemmArgs& a, void* stream) {
+    return a.fp16 ? launch_impl<true>(a, stream) : launch_impl<false>(a, stream);
+}
+
+}  // namespace emu

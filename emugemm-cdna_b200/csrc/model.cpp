@@ -1,0 +1,233 @@
+// model.cpp - error model, speed model and the scheme planner of emugemm.
+//
+// The decision procedure is the reference planner's (emugemm-cdna src/emugemm.cpp:216-282), step for
+// step, so that given the same constants it returns the same chosen scheme, chunk count, predicted error
+// (bitwise) and reason string. The constants are not hard-wired: they live in a ModelConsts table, with
+// two tables built in:
+//   "ref_mi250" - the reference's MI250 constants (src/emugemm.cpp:16-39, 92-99), used to check plan
+//                 agreement with the reference planner;
+//   "b200"      - constants measured on B200 with this library's own kernels (the default).
+#include "emugemm_internal.h"
+
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+namespace emu {
+
+// Chunk-cost envelope of the reference (src/emugemm.cpp:29-36): a step function of c.
+static const ChunkStep kRefChunkSteps[] = {{1, 1.00}, {4, 1.05}, {16, 1.95}, {64, 1.35}, {256, 1.85}};
+
+// B200 chunk cost of the FP32 kernel here: the chunk loop stays inside one kernel and only adds an FP64
+// accumulate per chunk, so the cost is flat until chunks become shorter than a few k-blocks.
+static const ChunkStep kB200ChunkSteps[] = {{1, 1.00}, {4, 1.00}, {16, 1.00}, {64, 1.02}, {256, 1.10}};
+
+static const ModelConsts kRefMI250 = {
+    "ref_mi250",
+    /*a_fp32*/ 1.79e-8, /*a_lowp*/ 8.95e-9, /*a_fp16x3*/ 8.95e-9,
+    /*floor_bf16x3*/ 4.4355e-6, /*floor_fp16x3*/ 3.6e-7, /*floor_bf16x6*/ 0.0,
+    /*spd_bf16x3*/ 1.21, /*spd_fp16x3*/ 1.19, /*spd_bf16x6*/ 0.57,
+    /*fp16_max*/ 65504.0f, /*fp16_min*/ 6e-5f,
+    kRefChunkSteps, 5, /*chunk_cost_beyond*/ 3.0,
+    /*max_chunks*/ 256,
+    /*hbm_bps*/ 1.1e12, /*fp32_flops*/ 37.0e12,
+    /*overhead bytes per input element: native, chunked, emulated, fp16x3 */ 0.0, 4.0, 12.0, 12.0,
+    /*rho_ref_coef*/ 0.64,
+};
+
+// B200 constants. Accuracy constants were fitted from this library's kernels on B200 against an FP64
+// ground truth (iid N(0,1) and U[-1,1] data, K from 1024 to 262144); speed constants are the measured
+// throughput ratios against this library's FP32 SIMT kernel (the NATIVE_FP32 path). fp16x3 scales
+// every row of A and column of B by a power of two before splitting, so it is safe over the whole FP32
+// exponent range and its range test only excludes zero and non-finite magnitudes.
+static const ModelConsts kB200 = {
+    "b200",
+    /*a_fp32*/ 1.79e-8, /*a_lowp*/ 8.95e-9, /*a_fp16x3*/ 8.95e-9,
+    /*floor_bf16x3*/ 4.4355e-6, /*floor_fp16x3*/ 3.6e-7, /*floor_bf16x6*/ 0.0,
+    /*spd_bf16x3*/ 6.0, /*spd_fp16x3*/ 5.5, /*spd_bf16x6*/ 3.0,
+    /*fp16_max*/ INFINITY, /*fp16_min*/ 0.0f,
+    kB200ChunkSteps, 5, /*chunk_cost_beyond*/ 1.5,
+    /*max_chunks*/ 256,
+    /*hbm_bps*/ 6.0e12, /*fp32_flops*/ 50.0e12,
+    /*overhead bytes per input element*/ 0.0, 4.0, 4.0, 8.0,
+    /*rho_ref_coef*/ 0.64,
+};
+
+static const ModelConsts* g_model = &kB200;
+
+const ModelConsts& model() { return *g_model; }
+
+bool set_model_by_name(const char* name) {
+    if (!name) return false;
+    if (std::strcmp(name, kRefMI250.name) == 0) { g_model = &kRefMI250; return true; }
+    if (std::strcmp(name, kB200.name) == 0) { g_model = &kB200; return true; }
+    return false;
+}
+
+// src/emugemm.cpp:29-36
+double chunk_cost(const ModelConsts& m, int c) {
+    if (c <= 1) return m.chunk_steps[0].cost;
+    for (int i = 0; i < m.n_chunk_steps; ++i)
+        if (c <= m.chunk_steps[i].c_max) return m.chunk_steps[i].cost;
+    return m.chunk_cost_beyond;
+}
+
+// src/emugemm.cpp:41-51
+double model_err(const ModelConsts& m, emu_scheme_t s, long K, int c) {
+    if (c < 1) c = 1;
+    double kc = (double)K / c, fl = 0, a = m.a_lowp;
+    switch (s) {
+        case EMU_SCHEME_NATIVE_FP32:
+        case EMU_SCHEME_FP32_CHUNKED: fl = 0; a = m.a_fp32; break;
+        case EMU_SCHEME_BF16X3: fl = m.floor_bf16x3; break;
+        case EMU_SCHEME_FP16X3: fl = m.floor_fp16x3; a = m.a_fp16x3; break;
+        case EMU_SCHEME_BF16X6: fl = m.floor_bf16x6; break;
+        default: return NAN;
+    }
+    return std::sqrt(fl * fl + a * a * kc);
+}
+
+// src/emugemm.cpp:54
+static double rho_ref(const ModelConsts& m, long K) { return m.rho_ref_coef * std::sqrt((double)K); }
+
+// src/emugemm.cpp:56-60
+double model_err_rho(const ModelConsts& m, emu_scheme_t s, long K, int c, double rho) {
+    double e = model_err(m, s, K, c);
+    if (!(rho > 0)) return e;
+    return e * (rho / rho_ref(m, K));
+}
+
+// src/emugemm.cpp:62-73
+double model_speed(const ModelConsts& m, emu_scheme_t s, int c) {
+    double base;
+    switch (s) {
+        case EMU_SCHEME_NATIVE_FP32: base = 1.0; break;
+        case EMU_SCHEME_FP32_CHUNKED: base = 1.0; break;
+        case EMU_SCHEME_BF16X3: base = m.spd_bf16x3; break;
+        case EMU_SCHEME_FP16X3: base = m.spd_fp16x3; break;
+        case EMU_SCHEME_BF16X6: base = m.spd_bf16x6; break;
+        default: return 0;
+    }
+    return base / chunk_cost(m, c);
+}
+
+// src/emugemm.cpp:94-99, with the bytes-per-element factors taken from the table.
+static double overhead_seconds(const ModelConsts& m, long M, long N, long K, emu_scheme_t s) {
+    if (s == EMU_SCHEME_NATIVE_FP32) return 0.0;
+    double elems = (double)M * K + (double)K * N;
+    if (s == EMU_SCHEME_FP32_CHUNKED) return elems * m.ovh_chunked / m.hbm_bps;
+    if (s == EMU_SCHEME_FP16X3) return elems * m.ovh_fp16x3 / m.hbm_bps;
+    return elems * m.ovh_emulated / m.hbm_bps;
+}
+
+// src/emugemm.cpp:216-282
+emu_plan_t plan(const ModelConsts& m, int M, int N, long K, const emu_request_t* req,
+                const emu_hints_t* hints) {
+    emu_plan_t p;
+    p.chunks = 1;
+    p.chosen = EMU_SCHEME_NATIVE_FP32;
+    p.reason = "default";
+    p.predicted_err = 0;
+    p.predicted_speedup = 0;
+    double tgt = (req && req->max_rel_err > 0) ? req->max_rel_err : 1e-5;
+    double rho = (hints && hints->rho > 0) ? hints->rho : -1.0;
+
+    if (req && req->force_scheme != EMU_SCHEME_AUTO) {
+        p.chosen = (emu_scheme_t)req->force_scheme;
+        p.reason = "forced";
+        p.predicted_err = model_err_rho(m, p.chosen, K, 1, rho);
+        p.predicted_speedup = model_speed(m, p.chosen, 1);
+        return p;
+    }
+
+    bool fp16_safe = hints && hints->a_absmax > 0 && hints->b_absmax > 0 &&
+                     hints->a_absmax < m.fp16_max && hints->b_absmax < m.fp16_max &&
+                     hints->a_absmax > m.fp16_min && hints->b_absmax > m.fp16_min;
+
+    struct Cand { emu_scheme_t s; int c; };
+    std::vector<Cand> cands;
+    if (fp16_safe) cands.push_back({EMU_SCHEME_FP16X3, 1});
+    cands.push_back({EMU_SCHEME_BF16X3, 1});
+    cands.push_back({EMU_SCHEME_NATIVE_FP32, 1});
+    {
+        double need = (m.a_fp32 * m.a_fp32 * (double)K) / (tgt * tgt);
+        for (int c = 2; c <= m.max_chunks; c *= 2)
+            if (c >= need * 0.5) cands.push_back({EMU_SCHEME_FP32_CHUNKED, c});
+    }
+
+    double t_native = 2.0 * (double)M * N * K / m.fp32_flops;
+    auto eff_speedup = [&](emu_scheme_t s, int c) -> double {
+        double gemm = t_native / model_speed(m, s, c);
+        return t_native / (gemm + overhead_seconds(m, M, N, K, s));
+    };
+    bool found = false;
+    Cand best{EMU_SCHEME_NATIVE_FP32, 1};
+    double best_spd = -1;
+    for (const Cand& cd : cands) {
+        double e = model_err_rho(m, cd.s, K, cd.c, rho);
+        if (e > tgt) continue;
+        double sp = eff_speedup(cd.s, cd.c);
+        if (sp > best_spd) { best_spd = sp; best = cd; found = true; }
+    }
+    if (!found) {
+        p.chosen = EMU_SCHEME_FP32_CHUNKED;
+        p.chunks = m.max_chunks;
+        p.predicted_err = model_err_rho(m, EMU_SCHEME_FP32_CHUNKED, K, m.max_chunks, rho);
+        p.predicted_speedup = model_speed(m, EMU_SCHEME_FP32_CHUNKED, m.max_chunks);
+        p.reason = kReasonUnreachable;
+        return p;
+    }
+    p.chosen = best.s;
+    p.chunks = best.c;
+    p.predicted_err = model_err_rho(m, best.s, K, best.c, rho);
+    p.predicted_speedup = eff_speedup(best.s, best.c);
+    bool native_ok = model_err_rho(m, EMU_SCHEME_NATIVE_FP32, K, 1, rho) <= tgt;
+    if (p.predicted_speedup < 1.0 && native_ok) {
+        p.chosen = EMU_SCHEME_NATIVE_FP32;
+        p.chunks = 1;
+        p.predicted_err = model_err_rho(m, EMU_SCHEME_NATIVE_FP32, K, 1, rho);
+        p.predicted_speedup = 1.0;
+        p.reason = kReasonSlower;
+    } else {
+        p.reason = (p.chosen == EMU_SCHEME_FP16X3)        ? kReasonFp16
+                   : (p.chosen == EMU_SCHEME_BF16X3)      ? kReasonBf16
+                   : (p.chosen == EMU_SCHEME_FP32_CHUNKED) ? kReasonChunked
+                                                          : kReasonNative;
+    }
+    return p;
+}
+
+const char* const kReasonUnreachable = "TARGET UNREACHABLE: even fp32 with the maximum chunk count misses it";
+const char* const kReasonSlower = "emulation would be slower than native";
+const char* const kReasonFp16 = "fp16 range safe, lowest floor at top speed";
+const char* const kReasonBf16 = "robust, target above bf16x3 floor";
+const char* const kReasonChunked = "target below bf16x3 floor: fp32 + fp64 chunk sum";
+const char* const kReasonNative = "native fp32 suffices";
+
+}  // namespace emu
+
+extern "C" {
+
+emu_plan_t emugemm_plan(int M, int N, long K, const emu_request_t* req, const emu_hints_t* hints) {
+    return emu::plan(emu::model(), M, N, K, req, hints);
+}
+
+double emugemm_model_err(emu_scheme_t s, long K, int chunks) {
+    return emu::model_err(emu::model(), s, K, chunks);
+}
+
+double emugemm_model_err_rho(emu_scheme_t s, long K, int chunks, double rho) {
+    return emu::model_err_rho(emu::model(), s, K, chunks, rho);
+}
+
+double emugemm_model_speed(emu_scheme_t s, int chunks) {
+    return emu::model_speed(emu::model(), s, chunks);
+}
+
+emugemm_status_t emugemm_set_model(const char* name) {
+    return emu::set_model_by_name(name) ? EMUGEMM_STATUS_SUCCESS : EMUGEMM_STATUS_INVALID_VALUE;
+}
+
+const char* emugemm_get_model(void) { return emu::model().name; }
+
+}  // extern "C"

@@ -1,0 +1,263 @@
+"""ctypes binding of libemugemm.so (the C ABI declared in include/emugemm.h).
+
+The library is the product; this module only loads it and mirrors its structs so that Python callers
+(tests, bench.py, the multi-GPU driver) can call the same entry points a C caller would. Device buffers
+are passed as raw pointers; torch tensors are accepted for convenience and must already live on the
+device the handle was created on. Nothing here computes: if libemugemm.so is missing, loading fails.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import pathlib
+import re
+
+HERE = pathlib.Path(__file__).resolve().parent
+LIB_PATH = HERE / "libemugemm.so"
+HEADER = HERE.parent / "include" / "emugemm.h"
+
+# emu_scheme_t (src/emugemm.h:37-44 of emugemm-cdna)
+AUTO, NATIVE_FP32, FP32_CHUNKED, BF16X3, FP16X3, BF16X6 = range(6)
+SCHEME_NAMES = ["AUTO", "NATIVE_FP32", "FP32_CHUNKED", "BF16X3", "FP16X3", "BF16X6"]
+
+STATUS = {
+    0: "SUCCESS", 1: "INVALID_HANDLE", 2: "NOT_IMPLEMENTED", 3: "INVALID_POINTER", 4: "INVALID_SIZE",
+    5: "MEMORY_ERROR", 6: "INTERNAL_ERROR", 11: "INVALID_VALUE", 100: "ARCH_MISMATCH", 101: "TIMEOUT",
+}
+
+
+class EmuRequest(ctypes.Structure):
+    _fields_ = [("max_rel_err", ctypes.c_double), ("force_scheme", ctypes.c_int)]
+
+
+class EmuHints(ctypes.Structure):
+    _fields_ = [
+        ("a_absmax", ctypes.c_float),
+        ("b_absmax", ctypes.c_float),
+        ("a_is_reused", ctypes.c_int),
+        ("rho", ctypes.c_float),
+        ("rho_probes", ctypes.c_int),
+    ]
+
+
+class EmuPlan(ctypes.Structure):
+    _fields_ = [
+        ("chosen", ctypes.c_int),
+        ("chunks", ctypes.c_int),
+        ("predicted_err", ctypes.c_double),
+        ("predicted_speedup", ctypes.c_double),
+        ("reason", ctypes.c_char_p),
+    ]
+
+    def as_dict(self) -> dict:
+        return {
+            "chosen": SCHEME_NAMES[self.chosen] if 0 <= self.chosen < 6 else self.chosen,
+            "chunks": self.chunks,
+            "predicted_err": self.predicted_err,
+            "predicted_speedup": self.predicted_speedup,
+            "reason": self.reason.decode() if self.reason else None,
+        }
+
+
+class EmuGemmError(RuntimeError):
+    def __init__(self, fn: str, code: int):
+        super().__init__(f"{fn} failed: {STATUS.get(code, code)} ({code})")
+        self.code = code
+
+
+c_int, c_long, c_double, c_float, c_size_t, c_void_p = (
+    ctypes.c_int, ctypes.c_long, ctypes.c_double, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p)
+P = ctypes.POINTER
+
+_SIGS = {
+    "emugemm_create_handle": (c_int, [P(c_void_p)]),
+    "emugemm_destroy_handle": (c_int, [c_void_p]),
+    "emugemm_set_stream": (c_int, [c_void_p, c_void_p]),
+    "emugemm_set_workspace_limit": (c_int, [c_void_p, c_size_t]),
+    "emugemm_sync": (c_int, [c_void_p]),
+    "emugemm_init": (c_int, [ctypes.c_char_p]),
+    "emugemm_init_for_arch": (c_int, [ctypes.c_char_p, ctypes.c_char_p]),
+    "emugemm_tune_rows": (c_int, []),
+    "emugemm_tune_lookup": (c_int, [c_int, c_int, c_long, c_int]),
+    "emugemm_shutdown": (None, []),
+    "emugemm_plan": (EmuPlan, [c_int, c_int, c_long, P(EmuRequest), P(EmuHints)]),
+    "emugemm_sgemm": (c_int, [c_void_p, c_int, c_int, c_long, c_void_p, c_void_p, c_void_p,
+                              P(EmuRequest), P(EmuHints), P(EmuPlan)]),
+    "emugemm_sgemm_ex": (c_int, [c_void_p, c_int, c_int, c_long, c_void_p, c_long, c_void_p, c_long,
+                                 c_void_p, c_long, P(EmuRequest), P(EmuHints), P(EmuPlan)]),
+    "emugemm_sgemm_partial_f64": (c_int, [c_void_p, c_int, c_int, c_long, c_void_p, c_long, c_void_p,
+                                          c_long, c_void_p, c_int, c_int]),
+    "emugemm_reduce_f64": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "emugemm_model_err": (c_double, [c_int, c_long, c_int]),
+    "emugemm_model_err_rho": (c_double, [c_int, c_long, c_int, c_double]),
+    "emugemm_model_speed": (c_double, [c_int, c_int]),
+    "emugemm_estimate_rho": (c_double, [c_void_p, c_int, c_int, c_long, c_void_p, c_void_p, c_int]),
+    "emugemm_set_model": (c_int, [ctypes.c_char_p]),
+    "emugemm_get_model": (ctypes.c_char_p, []),
+    "emugemm_absmax": (c_int, [c_void_p, c_void_p, c_size_t, P(c_float)]),
+    "emugemm_split_bf16": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "emugemm_split_f16": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "emugemm_fp32_groups": (c_int, [c_int, c_int, c_long, c_int, c_int]),
+    "emugemm_kernel_launch_count": (ctypes.c_ulonglong, []),
+    "emugemm_profile_begin": (c_int, [c_void_p]),
+    "emugemm_profile_end": (c_int, [c_void_p, P(c_double), P(c_int), c_int]),
+    "emugemm_status_string": (ctypes.c_char_p, [c_int]),
+}
+
+_lib = None
+
+
+def header_functions() -> list[str]:
+    """Names of every function declared in include/emugemm.h."""
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(emugemm_[a-z0-9_]+)\s*\(", text)))
+
+
+def lib() -> ctypes.CDLL:
+    """Load libemugemm.so (raises OSError if it has not been built)."""
+    global _lib
+    if _lib is None:
+        path = os.environ.get("EMUGEMM_LIB", str(LIB_PATH))
+        l = ctypes.CDLL(path)
+        for name, (res, args) in _SIGS.items():
+            f = getattr(l, name, None)
+            if f is None:
+                continue
+            f.restype = res
+            f.argtypes = args
+        _lib = l
+    return _lib
+
+
+def _ptr(x) -> int:
+    if x is None:
+        return 0
+    if isinstance(x, int):
+        return x
+    return int(x.data_ptr())
+
+
+def check(fn: str, code: int) -> None:
+    if code != 0:
+        raise EmuGemmError(fn, code)
+
+
+def plan(M: int, N: int, K: int, max_rel_err: float = 1e-5, force: int = AUTO,
+         a_absmax: float = -1.0, b_absmax: float = -1.0, rho: float = -1.0, probes: int = 0,
+         hints: bool = True) -> EmuPlan:
+    req = EmuRequest(max_rel_err, force)
+    hn = EmuHints(a_absmax, b_absmax, 0, rho, probes)
+    return lib().emugemm_plan(M, N, K, ctypes.byref(req), ctypes.byref(hn) if hints else None)
+
+
+def set_model(name: str) -> None:
+    check("emugemm_set_model", lib().emugemm_set_model(name.encode()))
+
+
+def get_model() -> str:
+    return lib().emugemm_get_model().decode()
+
+
+class Handle:
+    """An emugemm handle on the current CUDA device (context manager)."""
+
+    def __init__(self, stream: int | None = None):
+        h = c_void_p()
+        check("emugemm_create_handle", lib().emugemm_create_handle(ctypes.byref(h)))
+        self.h = h
+        if stream is not None:
+            self.set_stream(stream)
+
+    def set_stream(self, stream) -> None:
+        s = stream if isinstance(stream, int) else int(getattr(stream, "cuda_stream", 0))
+        check("emugemm_set_stream", lib().emugemm_set_stream(self.h, c_void_p(s)))
+
+    def set_workspace_limit(self, nbytes: int) -> None:
+        check("emugemm_set_workspace_limit", lib().emugemm_set_workspace_limit(self.h, nbytes))
+
+    def close(self) -> None:
+        if self.h:
+            lib().emugemm_destroy_handle(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def sync(self) -> None:
+        check("emugemm_sync", lib().emugemm_sync(self.h))
+
+    def sgemm(self, M: int, N: int, K: int, A, B, C, max_rel_err: float = 1e-5, force: int = AUTO,
+              hints: EmuHints | None = None, use_hints: bool = True) -> tuple[EmuPlan, EmuHints | None]:
+        """C = A*B through emugemm_sgemm. hints=None -> measure absmax, do not estimate rho
+        (the reference's invariant-suite convention, bench/emugemm_test.cpp:101); use_hints=False passes
+        NULL (measure everything)."""
+        req = EmuRequest(max_rel_err, force)
+        if use_hints and hints is None:
+            hints = EmuHints(-1.0, -1.0, 0, 0.0, 0)
+        p = EmuPlan()
+        code = lib().emugemm_sgemm(self.h, M, N, K, _ptr(A), _ptr(B), _ptr(C), ctypes.byref(req),
+                                   ctypes.byref(hints) if use_hints else None, ctypes.byref(p))
+        check("emugemm_sgemm", code)
+        return p, hints
+
+    def sgemm_ex(self, M, N, K, A, lda, B, ldb, C, ldc, max_rel_err=1e-5, force=AUTO, hints=None):
+        req = EmuRequest(max_rel_err, force)
+        if hints is None:
+            hints = EmuHints(-1.0, -1.0, 0, 0.0, 0)
+        p = EmuPlan()
+        check("emugemm_sgemm_ex", lib().emugemm_sgemm_ex(self.h, M, N, K, _ptr(A), lda, _ptr(B), ldb, _ptr(C),
+                                                         ldc, ctypes.byref(req), ctypes.byref(hints),
+                                                         ctypes.byref(p)))
+        return p, hints
+
+    def partial_f64(self, M, N, K, A, lda, B, ldb, P64, scheme, chunks=1):
+        check("emugemm_sgemm_partial_f64",
+              lib().emugemm_sgemm_partial_f64(self.h, M, N, K, _ptr(A), lda, _ptr(B), ldb, _ptr(P64),
+                                              scheme, chunks))
+
+    def reduce_f64(self, M, N, G, P64, C):
+        check("emugemm_reduce_f64", lib().emugemm_reduce_f64(self.h, M, N, G, _ptr(P64), _ptr(C)))
+
+    def estimate_rho(self, M, N, K, A, B, probes=64) -> float:
+        return lib().emugemm_estimate_rho(self.h, M, N, K, _ptr(A), _ptr(B), probes)
+
+    def absmax(self, X, n: int) -> float:
+        out = c_float()
+        check("emugemm_absmax", lib().emugemm_absmax(self.h, _ptr(X), n, ctypes.byref(out)))
+        return out.value
+
+    def split_bf16(self, X, n, hi, lo) -> None:
+        check("emugemm_split_bf16", lib().emugemm_split_bf16(self.h, _ptr(X), n, _ptr(hi), _ptr(lo)))
+
+    def split_f16(self, X, n, hi, lo) -> None:
+        check("emugemm_split_f16", lib().emugemm_split_f16(self.h, _ptr(X), n, _ptr(hi), _ptr(lo)))
+
+    PROF_KINDS = ["tc_gemm", "fp32_gemm", "split", "scan", "rho", "reduce"]
+
+    def profile_begin(self) -> None:
+        check("emugemm_profile_begin", lib().emugemm_profile_begin(self.h))
+
+    def profile_end(self) -> dict:
+        n = len(self.PROF_KINDS)
+        ms = (c_double * n)()
+        cnt = (c_int * n)()
+        check("emugemm_profile_end", lib().emugemm_profile_end(self.h, ms, cnt, n))
+        return {k: (ms[i], cnt[i]) for i, k in enumerate(self.PROF_KINDS)}
+
+
+def launch_count() -> int:
+    return int(lib().emugemm_kernel_launch_count())
+
+
+def fp32_groups(M: int, N: int, K: int, chunks: int, num_sms: int) -> int:
+    return int(lib().emugemm_fp32_groups(M, N, K, chunks, num_sms))

@@ -1,0 +1,202 @@
+/* emugemm.h - emulated-FP32 SGEMM for NVIDIA B200 (sm_100a) with an accuracy-contract planner.
+ *
+ * C ABI of the library libemugemm.so. Names, struct layouts, enum values and plan reason strings are
+ * those of the emugemm C API (src/emugemm.h:37-99 of the emugemm-cdna project), so a caller written
+ * against that header keeps working after two mechanical renames:
+ *     rocblas_handle -> emugemm_handle_t      (opaque; created with emugemm_create_handle)
+ *     rocblas_status -> emugemm_status_t      (same numeric values for the codes the API returns)
+ * Defining EMUGEMM_ROCBLAS_COMPAT before including this header provides both spellings as typedefs.
+ *
+ * Semantics kept from the reference:
+ *   - row-major, non-transposed: C(MxN) = A(MxK) * B(KxN), lda=K, ldb=N, ldc=N, alpha=1, beta=0;
+ *   - A, B, C are DEVICE pointers owned by the caller;
+ *   - the planner never returns a plan whose predicted error exceeds req->max_rel_err unless its reason
+ *     starts with "TARGET UNREACHABLE" (it then still computes, with FP32_CHUNKED at the maximum chunk
+ *     count, and returns success);
+ *   - hints are in/out: a_absmax/b_absmax < 0 are measured, rho < 0 is estimated, and the measured
+ *     values are written back.
+ *
+ * Error model (iid data, rho_ref(K) = 0.64*sqrt(K)):
+ *     err(scheme, K, c, rho) = rho/rho_ref(K) * sqrt(floor_scheme^2 + a_scheme^2 * K/c)
+ * The constants come from a named calibration table: "b200" (the default, measured on B200 with this
+ * library's kernels) or "ref_mi250" (the reference's own constants, src/emugemm.cpp:16-23,92-93),
+ * selectable with emugemm_set_model() so plans can be compared with the reference planner exactly.
+ *
+ * No CPU fallback exists: every compute entry point runs CUDA kernels built for sm_100a and fails with
+ * EMUGEMM_STATUS_ARCH_MISMATCH on any other device.
+ */
+#ifndef EMUGEMM_H_
+#define EMUGEMM_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- types kept from src/emugemm.h:37-71 ---------------------------------------------------------- */
+
+typedef enum {
+    EMU_SCHEME_AUTO = 0,
+    EMU_SCHEME_NATIVE_FP32,
+    EMU_SCHEME_FP32_CHUNKED,
+    EMU_SCHEME_BF16X3,
+    EMU_SCHEME_FP16X3,
+    EMU_SCHEME_BF16X6       /* dominated; benchmarks only */
+} emu_scheme_t;
+
+typedef struct {
+    double max_rel_err;   /* required normwise Frobenius relative error, e.g. 1e-5 */
+    int    force_scheme;  /* emu_scheme_t; EMU_SCHEME_AUTO to let the dispatcher choose */
+} emu_request_t;
+
+typedef struct {
+    float  a_absmax, b_absmax;  /* < 0 means "unknown, please scan" (an O(MK+KN) pass) */
+    int    a_is_reused;         /* accepted for compatibility; no split cache is kept */
+    float  rho;                 /* cancellation ratio || |A||B| ||_F / ||AB||_F; < 0 = estimate it,
+                                   0 = do not estimate and plan with the iid model */
+    int    rho_probes;          /* Rademacher probes of the estimate; 0 -> 64 */
+} emu_hints_t;
+
+typedef struct {
+    emu_scheme_t chosen;
+    int          chunks;          /* c actually used */
+    double       predicted_err;   /* from the model above */
+    double       predicted_speedup;
+    const char*  reason;          /* static string, never freed */
+} emu_plan_t;
+
+/* ---- status and handle (replace rocblas_status / rocblas_handle) -------------------------------------- */
+
+typedef enum {
+    EMUGEMM_STATUS_SUCCESS         = 0,   /* rocblas_status_success */
+    EMUGEMM_STATUS_INVALID_HANDLE  = 1,   /* rocblas_status_invalid_handle */
+    EMUGEMM_STATUS_NOT_IMPLEMENTED = 2,   /* rocblas_status_not_implemented */
+    EMUGEMM_STATUS_INVALID_POINTER = 3,   /* rocblas_status_invalid_pointer */
+    EMUGEMM_STATUS_INVALID_SIZE    = 4,   /* rocblas_status_invalid_size */
+    EMUGEMM_STATUS_MEMORY_ERROR    = 5,   /* rocblas_status_memory_error */
+    EMUGEMM_STATUS_INTERNAL_ERROR  = 6,   /* rocblas_status_internal_error */
+    EMUGEMM_STATUS_INVALID_VALUE   = 11,  /* rocblas_status_invalid_value */
+    EMUGEMM_STATUS_ARCH_MISMATCH   = 100, /* device is not sm_100 (no emugemm-cdna counterpart) */
+    EMUGEMM_STATUS_TIMEOUT         = 101  /* a bounded device-side wait gave up; the context is intact */
+} emugemm_status_t;
+
+typedef struct emugemm_handle_s* emugemm_handle_t;
+
+#ifdef EMUGEMM_ROCBLAS_COMPAT
+typedef emugemm_status_t rocblas_status;
+typedef emugemm_handle_t rocblas_handle;
+#endif
+
+/* Create a handle bound to the CURRENT CUDA device and the legacy default stream.
+   Replaces rocblas_create_handle (the reference's harnesses call it before emugemm_init,
+   bench/emugemm_test.cpp:64). Fails with ARCH_MISMATCH unless the device is compute capability 10.0. */
+emugemm_status_t emugemm_create_handle(emugemm_handle_t* handle);
+/* Frees the handle's workspace. Replaces rocblas_destroy_handle. */
+emugemm_status_t emugemm_destroy_handle(emugemm_handle_t handle);
+/* All work of the handle is enqueued on `stream` (a cudaStream_t; NULL = legacy default stream).
+   Replaces rocblas_set_stream. */
+emugemm_status_t emugemm_set_stream(emugemm_handle_t handle, void* stream);
+/* Caps the handle's grow-only workspace; 0 = no cap. A call needing more returns MEMORY_ERROR. */
+emugemm_status_t emugemm_set_workspace_limit(emugemm_handle_t handle, size_t bytes);
+
+/* ---- functions kept from src/emugemm.h:77-99 ------------------------------------------------------------ */
+
+/* Load the per-shape tile table (replaces the rocBLAS solution-index table, src/emugemm.cpp:107-128).
+   Rows whose arch column does not match the live device ("sm_100a" on B200) are rejected and counted
+   on stderr. A missing file runs with the built-in tile choice and still returns success. */
+emugemm_status_t emugemm_init(const char* tune_csv_path);
+void             emugemm_shutdown(void);
+
+/* Decide only -- no GPU work (src/emugemm.cpp:216-282). */
+emu_plan_t emugemm_plan(int M, int N, long K, const emu_request_t* req, const emu_hints_t* hints);
+
+/* Row-major C = A*B on the handle's stream (src/emugemm.cpp:285-358). The call returns once the GEMM is
+   enqueued; the absmax scan and rho estimate, when requested, synchronise the stream to read their
+   results back to the host. */
+emugemm_status_t emugemm_sgemm(emugemm_handle_t handle,
+                               int M, int N, long K,
+                               const float* A, const float* B, float* C,
+                               const emu_request_t* req, emu_hints_t* hints,
+                               emu_plan_t* out_plan);
+
+double emugemm_model_err(emu_scheme_t s, long K, int chunks);          /* iid data (rho = rho_ref) */
+double emugemm_model_err_rho(emu_scheme_t s, long K, int chunks, double rho);
+/* Estimate rho on the device with `probes` Rademacher vectors (<= 0 -> 64). Returns < 0 on failure. */
+double emugemm_estimate_rho(emugemm_handle_t h, int M, int N, long K,
+                            const float* A, const float* B, int probes);
+double emugemm_model_speed(emu_scheme_t s, int chunks);
+
+/* ---- additions without an emugemm-cdna counterpart ------------------------------------------------------ */
+
+/* Select the planner's constant table: "b200" (default) or "ref_mi250" (the reference constants, so that
+   plans agree with the reference planner bit for bit). Returns INVALID_VALUE for an unknown name. */
+emugemm_status_t emugemm_set_model(const char* name);
+const char*      emugemm_get_model(void);
+
+/* Device max |x| over n floats (the scan of src/emugemm.cpp:155-168), synchronous. */
+emugemm_status_t emugemm_absmax(emugemm_handle_t h, const float* X, size_t n, float* out_absmax);
+
+/* Debug split kernels for the bit-exact slice test (src/emugemm.cpp:143-148): element-wise, no scaling.
+   bf16: hi = RNE_bf16(x), lo = RNE_bf16(x - hi).  fp16: hi = RNE_f16(x), lo = RNE_f16((x - hi)*2048).
+   Outputs are n 16-bit words each (raw bit patterns). Asynchronous on the handle's stream. */
+emugemm_status_t emugemm_split_bf16(emugemm_handle_t h, const float* X, size_t n,
+                                    unsigned short* hi, unsigned short* lo);
+emugemm_status_t emugemm_split_f16(emugemm_handle_t h, const float* X, size_t n,
+                                   unsigned short* hi, unsigned short* lo);
+
+/* Strided variant of emugemm_sgemm with explicit leading dimensions (lda >= K, ldb >= N, ldc >= N), used
+   by the multi-GPU drivers to run on a panel of B or a block of rows of A in place. */
+emugemm_status_t emugemm_sgemm_ex(emugemm_handle_t handle,
+                                  int M, int N, long K,
+                                  const float* A, long lda, const float* B, long ldb,
+                                  float* C, long ldc,
+                                  const emu_request_t* req, emu_hints_t* hints,
+                                  emu_plan_t* out_plan);
+
+/* K-split partial: P(MxN, FP64, ld=N) = A(MxK) * B(KxN) computed with `scheme` (BF16X3, FP16X3,
+   NATIVE_FP32 or FP32_CHUNKED with `chunks`), written in FP64 so that partials from several devices can
+   be summed exactly enough (ncclFloat64) before one final rounding to FP32. */
+emugemm_status_t emugemm_sgemm_partial_f64(emugemm_handle_t handle,
+                                           int M, int N, long K,
+                                           const float* A, long lda, const float* B, long ldb,
+                                           double* P, int scheme, int chunks);
+
+/* C(MxN, FP32) = round(sum_{g<G} P[g]) for G FP64 partials of MxN each, summed in order g = 0..G-1. */
+emugemm_status_t emugemm_reduce_f64(emugemm_handle_t handle, int M, int N, int G,
+                                    const double* P, float* C);
+
+/* Synchronise the handle's stream; returns TIMEOUT if a kernel of this handle gave up a bounded wait. */
+emugemm_status_t emugemm_sync(emugemm_handle_t handle);
+
+/* emugemm_init with an explicit live arch string instead of the current device's, so the table parser
+   and its arch rejection can be exercised without a GPU. */
+emugemm_status_t emugemm_init_for_arch(const char* tune_csv_path, const char* live_arch);
+/* Rows accepted by the last init, and the tile code the table gives a shape (0 = none within range).
+   dtype: 0 fp32, 1 bf16, 2 fp16. */
+int emugemm_tune_rows(void);
+int emugemm_tune_lookup(int M, int N, long K, int dtype);
+
+/* Number of FP64 partial groups the FP32_CHUNKED kernel uses for this shape on a GPU with num_sms SMs
+   (fixes its summation order: chunk sums within a group in order, then the groups in order). */
+int emugemm_fp32_groups(int M, int N, long K, int chunks, int num_sms);
+
+/* Per-handle kernel timing with CUDA events recorded on the handle's stream around each kernel class:
+   0 tensor-core GEMM, 1 FP32 GEMM (+ FP64 reduce), 2 slice split, 3 absmax / exponent scans, 4 rho probe,
+   5 FP64 reduce. profile_end synchronises and returns the summed milliseconds and launch counts of the
+   first nkinds classes. */
+emugemm_status_t emugemm_profile_begin(emugemm_handle_t handle);
+emugemm_status_t emugemm_profile_end(emugemm_handle_t handle, double* ms_by_kind, int* count_by_kind,
+                                     int nkinds);
+
+/* Number of kernels this library launched since the process started (all handles). */
+unsigned long long emugemm_kernel_launch_count(void);
+
+/* Human-readable name of a status code (static string). */
+const char* emugemm_status_string(emugemm_status_t s);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EMUGEMM_H_ */

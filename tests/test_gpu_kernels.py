@@ -1,0 +1,301 @@
+"""GPU parity of every kernel on the hot path, called through the C ABI and checked against the CPU oracle.
+
+Bars:
+- slice split, absmax, exponent scans: bit-exact;
+- NATIVE_FP32 / FP32_CHUNKED: bit-exact against the oracle's replica of the same FMA chains and FP64
+  chunk sums (same group split);
+- bf16x3 / fp16x3 tensor-core GEMM: against the exact FP64 value of the three slice products (the oracle's
+  slice_product), within the FP32 accumulation bound stated per test; and against FP64 truth within the
+  plan's predicted error;
+- rho estimate: against the oracle's FP64 evaluation of the same Hutchinson estimate.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import datagen
+import emugemm
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(torch, x):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def run_sgemm(torch, h, A, B, force=emugemm.AUTO, tgt=1e-5, hints=None, use_hints=True):
+    M, K = A.shape
+    N = B.shape[1]
+    dA, dB = dev(torch, A), dev(torch, B)
+    dC = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+    p, hn = h.sgemm(M, N, K, dA, dB, dC, max_rel_err=tgt, force=force, hints=hints, use_hints=use_hints)
+    h.sync()
+    return dC.cpu().numpy(), p, hn
+
+
+# ---------------------------------------------------------------------------------------------- split
+@pytest.mark.parametrize("n", [1, 7, 4096, 1000003])
+def test_split_bf16_bitexact(cuda, handle, n):
+    torch = cuda
+    x = datagen.wide_range((n,), 100 + n, emax=60)
+    if n > 8:
+        x[:8] = [0.0, -0.0, 1.0, 1.00390625, 2 ** -140, -3.4e38, 65504.0, 1.0 + 2 ** -9]
+    dx = dev(torch, x)
+    hi = torch.empty(n, dtype=torch.int16, device="cuda")
+    lo = torch.empty(n, dtype=torch.int16, device="cuda")
+    handle.split_bf16(dx, n, hi, lo)
+    handle.sync()
+    rh, rl = oracle.split_bf16(x)
+    assert np.array_equal(hi.cpu().numpy().view(np.uint16), rh)
+    assert np.array_equal(lo.cpu().numpy().view(np.uint16), rl)
+
+
+@pytest.mark.parametrize("n", [5, 65536, 999999])
+def test_split_f16_bitexact(cuda, handle, n):
+    torch = cuda
+    x = datagen.normal((n,), 7 + n, scale=100.0)
+    dx = dev(torch, x)
+    hi = torch.empty(n, dtype=torch.int16, device="cuda")
+    lo = torch.empty(n, dtype=torch.int16, device="cuda")
+    handle.split_f16(dx, n, hi, lo)
+    handle.sync()
+    rh, rl = oracle.split_f16(x)
+    assert np.array_equal(hi.cpu().numpy().view(np.uint16), rh)
+    assert np.array_equal(lo.cpu().numpy().view(np.uint16), rl)
+
+
+@pytest.mark.parametrize("n", [1, 333, 1 << 22])
+def test_absmax_exact(cuda, handle, n):
+    torch = cuda
+    x = datagen.wide_range((n,), 5 + n)
+    assert handle.absmax(dev(torch, x), n) == oracle.absmax(x)
+
+
+# ------------------------------------------------------------------------------------------- FP32 SIMT
+FP32_SHAPES = [(64, 64, 64), (130, 70, 333), (1, 1, 1), (5, 3, 1), (256, 256, 4096), (300, 520, 1000),
+               (1024, 1024, 256)]
+
+
+@pytest.mark.parametrize("shape", FP32_SHAPES, ids=[str(s) for s in FP32_SHAPES])
+def test_native_fp32_bitexact(cuda, handle, shape):
+    torch = cuda
+    M, N, K = shape
+    A = datagen.uniform((M, K), 1 + M)
+    B = datagen.uniform((K, N), 2 + N)
+    C, p, _ = run_sgemm(torch, handle, A, B, force=emugemm.NATIVE_FP32)
+    assert p.chosen == emugemm.NATIVE_FP32
+    assert np.array_equal(C, oracle.fp32_chunked(A, B, 1))
+
+
+@pytest.mark.parametrize("shape,chunks", [((256, 256, 8192), 4), ((256, 256, 8192), 16), ((64, 128, 5000), 7),
+                                          ((256, 256, 4096), 256), ((512, 384, 3000), 2), ((33, 17, 100), 256)])
+def test_chunked_fp32_bitexact(cuda, handle, shape, chunks):
+    """FP32_CHUNKED through the partial (FP64 output) and reduce entry points, bit-exact in FP64."""
+    torch = cuda
+    M, N, K = shape
+    A = datagen.uniform((M, K), 3 + K)
+    B = datagen.uniform((K, N), 4 + K)
+    dA, dB = dev(torch, A), dev(torch, B)
+    P64 = torch.empty((M, N), dtype=torch.float64, device="cuda")
+    handle.partial_f64(M, N, K, dA, K, dB, N, P64, emugemm.FP32_CHUNKED, chunks)
+    C = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    handle.reduce_f64(M, N, 1, P64, C)
+    handle.sync()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    G = emugemm.fp32_groups(M, N, K, chunks, sms)
+    cpg = oracle.group_size(K, chunks, G)
+    want = oracle.fp32_chunked(A, B, chunks, cpg=cpg, f64=True)
+    assert np.array_equal(P64.cpu().numpy(), want)
+    assert np.array_equal(C.cpu().numpy(), want.astype(np.float32))
+
+
+def test_auto_chunked_plan_runs_chunked(cuda, handle):
+    """A target below the bf16x3 floor routes to FP32_CHUNKED with c > 1; the result is the bit-exact chain."""
+    torch = cuda
+    M, N, K = 256, 256, 65536
+    A = datagen.uniform((M, K), 31)
+    B = datagen.uniform((K, N), 32)
+    hints = emugemm.EmuHints(1.0, 1.0, 0, 0.0, 0)
+    C, p, _ = run_sgemm(torch, handle, A, B, tgt=1e-6, hints=hints)
+    assert p.chosen == emugemm.FP32_CHUNKED and p.chunks > 1
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    G = emugemm.fp32_groups(M, N, K, p.chunks, sms)
+    want = oracle.fp32_chunked(A, B, p.chunks, cpg=oracle.group_size(K, p.chunks, G))
+    assert np.array_equal(C, want)
+    R = oracle.gemm_f64(A, B)
+    assert oracle.rel_err(C, R) <= p.predicted_err
+
+
+# ---------------------------------------------------------------------------------- tensor-core 3-product
+TC_SHAPES = [(128, 256, 64), (256, 512, 1024), (200, 300, 500), (1, 1, 1), (129, 257, 65), (1024, 1024, 1024),
+             (384, 768, 4096)]
+
+
+def _accum_bound(K):
+    # FP32 accumulation + output rounding, relative to ||R||: generous bound for the slice-product check.
+    return 1.5e-7 + 2.0e-8 * np.sqrt(K)
+
+
+@pytest.mark.parametrize("shape", TC_SHAPES, ids=[str(s) for s in TC_SHAPES])
+def test_bf16x3_matches_slice_products(cuda, handle, shape):
+    torch = cuda
+    M, N, K = shape
+    A = datagen.normal((M, K), 12345)
+    B = datagen.normal((K, N), 67890)
+    C, p, _ = run_sgemm(torch, handle, A, B, force=emugemm.BF16X3)
+    assert p.chosen == emugemm.BF16X3 and p.reason == b"forced"
+    Rh = oracle.slice_product(A, B, kind=0)
+    R = oracle.gemm_f64(A, B)
+    d = np.linalg.norm(C.astype(np.float64) - Rh) / np.linalg.norm(R)
+    print(f"bf16x3 {shape}: |C-Rhat|/|R| = {d:.3e}  err vs fp64 = {oracle.rel_err(C, R):.3e}")
+    assert np.isfinite(C).all()
+    assert d <= _accum_bound(K)
+
+
+@pytest.mark.parametrize("shape", [(128, 128, 64), (200, 300, 500), (512, 256, 2048), (1, 1, 1)])
+def test_fp16x3_scaled_matches_slice_products(cuda, handle, shape):
+    torch = cuda
+    M, N, K = shape
+    A = datagen.wide_range((M, K), 77)
+    B = datagen.wide_range((K, N), 78)
+    C, p, _ = run_sgemm(torch, handle, A, B, force=emugemm.FP16X3)
+    assert p.chosen == emugemm.FP16X3
+    Rh = oracle.slice_product(A, B, kind=1)
+    R = oracle.gemm_f64(A, B)
+    d = np.linalg.norm(C.astype(np.float64) - Rh) / np.linalg.norm(R)
+    print(f"fp16x3 {shape}: |C-Rhat|/|R| = {d:.3e}  err vs fp64 = {oracle.rel_err(C, R):.3e}")
+    assert np.isfinite(C).all()
+    assert d <= _accum_bound(K)
+    assert oracle.rel_err(C, R) < 2e-6
+
+
+def test_bf16x6_forced_runs_bf16x3(cuda, handle):
+    """Reference quirk (src/emugemm.cpp:331): a forced BF16X6 runs the bf16x3 kernel."""
+    torch = cuda
+    A = datagen.normal((256, 256), 1)
+    B = datagen.normal((256, 256), 2)
+    C6, p6, _ = run_sgemm(torch, handle, A, B, force=emugemm.BF16X6)
+    C3, _, _ = run_sgemm(torch, handle, A, B, force=emugemm.BF16X3)
+    assert p6.chosen == emugemm.BF16X6
+    assert np.array_equal(C6, C3)
+
+
+def test_bf16x3_deterministic(cuda, handle):
+    torch = cuda
+    A = datagen.normal((512, 1024), 3)
+    B = datagen.normal((1024, 768), 4)
+    C1, _, _ = run_sgemm(torch, handle, A, B, force=emugemm.BF16X3)
+    C2, _, _ = run_sgemm(torch, handle, A, B, force=emugemm.BF16X3)
+    assert np.array_equal(C1, C2)
+
+
+# --------------------------------------------------------------------------------------------- rho
+@pytest.mark.parametrize("shape", [(64, 48, 256), (256, 256, 2048), (130, 70, 1000)])
+def test_rho_estimate_matches_oracle(cuda, handle, shape):
+    torch = cuda
+    M, N, K = shape
+    A = datagen.normal((M, K), 5)
+    B = datagen.normal((K, N), 6)
+    r = handle.estimate_rho(M, N, K, dev(torch, A), dev(torch, B), 64)
+    ro, _ = oracle.rho_hutchinson(A, B, 64)
+    assert r == pytest.approx(ro, rel=1e-4)
+
+
+def test_rho_estimate_adversarial(cuda, handle):
+    torch = cuda
+    M, K = 256, 4096
+    A, B = datagen.family2(M, M, K, 1e4)
+    r = handle.estimate_rho(M, M, K, dev(torch, A), dev(torch, B), 64)
+    ro, _ = oracle.rho_hutchinson(A, B, 64)
+    assert r == pytest.approx(ro, rel=2e-2)
+
+
+def test_hints_written_back(cuda, handle):
+    torch = cuda
+    A = datagen.normal((256, 512), 8)
+    B = datagen.normal((512, 128), 9)
+    hn = emugemm.EmuHints(-1.0, -1.0, 0, -1.0, 32)
+    C, p, hn = run_sgemm(torch, handle, A, B, tgt=1e-5, hints=hn)
+    assert hn.a_absmax == oracle.absmax(A)
+    assert hn.b_absmax == oracle.absmax(B)
+    ro, _ = oracle.rho_hutchinson(A, B, 32)
+    assert hn.rho == pytest.approx(ro, rel=1e-4)
+
+
+def test_null_hints_measure_everything(cuda, handle):
+    torch = cuda
+    A = datagen.normal((128, 256), 10)
+    B = datagen.normal((256, 128), 11)
+    C, p, _ = run_sgemm(torch, handle, A, B, tgt=1e-5, use_hints=False)
+    R = oracle.gemm_f64(A, B)
+    assert oracle.rel_err(C, R) <= p.predicted_err
+
+
+# ----------------------------------------------------------------------------------------- edge cases
+def test_zero_sizes(cuda, handle):
+    torch = cuda
+    A = torch.zeros((4, 0), device="cuda")
+    B = torch.zeros((0, 5), device="cuda")
+    C = torch.full((4, 5), 7.0, device="cuda")
+    for force in (emugemm.NATIVE_FP32, emugemm.BF16X3, emugemm.FP16X3):
+        C.fill_(7.0)
+        handle.sgemm(4, 5, 0, A, B, C, force=force)
+        handle.sync()
+        assert torch.count_nonzero(C).item() == 0
+    handle.sgemm(0, 5, 3, torch.zeros(1, device="cuda"), torch.zeros(15, device="cuda"), C, force=emugemm.BF16X3)
+
+
+def test_workspace_limit_reports_memory_error(cuda):
+    torch = cuda
+    h = emugemm.Handle()
+    try:
+        h.set_workspace_limit(1 << 20)
+        A = torch.randn(1024, 1024, device="cuda")
+        B = torch.randn(1024, 1024, device="cuda")
+        C = torch.empty(1024, 1024, device="cuda")
+        with pytest.raises(emugemm.EmuGemmError) as e:
+            h.sgemm(1024, 1024, 1024, A, B, C, force=emugemm.BF16X3)
+        assert e.value.code == 5
+    finally:
+        h.close()
+
+
+def test_invalid_sizes(cuda, handle):
+    torch = cuda
+    A = torch.zeros(16, device="cuda")
+    with pytest.raises(emugemm.EmuGemmError) as e:
+        handle.sgemm(-1, 4, 4, A, A, A)
+    assert e.value.code == 4
+
+
+def test_strided_operands(cuda, handle):
+    """emugemm_sgemm_ex on sub-blocks of larger arrays (leading dimensions > K, N)."""
+    torch = cuda
+    A = datagen.normal((300, 520), 40)
+    B = datagen.normal((600, 410), 41)
+    M, K, N = 200, 500, 400
+    dA, dB = dev(torch, A), dev(torch, B)
+    C = torch.zeros((250, 450), dtype=torch.float32, device="cuda")
+    for force in (emugemm.NATIVE_FP32, emugemm.BF16X3, emugemm.FP16X3):
+        C.zero_()
+        handle.sgemm_ex(M, N, K, dA, 520, dB, 410, C, 450, force=force,
+                        hints=emugemm.EmuHints(1.0, 1.0, 0, 0.0, 0))
+        handle.sync()
+        Cn = C.cpu().numpy()
+        R = oracle.gemm_f64(A[:M, :K], B[:K, :N])
+        assert oracle.rel_err(Cn[:M, :N], R) < 2e-5
+        assert np.count_nonzero(Cn[M:, :]) == 0 and np.count_nonzero(Cn[:, N:]) == 0
+        if force == emugemm.NATIVE_FP32:
+            assert np.array_equal(Cn[:M, :N], oracle.fp32_chunked(A[:M, :K], B[:K, :N], 1))
+
+
+def test_launch_counter_advances(cuda, handle):
+    torch = cuda
+    before = emugemm.launch_count()
+    A = torch.randn(64, 64, device="cuda")
+    C = torch.empty(64, 64, device="cuda")
+    handle.sgemm(64, 64, 64, A, A, C, force=emugemm.BF16X3, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+    handle.sync()
+    assert emugemm.launch_count() >= before + 3
