@@ -35,13 +35,14 @@ SCHEMES = {"bf16x3": 3, "fp16x3": 4, "native": 1}
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--size", type=int, default=8192)
     ap.add_argument("--scheme", default="bf16x3", choices=list(SCHEMES))
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-cublas", action="store_true")
     return ap.parse_args()
 
 
@@ -68,7 +69,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -285,6 +286,25 @@ def ours(args) -> None:
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_fp64_baseline(S)
 
+    # cuBLAS SGEMM on the same GPU and shape (strict FP32: no TF32), a comparison figure only
+    cublas = None
+    if world == 1 and not args.no_cublas:
+        torch.backends.cuda.matmul.allow_tf32 = False
+        torch.set_float32_matmul_precision("highest")
+        for _ in range(3):
+            torch.matmul(A, B, out=C)
+        torch.cuda.synchronize()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_cb = 10
+        c0.record(stream)
+        for _ in range(n_cb):
+            torch.matmul(A, B, out=C)
+        c1.record(stream)
+        torch.cuda.synchronize()
+        cb_ms = c0.elapsed_time(c1) / n_cb
+        cublas = {"sgemm_tflops": 2.0 * M * N * K / (cb_ms * 1e-3) / 1e12, "ms": cb_ms,
+                  "note": "torch.matmul fp32, allow_tf32=False, same inputs"}
+
     if rank == 0:
         line = {
             "metric": "emulated-FP32 TFLOPS", "value": value, "unit": "TFLOPS", "n_gpus": world,
@@ -303,6 +323,7 @@ def ours(args) -> None:
                          "traffic": None},
             "kernel_ms": {k: (v[0] / v[1] if v[1] else None) for k, v in prof.items()},
             "cpu_baseline": cpu,
+            "cublas_sgemm": cublas,
             "e2e": e2e,
             "clocks": clk.summary(),
             "gpu_launches": launches,

@@ -25,6 +25,7 @@ struct ModelConsts {
     double hbm_bps, fp32_flops;
     double ovh_native, ovh_chunked, ovh_emulated, ovh_fp16x3;   // bytes per input element
     double rho_ref_coef;
+    double rho_factor_min;   // lower clamp of rho/rho_ref(K); 0 = none (the reference's model)
 };
 
 const ModelConsts& model();

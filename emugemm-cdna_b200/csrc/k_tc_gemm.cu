@@ -6,16 +6,25 @@
 // into two (fp16x3: hi*hi and the two cross products, which carry the lo slice's 2^11 factor), so C is
 // written once.
 //
+// Promotion. The tensor-core FP32 accumulator truncates its partial sums (measured on B200: the error of
+// an accumulation grows linearly in K with a systematic bias toward zero, about 4e-6 relative at
+// K = 4096), which would exceed the bf16x3 floor by K ~ 4000. So a TMEM accumulator only ever sums one
+// chunk of kChunkKB k-blocks (128 values of K); the epilogue warps drain every chunk into FP32 registers
+// with round-to-nearest adds while the MMAs of the next chunk run into the other TMEM buffer. Measured at
+// 8192^3 on N(0,1) data: chunks of 64/128/256/512 values of K give bf16x3 errors 4.43/4.44/4.50/4.72e-6
+// (the representation floor of the split is 4.4355e-6) for kernel times 2.44/2.34/2.30/2.25 ms.
+//
 // Operands are pre-split 16-bit slices in HBM, K-major (A: Mp x Kp, B transposed: Np x Kp), loaded by
 // TMA with the 128-byte swizzle straight into the UMMA canonical layout.
 //
-// Warp roles (192 threads, one CTA per SM, persistent over output tiles):
+// Warp roles (320 threads, one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer (one elected thread)
 //   warp 1      TMEM allocator and MMA issuer (one elected thread)
-//   warps 2..5  epilogue: tcgen05.ld from TMEM -> registers -> C
-// TMEM holds two accumulator buffers (512 columns), so the epilogue of tile i overlaps the MMAs of tile
-// i+1. Every wait is bounded; on a timeout the kernel records it in the error word, drains its copies
-// and MMAs in flight, frees TMEM and returns.
+//   warps 2..9  promotion/epilogue: warp w drains TMEM lanes 32*(w%4).. and half (w-2)/4 of the columns,
+//               keeps the running FP32 sums of its 32 rows x BN/2 columns in registers, stores C
+// TMEM holds two accumulator buffers (512 columns) that alternate chunk by chunk. Every wait is bounded;
+// on a timeout the kernel records it in the error word, drains its copies and MMAs in flight, frees TMEM
+// and returns.
 #include "device_utils.cuh"
 #include "emugemm_internal.h"
 
@@ -32,7 +41,12 @@ using namespace dev;
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;              // 64 16-bit elements = one 128-byte swizzle row
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+#ifndef EMUGEMM_CHUNK_KB
+#define EMUGEMM_CHUNK_KB 2
+#endif
+constexpr int kChunkKB = EMUGEMM_CHUNK_KB;   // k-blocks accumulated in TMEM before promotion (2 = 128 of K)
 constexpr int kGroupM = 16;          // tile raster: groups of 16 row blocks sweep all column blocks
 
 template <bool FP16>
@@ -43,6 +57,7 @@ struct Cfg {
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     static constexpr int STAGES = FP16 ? 3 : 2;
     static constexpr int ACC_COLS = FP16 ? 2 * BN : BN;    // TMEM columns per accumulator buffer
+    static constexpr int HALF = BN / 2;                     // columns per epilogue thread
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*control*/;
     static constexpr uint32_t IDESC = idesc_f16(kBM, BN, !FP16);
 };
@@ -97,6 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int num_tiles = p.num_m * p.num_n;
+    const int nchunks = (p.nk + kChunkKB - 1) / kChunkKB;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C_::STAGES; ++s) {
@@ -105,7 +121,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&ctl->tmem_full[b], 1);
-            mbar_init(&ctl->tmem_empty[b], 128);
+            mbar_init(&ctl->tmem_empty[b], 32 * kEpiWarps);
         }
         mbar_init(&ctl->drain, 1);
         ctl->abort = 0;
@@ -155,39 +171,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            // ---------------- MMA issuer ----------------
-            long it = 0;
-            int local = 0;
+            // ---------------- MMA issuer: one TMEM buffer per chunk of kChunkKB k-blocks ----------------
+            long it = 0, ch = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
-                const int b = local & 1;
-                const uint32_t bph = (uint32_t)((local >> 1) & 1);
-                if (!mbar_wait(&ctl->tmem_empty[b], bph ^ 1u, abort, p.err, kErrTimeoutMma)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t d_main = tmem_base + (uint32_t)(b * C_::ACC_COLS);
-                const uint32_t d_cross = FP16 ? d_main + (uint32_t)C_::BN : d_main;
-                for (int kb = 0; kb < p.nk; ++kb, ++it) {
-                    const int s = (int)(it % C_::STAGES);
-                    const uint32_t ph = (uint32_t)((it / C_::STAGES) & 1);
-                    if (!mbar_wait(&ctl->full[s], ph, abort, p.err, kErrTimeoutMma)) { ok = false; break; }
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+                for (int kb0 = 0; kb0 < p.nk && ok; kb0 += kChunkKB, ++ch) {
+                    const int b = (int)(ch & 1);
+                    const uint32_t bph = (uint32_t)((ch >> 1) & 1);
+                    if (!mbar_wait(&ctl->tmem_empty[b], bph ^ 1u, abort, p.err, kErrTimeoutMma)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t st = smem_u32(smem + s * C_::STAGE_BYTES);
-                    const uint64_t a_hi = sdesc_kmajor_sw128(st);
-                    const uint64_t a_lo = sdesc_kmajor_sw128(st + C_::A_BYTES);
-                    const uint64_t b_hi = sdesc_kmajor_sw128(st + 2 * C_::A_BYTES);
-                    const uint64_t b_lo = sdesc_kmajor_sw128(st + 2 * C_::A_BYTES + C_::B_BYTES);
+                    const uint32_t d_main = tmem_base + (uint32_t)(b * C_::ACC_COLS);
+                    const uint32_t d_cross = FP16 ? d_main + (uint32_t)C_::BN : d_main;
+                    const int kb1 = min(p.nk, kb0 + kChunkKB);
+                    for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                        const int s = (int)(it % C_::STAGES);
+                        const uint32_t ph = (uint32_t)((it / C_::STAGES) & 1);
+                        if (!mbar_wait(&ctl->full[s], ph, abort, p.err, kErrTimeoutMma)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t st = smem_u32(smem + s * C_::STAGE_BYTES);
+                        const uint64_t a_hi = sdesc_kmajor_sw128(st);
+                        const uint64_t a_lo = sdesc_kmajor_sw128(st + C_::A_BYTES);
+                        const uint64_t b_hi = sdesc_kmajor_sw128(st + 2 * C_::A_BYTES);
+                        const uint64_t b_lo = sdesc_kmajor_sw128(st + 2 * C_::A_BYTES + C_::B_BYTES);
 #pragma unroll
-                    for (int ks = 0; ks < kBK / 16; ++ks) {
-                        const uint64_t adv = (uint64_t)(ks * 32) >> 4;   // 16 elements = 32 bytes along K
-                        const uint32_t acc = (kb | ks) ? 1u : 0u;
-                        mma_f16_ss(d_cross, a_lo + adv, b_hi + adv, C_::IDESC, acc);
-                        mma_f16_ss(d_cross, a_hi + adv, b_lo + adv, C_::IDESC, 1u);
-                        mma_f16_ss(d_main, a_hi + adv, b_hi + adv, C_::IDESC, FP16 ? acc : 1u);
+                        for (int ks = 0; ks < kBK / 16; ++ks) {
+                            const uint64_t adv = (uint64_t)(ks * 32) >> 4;   // 16 elements = 32 bytes along K
+                            const uint32_t acc = (kb != kb0 || ks != 0) ? 1u : 0u;
+                            mma_f16_ss(d_cross, a_lo + adv, b_hi + adv, C_::IDESC, acc);
+                            mma_f16_ss(d_cross, a_hi + adv, b_lo + adv, C_::IDESC, 1u);
+                            mma_f16_ss(d_main, a_hi + adv, b_hi + adv, C_::IDESC, FP16 ? acc : 1u);
+                        }
+                        mma_commit(&ctl->empty[s]);
                     }
-                    mma_commit(&ctl->empty[s]);
+                    if (!ok) break;
+                    mma_commit(&ctl->tmem_full[b]);
                 }
-                if (!ok) break;
-                mma_commit(&ctl->tmem_full[b]);
             }
             if (!ok) {
                 mma_commit(&ctl->drain);
@@ -195,72 +213,85 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
-        const int sp = warp & 3;                 // TMEM sub-partition this warp may access
+        // ---------------- promotion + epilogue (warps 2..9) ----------------
+        const int sp = warp & 3;                       // TMEM sub-partition this warp may access
+        const int half = (warp - 2) >> 2;              // column half of the tile
         const int row_in_tile = sp * 32 + lane;
-        int local = 0;
-        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+        const int col0 = half * C_::HALF;
+        const uint32_t lane_off = (uint32_t)(sp * 32) << 16;
+        long ch = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
             int mb, nb;
             tile_coords(t, p.num_m, p.num_n, mb, nb);
-            const int b = local & 1;
-            const uint32_t bph = (uint32_t)((local >> 1) & 1);
-            bool ready = mbar_wait(&ctl->tmem_full[b], bph, abort, p.err, kErrTimeoutEpilogue);
-            if (!__all_sync(0xffffffffu, ready)) break;   // tcgen05.ld below needs the whole warp
-            tc_fence_after();
-            const int m = mb * kBM + row_in_tile;
-            const uint32_t tbase = tmem_base + ((uint32_t)(sp * 32) << 16) + (uint32_t)(b * C_::ACC_COLS);
-            int e_row = 0;
-            if (FP16 && m < p.M) e_row = p.row_exp[m];
-#pragma unroll 1
-            for (int cc = 0; cc < C_::BN / 32; ++cc) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(tbase + (uint32_t)(cc * 32), r);
-                float v[32];
-                if (FP16) {
-                    uint32_t x[32];
-                    tmem_ld_32x32b_x32(tbase + (uint32_t)(C_::BN + cc * 32), x);
-                    tmem_ld_wait();
+            float sum[C_::HALF];
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        v[j] = __uint_as_float(r[j]) + __uint_as_float(x[j]) * (1.0f / 2048.0f);
-                } else {
-                    tmem_ld_wait();
+            for (int j = 0; j < C_::HALF; ++j) sum[j] = 0.f;
+            for (int c = 0; c < nchunks; ++c, ++ch) {
+                const int b = (int)(ch & 1);
+                const uint32_t bph = (uint32_t)((ch >> 1) & 1);
+                bool ready = mbar_wait(&ctl->tmem_full[b], bph, abort, p.err, kErrTimeoutEpilogue);
+                if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }   // tcgen05.ld needs the whole warp
+                tc_fence_after();
+                const uint32_t tb = tmem_base + lane_off + (uint32_t)(b * C_::ACC_COLS + col0);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-                }
-                if (m < p.M) {
-                    const int n0 = nb * C_::BN + cc * 32;
+                for (int q = 0; q < C_::HALF / 16; ++q) {
+                    uint32_t r[16];
+                    tmem_ld_32x32b_x16(tb + (uint32_t)(q * 16), r);
                     if (FP16) {
+                        uint32_t x[16];
+                        tmem_ld_32x32b_x16(tb + (uint32_t)(C_::BN + q * 16), x);
+                        tmem_ld_wait();
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int n = n0 + j;
-                            if (n < p.N) v[j] = ldexpf(v[j], e_row + p.col_exp[n]);
+                        for (int j = 0; j < 16; ++j) {
+                            const float v = __uint_as_float(r[j]) + __uint_as_float(x[j]) * (1.0f / 2048.0f);
+                            sum[q * 16 + j] += v;
+                        }
+                    } else {
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const float v = __uint_as_float(r[j]);
+                            sum[q * 16 + j] += v;
                         }
                     }
-                    if (p.C64) {
-                        double* crow = p.C64 + (size_t)m * p.ldc64;
+                }
+                tc_fence_before();
+                mbar_arrive(&ctl->tmem_empty[b]);
+            }
+            if (!ok) break;
+            const int m = mb * kBM + row_in_tile;
+            if (m < p.M) {
+                const int n0 = nb * C_::BN + col0;
+                if (FP16) {
+                    const int e_row = p.row_exp[m];
 #pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (n0 + j < p.N) crow[n0 + j] = (double)v[j];
+                    for (int j = 0; j < C_::HALF; ++j) {
+                        const int n = n0 + j;
+                        if (n < p.N) sum[j] = ldexpf(sum[j], e_row + p.col_exp[n]);
+                    }
+                }
+                if (p.C64) {
+                    double* crow = p.C64 + (size_t)m * p.ldc64;
+#pragma unroll
+                    for (int j = 0; j < C_::HALF; ++j)
+                        if (n0 + j < p.N) crow[n0 + j] = (double)sum[j];
+                } else {
+                    float* crow = p.C + (size_t)m * p.ldc;
+                    const bool vec = (n0 + C_::HALF <= p.N) && ((p.ldc & 3) == 0) &&
+                                     ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
+                    if (vec) {
+                        float4* c4 = reinterpret_cast<float4*>(crow + n0);
+#pragma unroll
+                        for (int j = 0; j < C_::HALF / 4; ++j)
+                            c4[j] = make_float4(sum[4 * j], sum[4 * j + 1], sum[4 * j + 2], sum[4 * j + 3]);
                     } else {
-                        float* crow = p.C + (size_t)m * p.ldc;
-                        const bool vec = (n0 + 32 <= p.N) && ((p.ldc & 3) == 0) &&
-                                         ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
-                        if (vec) {
-                            float4* c4 = reinterpret_cast<float4*>(crow + n0);
 #pragma unroll
-                            for (int j = 0; j < 8; ++j)
-                                c4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (n0 + j < p.N) crow[n0 + j] = v[j];
-                        }
+                        for (int j = 0; j < C_::HALF; ++j)
+                            if (n0 + j < p.N) crow[n0 + j] = sum[j];
                     }
                 }
             }
-            tc_fence_before();
-            mbar_arrive(&ctl->tmem_empty[b]);
         }
     }
 

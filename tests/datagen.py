@@ -4,8 +4,8 @@
 - uniform: U[-1,1] from the same hash
 - family2: the adversarial cancellation family of bench/emu_adversarial.cpp:32-40 / bench/rho_sweep.cpp:72-82,
   A = [G|G], B = [H; -H + d*G2], d = 0.6366*sqrt(2K)/rho
-- oscillatory: A[i,k] = exp(-((k/K - i/M)^2)/0.01), B[k,j] = cos(2*pi*f_j*k/K) with frequencies f_j spread
-  so that the cancellation ratio spans roughly 1 to a few thousand
+- oscillatory: A[i,k] = exp(-((k/K - i/M)^2)/0.01), B[k,j] = cos(2*pi*f_j*k/K + phi_j) with the frequencies
+  set per case so that the cancellation ratio spans about 1.2 to 3000
 - wide_range: N(0,1) * 2^e with e uniform in [-20, 20] per element (full FP32 exponent-range stress)
 All values are computed in float32 with numpy; the FP64 ground truth is always taken from the same arrays.
 """
@@ -77,15 +77,17 @@ def family2(M: int, N: int, K: int, rho: float) -> tuple[np.ndarray, np.ndarray]
     return np.ascontiguousarray(A, np.float32), np.ascontiguousarray(B, np.float32)
 
 
-def oscillatory(M: int, N: int, K: int, fmax: float, seed: int = 977) -> tuple[np.ndarray, np.ndarray]:
+def oscillatory(M: int, N: int, K: int, f0: float, seed: int = 977) -> tuple[np.ndarray, np.ndarray]:
     """A[i,k] = exp(-((k/K - i/M)^2)/0.01): Gaussian bumps sliding along K; B[k,j] = cos(2 pi f_j k / K + phi_j)
-    with f_j log-spaced in [0, fmax]: the inner product of a smooth bump with a fast oscillation nearly
-    vanishes, so the cancellation ratio grows with f_j."""
+    with f_j = f0 + u_j, u_j ~ U[0,1) per column and a random phase. The inner product of a bump with a fast
+    oscillation nearly vanishes, so the cancellation ratio grows with f0 (measured in FP64 at 512x512x8192:
+    f0 = 1.3 -> rho ~ 1.2, f0 = 11 -> ~30, f0 = 1150 -> ~3000; the bumps truncated at the ends of [0,1) make
+    it grow linearly in f0)."""
     i = np.arange(M, dtype=np.float64)[:, None] / M
     k = np.arange(K, dtype=np.float64)[None, :] / K
     A = np.exp(-((k - i) ** 2) / 0.01).astype(np.float32)
     u = _unif(np.arange(N, dtype=np.uint64), seed).astype(np.float64)
-    f = np.floor(np.expm1(u * np.log1p(fmax)))
+    f = f0 + u
     ph = 2 * np.pi * _unif(np.arange(N, dtype=np.uint64), seed + 1).astype(np.float64)
     kk = np.arange(K, dtype=np.float64)[:, None]
     B = np.cos(2 * np.pi * f[None, :] * kk / K + ph[None, :]).astype(np.float32)

@@ -1,0 +1,227 @@
+"""The accuracy contract on the benchmark configurations, through emugemm_sgemm.
+
+Contract (bench/emu_adversarial.cpp:76-77, bench/emugemm_test.cpp:116): the measured normwise error
+||C - R||_F / ||R||_F against an FP64 ground truth is <= the requested max_rel_err unless the plan's reason
+says TARGET UNREACHABLE. The stricter rule checked as well: measured error <= plan.predicted_err.
+
+Configurations (seeded synthetic data; the reference harness generators restated in tests/datagen.py):
+  C1  1024^3, U[-1,1], target 1e-5, AUTO and forced BF16X3 (split/reassembly checked on the host)
+  C2  M=N=K in {4096, 8192, 16384}, N(0,1)*2^e with e ~ U{-20..20}, forced BF16X3 and FP16X3 (scaled)
+  C3  M=N=256, K in {65536, 262144}, U[-1,1]: FP32_CHUNKED c in {1,4,16}, BF16X3, NATIVE; AUTO at 1e-6/1e-7
+  C4  2048 x 2048 x 8192 cancellation: family 2 (rho ~1e2..1.1e6) and oscillatory, rho measured (hint -1)
+Ground truth: FP64 GEMM on the device (cuBLAS DGEMM through torch), cross-checked on sampled rows by the
+oracle's host FP64 GEMM. With EMUGEMM_CONTRACT_LOG=<path>, every case is appended as a JSON line.
+"""
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+import pytest
+
+import datagen
+import emugemm
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+LOG = os.environ.get("EMUGEMM_CONTRACT_LOG")
+
+
+def record(**kw):
+    if LOG:
+        with open(LOG, "a") as f:
+            f.write(json.dumps(kw) + "\n")
+
+
+def truth(torch, dA, dB, A=None, B=None, sample_rows=16):
+    R = (dA.double() @ dB.double())
+    if A is not None:
+        rows = np.linspace(0, A.shape[0] - 1, sample_rows).astype(int)
+        Rs = oracle.gemm_f64(A[rows], B)
+        Rd = R[torch.from_numpy(rows).cuda()].cpu().numpy()
+        assert np.linalg.norm(Rs - Rd) <= 1e-12 * np.linalg.norm(Rd)
+    return R
+
+
+def rel(torch, C, R):
+    return ((C.double() - R).norm() / R.norm()).item()
+
+
+def check(p, err, tgt, **info):
+    unreachable = b"UNREACHABLE" in p.reason
+    ok_ref = err <= tgt or unreachable
+    ok_pred = err <= p.predicted_err
+    record(chosen=emugemm.SCHEME_NAMES[p.chosen], chunks=p.chunks, predicted=p.predicted_err, measured=err,
+           target=tgt, reason=p.reason.decode(), ok_ref=ok_ref, ok_pred=ok_pred, **info)
+    assert ok_ref, f"contract broken: err {err:.3e} > target {tgt:.0e} ({p.as_dict()})"
+    assert ok_pred, f"err {err:.3e} above predicted {p.predicted_err:.3e} ({p.as_dict()})"
+
+
+# ------------------------------------------------------------------------------------------------- C1
+@pytest.mark.parametrize("force", [emugemm.AUTO, emugemm.BF16X3])
+@pytest.mark.parametrize("model", ["b200", "ref_mi250"])
+def test_c1_1024(cuda, handle, force, model):
+    torch = cuda
+    emugemm.set_model(model)
+    try:
+        M = N = K = 1024
+        A = datagen.uniform((M, K), 12345)
+        B = datagen.uniform((K, N), 67890)
+        dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+        dC = torch.empty((M, N), device="cuda")
+        p, hn = handle.sgemm(M, N, K, dA, dB, dC, max_rel_err=1e-5, force=force,
+                             hints=emugemm.EmuHints(-1, -1, 0, -1.0, 64))
+        handle.sync()
+        R = oracle.gemm_f64(A, B)         # host FP64 GEMM of the same inputs
+        C = dC.cpu().numpy()
+        err = oracle.rel_err(C, R)
+        if p.chosen == emugemm.BF16X3:
+            # split and reassembly on the host: the exact slice-product value
+            d = np.linalg.norm(C - oracle.slice_product(A, B, 0)) / np.linalg.norm(R)
+            assert d < 1e-6
+        check(p, err, 1e-5, config="C1", model=model, M=M, N=N, K=K, rho=hn.rho)
+    finally:
+        emugemm.set_model("b200")
+
+
+# ------------------------------------------------------------------------------------------------- C2
+@pytest.mark.parametrize("S", [4096, 8192, 16384])
+@pytest.mark.parametrize("force", [emugemm.BF16X3, emugemm.FP16X3, emugemm.AUTO])
+def test_c2_square_wide_range(cuda, handle, S, force):
+    torch = cuda
+    g = torch.Generator(device="cuda").manual_seed(S)
+    dA = torch.ldexp(torch.randn(S, S, device="cuda", generator=g),
+                     torch.randint(-20, 21, (S, S), device="cuda", generator=g).float())
+    dB = torch.ldexp(torch.randn(S, S, device="cuda", generator=g),
+                     torch.randint(-20, 21, (S, S), device="cuda", generator=g).float())
+    dC = torch.empty((S, S), device="cuda")
+    p, hn = handle.sgemm(S, S, S, dA, dB, dC, max_rel_err=1e-5, force=force)
+    handle.sync()
+    rows = torch.arange(0, S, S // 64, device="cuda")
+    Rs = dA[rows].double() @ dB.double()
+    err_rows = rel(torch, dC[rows], Rs)
+    # host cross-check of the device FP64 truth on a few rows
+    hr = np.arange(0, S, S // 4)
+    Rh = oracle.gemm_f64(dA[torch.from_numpy(hr).cuda()].cpu().numpy(), dB.cpu().numpy())
+    Rd = (dA[torch.from_numpy(hr).cuda()].double() @ dB.double()).cpu().numpy()
+    assert np.linalg.norm(Rh - Rd) <= 1e-12 * np.linalg.norm(Rd)
+    R = dA.double() @ dB.double()
+    err = rel(torch, dC, R)
+    del R
+    assert np.isfinite(err)
+    check(p, err, 1e-5, config="C2", M=S, N=S, K=S, err_sampled_rows=err_rows, a_absmax=hn.a_absmax)
+
+
+# ------------------------------------------------------------------------------------------------- C3
+@pytest.fixture(scope="module")
+def c3_data(cuda):
+    torch = cuda
+    out = {}
+    for K in (65536, 262144):
+        A = datagen.uniform((256, K), 101 + K)
+        B = datagen.uniform((K, 256), 202 + K)
+        dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+        out[K] = (A, B, dA, dB, dA.double() @ dB.double())
+    return out
+
+
+@pytest.mark.parametrize("K", [65536, 262144])
+@pytest.mark.parametrize("chunks", [1, 4, 16])
+def test_c3_chunked(cuda, handle, c3_data, K, chunks):
+    torch = cuda
+    A, B, dA, dB, R = c3_data[K]
+    P64 = torch.empty((256, 256), dtype=torch.float64, device="cuda")
+    handle.partial_f64(256, 256, K, dA, K, dB, 256, P64, emugemm.FP32_CHUNKED, chunks)
+    C = torch.empty((256, 256), device="cuda")
+    handle.reduce_f64(256, 256, 1, P64, C)
+    handle.sync()
+    err = rel(torch, C, R)
+    pred = emugemm.lib().emugemm_model_err(emugemm.FP32_CHUNKED, K, chunks)
+    record(config="C3", K=K, chunks=chunks, scheme="FP32_CHUNKED", measured=err, predicted=pred)
+    assert err <= pred
+
+
+def test_c3_k_over_c_law(cuda, handle, c3_data):
+    torch = cuda
+    errs = {}
+    for K, c in ((65536, 1), (262144, 4), (65536, 4), (262144, 16)):
+        A, B, dA, dB, R = c3_data[K]
+        P64 = torch.empty((256, 256), dtype=torch.float64, device="cuda")
+        handle.partial_f64(256, 256, K, dA, K, dB, 256, P64, emugemm.FP32_CHUNKED, c)
+        C = torch.empty((256, 256), device="cuda")
+        handle.reduce_f64(256, 256, 1, P64, C)
+        handle.sync()
+        errs[(K, c)] = rel(torch, C, R)
+    record(config="C3-law", errs={f"{k[0]}/{k[1]}": v for k, v in errs.items()})
+    assert errs[(262144, 4)] == pytest.approx(errs[(65536, 1)], rel=0.15)
+    assert errs[(262144, 16)] == pytest.approx(errs[(65536, 4)], rel=0.15)
+
+
+@pytest.mark.parametrize("K", [65536, 262144])
+@pytest.mark.parametrize("force", [emugemm.BF16X3, emugemm.NATIVE_FP32])
+def test_c3_forced(cuda, handle, c3_data, K, force):
+    torch = cuda
+    A, B, dA, dB, R = c3_data[K]
+    C = torch.empty((256, 256), device="cuda")
+    p, _ = handle.sgemm(256, 256, K, dA, dB, C, max_rel_err=1e-5, force=force)
+    handle.sync()
+    check(p, rel(torch, C, R), 1e5, config="C3", K=K)
+
+
+@pytest.mark.parametrize("K", [65536, 262144])
+@pytest.mark.parametrize("tgt", [1e-6, 1e-7])
+def test_c3_auto_below_floor(cuda, handle, c3_data, K, tgt):
+    torch = cuda
+    A, B, dA, dB, R = c3_data[K]
+    C = torch.empty((256, 256), device="cuda")
+    p, hn = handle.sgemm(256, 256, K, dA, dB, C, max_rel_err=tgt,
+                         hints=emugemm.EmuHints(-1, -1, 0, -1.0, 64))
+    handle.sync()
+    assert p.chosen == emugemm.FP32_CHUNKED
+    assert p.chunks > 1
+    check(p, rel(torch, C, R), tgt, config="C3", K=K, rho=hn.rho)
+
+
+# ------------------------------------------------------------------------------------------------- C4
+@pytest.fixture(scope="module")
+def fam2(cuda):
+    torch = cuda
+    out = {}
+    for rho in (1e2, 1e4, 1.1e6):
+        A, B = datagen.family2(2048, 2048, 8192, rho)
+        dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+        R = dA.double() @ dB.double()
+        absAB = dA.double().abs() @ dB.double().abs()
+        rho_true = (absAB.norm() / R.norm()).item()
+        del absAB
+        out[rho] = (dA, dB, R, rho_true)
+    return out
+
+
+@pytest.mark.parametrize("rho", [1e2, 1e4, 1.1e6])
+@pytest.mark.parametrize("tgt", [1e-5, 1e-4])
+def test_c4_family2(cuda, handle, fam2, rho, tgt):
+    torch = cuda
+    dA, dB, R, rho_true = fam2[rho]
+    C = torch.empty((2048, 2048), device="cuda")
+    p, hn = handle.sgemm(2048, 2048, 8192, dA, dB, C, max_rel_err=tgt,
+                         hints=emugemm.EmuHints(-1, -1, 0, -1.0, 64))
+    handle.sync()
+    check(p, rel(torch, C, R), tgt, config="C4-family2", rho_target=rho, rho_true=rho_true, rho_hat=hn.rho)
+
+
+@pytest.mark.parametrize("f0", [1.3, 11.0, 1150.0])
+@pytest.mark.parametrize("tgt", [1e-5, 1e-4])
+def test_c4_oscillatory(cuda, handle, f0, tgt):
+    torch = cuda
+    A, B = datagen.oscillatory(2048, 2048, 8192, f0)
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    R = dA.double() @ dB.double()
+    rho_true = ((dA.double().abs() @ dB.double().abs()).norm() / R.norm()).item()
+    C = torch.empty((2048, 2048), device="cuda")
+    p, hn = handle.sgemm(2048, 2048, 8192, dA, dB, C, max_rel_err=tgt,
+                         hints=emugemm.EmuHints(-1, -1, 0, -1.0, 64))
+    handle.sync()
+    check(p, rel(torch, C, R), tgt, config="C4-oscillatory", f0=f0, rho_true=rho_true, rho_hat=hn.rho)
