@@ -35,7 +35,7 @@ SCHEMES = {"bf16x3": 3, "fp16x3": 4, "native": 1}
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--size", type=int, default=8192)
@@ -56,7 +56,8 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms by a reader thread; only samples that arrive
+    between mark_start() and mark_end() (the timed region) are summarised."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -65,30 +66,51 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.lines = []
+        self.t0 = self.t1 = None
 
     def __enter__(self):
+        import threading
+
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+
+        def reader():
+            for line in self.proc.stdout:
+                self.lines.append((time.time(), line))
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+        deadline = time.time() + 5.0
+        while not self.lines and time.time() < deadline:   # wait for the first sample
+            time.sleep(0.05)
         return self
 
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
     def __exit__(self, *exc):
-        self.out = ""
         if self.proc:
             self.proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                self.out, _ = self.proc.communicate()
 
     def summary(self) -> dict:
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in (self.out or "").splitlines():
+        for t, line in self.lines:
+            if self.t0 is not None and not (self.t0 <= t <= (self.t1 or t)):
+                continue
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
@@ -230,11 +252,13 @@ def ours(args) -> None:
     h.profile_begin()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        clk.mark_start()
         ev0.record(stream)
         for _ in range(args.steps):
             step()
         ev1.record(stream)
         torch.cuda.synchronize()
+        clk.mark_end()
     prof = h.profile_end()
     launches = emugemm.launch_count() - launches0
     ms_total = ev0.elapsed_time(ev1)

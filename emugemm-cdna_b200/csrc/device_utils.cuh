@@ -148,17 +148,17 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Shared-memory matrix descriptor for a K-major operand tile stored with the 128-byte swizzle: rows of
-// 64 16-bit elements (128 B), 8-row atoms of 1024 B placed back to back (stride byte offset 1024 B).
-// The tile must start on a 1024-byte boundary; advancing along K inside the atom adds k*2 bytes to the
-// start address.
-__device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t smem_addr) {
+// Shared-memory matrix descriptor for a K-major operand tile stored with the TMA swizzle of its row width:
+// rows of `swz` bytes (128: 64 16-bit elements, 64: 32 elements), 8-row atoms of 8*swz bytes placed back to
+// back (stride byte offset 8*swz). The tile must start on an atom boundary aligned to 1024 B; advancing along
+// K inside a row adds k*2 bytes to the start address.
+__device__ __forceinline__ uint64_t sdesc_kmajor(uint32_t smem_addr, int swz) {
     uint64_t d = 0;
     d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);          // start address, bits [0,14)
     d |= (uint64_t)(1u) << 16;                              // leading byte offset (unused for swizzled K-major)
-    d |= (uint64_t)(1024u >> 4) << 32;                      // stride byte offset, bits [32,46)
+    d |= (uint64_t)((8u * (uint32_t)swz) >> 4) << 32;       // stride byte offset, bits [32,46)
     d |= (uint64_t)1u << 46;                                // descriptor version for sm_100
-    d |= (uint64_t)2u << 61;                                // layout: 128-byte swizzle
+    d |= (uint64_t)(swz == 128 ? 2u : swz == 64 ? 4u : 6u) << 61;   // layout: 128/64/32-byte swizzle
     return d;
 }
 

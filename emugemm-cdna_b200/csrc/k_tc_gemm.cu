@@ -40,13 +40,17 @@ namespace {
 using namespace dev;
 
 constexpr int kBM = 128;
-constexpr int kBK = 64;              // 64 16-bit elements = one 128-byte swizzle row
+#ifndef EMUGEMM_TC_BK
+#define EMUGEMM_TC_BK 64
+#endif
+constexpr int kBK = EMUGEMM_TC_BK;   // k-block: 64 (rows of 128 B, 128-byte swizzle) or 32 (64-byte swizzle)
+constexpr int kSwizzleBytes = kBK * 2;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-#ifndef EMUGEMM_CHUNK_KB
-#define EMUGEMM_CHUNK_KB 2
+#ifndef EMUGEMM_CHUNK_K
+#define EMUGEMM_CHUNK_K 128
 #endif
-constexpr int kChunkKB = EMUGEMM_CHUNK_KB;   // k-blocks accumulated in TMEM before promotion (2 = 128 of K)
+constexpr int kChunkKB = EMUGEMM_CHUNK_K / kBK;   // k-blocks accumulated in TMEM before promotion
 constexpr int kGroupM = 16;          // tile raster: groups of 16 row blocks sweep all column blocks
 
 template <bool FP16>
@@ -55,7 +59,7 @@ struct Cfg {
     static constexpr int A_BYTES = kBM * kBK * 2;
     static constexpr int B_BYTES = BN * kBK * 2;
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-    static constexpr int STAGES = FP16 ? 3 : 2;
+    static constexpr int STAGES = (196608 / STAGE_BYTES) < 6 ? (196608 / STAGE_BYTES) : 6;
     static constexpr int ACC_COLS = FP16 ? 2 * BN : BN;    // TMEM columns per accumulator buffer
     static constexpr int HALF = BN / 2;                     // columns per epilogue thread
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*control*/;
@@ -63,8 +67,8 @@ struct Cfg {
 };
 
 struct Ctl {
-    uint64_t full[4];
-    uint64_t empty[4];
+    uint64_t full[8];
+    uint64_t empty[8];
     uint64_t tmem_full[2];
     uint64_t tmem_empty[2];
     uint64_t drain;
@@ -189,10 +193,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (!mbar_wait(&ctl->full[s], ph, abort, p.err, kErrTimeoutMma)) { ok = false; break; }
                         tc_fence_after();
                         const uint32_t st = smem_u32(smem + s * C_::STAGE_BYTES);
-                        const uint64_t a_hi = sdesc_kmajor_sw128(st);
-                        const uint64_t a_lo = sdesc_kmajor_sw128(st + C_::A_BYTES);
-                        const uint64_t b_hi = sdesc_kmajor_sw128(st + 2 * C_::A_BYTES);
-                        const uint64_t b_lo = sdesc_kmajor_sw128(st + 2 * C_::A_BYTES + C_::B_BYTES);
+                        const uint64_t a_hi = sdesc_kmajor(st, kSwizzleBytes);
+                        const uint64_t a_lo = sdesc_kmajor(st + C_::A_BYTES, kSwizzleBytes);
+                        const uint64_t b_hi = sdesc_kmajor(st + 2 * C_::A_BYTES, kSwizzleBytes);
+                        const uint64_t b_lo = sdesc_kmajor(st + 2 * C_::A_BYTES + C_::B_BYTES, kSwizzleBytes);
 #pragma unroll
                         for (int ks = 0; ks < kBK / 16; ++ks) {
                             const uint64_t adv = (uint64_t)(ks * 32) >> 4;   // 16 elements = 32 bytes along K
@@ -318,14 +322,15 @@ bool get_encode() {
     return g_encode != nullptr;
 }
 
-// rows x Kp 16-bit matrix, K-major; box = 64 (K) x box_rows, 128-byte swizzle.
+// rows x Kp 16-bit matrix, K-major; box = kBK (K) x box_rows, swizzled by the k-block's row width.
 bool make_tmap(CUtensorMap* m, const uint16_t* base, long Kp, int rows, int box_rows) {
     cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)Kp * 2};
     cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(base), dims, strides, box,
-                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          kSwizzleBytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }

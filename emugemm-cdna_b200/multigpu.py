@@ -1,0 +1,110 @@
+"""Multi-GPU drivers of the emulated SGEMM: one process per GPU, torch.distributed (NCCL) for the plumbing,
+libemugemm for every GEMM.
+
+row_sharded   C = A*B with the rows of A (and C) split across ranks and B held by one rank. B travels in
+              column panels: rank `src` packs B[:, n0:n1] into a contiguous panel and NCCL broadcasts it; each
+              rank's GEMM of panel j (emugemm_sgemm_ex on the panel, writing C[:, n0:n1] in place) starts as
+              soon as that panel has arrived, so the broadcast of later panels overlaps the GEMMs of earlier
+              ones. No data-path collective besides the broadcast.
+k_split       C = A*B with K split across ranks: rank g holds A[:, Kg] and B[Kg, :], computes its partial product
+              in FP64 (emugemm_sgemm_partial_f64), the partials are summed with NCCL in FP64, and one final
+              rounding gives C (emugemm_reduce_f64). With bf16x3 per rank the error model sees G = world size
+              chunks summed in FP64.
+The GEMM callables are injectable so the partitioning and collective logic runs on CPU (gloo) in tests.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+
+def row_range(M: int, rank: int, world: int) -> tuple[int, int]:
+    """Rows of A owned by `rank`: contiguous blocks, the first M % world ranks one row longer."""
+    base, extra = divmod(M, world)
+    r0 = rank * base + min(rank, extra)
+    return r0, r0 + base + (1 if rank < extra else 0)
+
+
+def k_range(K: int, rank: int, world: int, align: int = 64) -> tuple[int, int]:
+    """K range of `rank` for the K-split: blocks aligned to `align` so every rank's slices are whole k-blocks."""
+    blocks = -(-K // align)
+    b0, b1 = row_range(blocks, rank, world)
+    return min(K, b0 * align), min(K, b1 * align)
+
+
+def panels(N: int, panel: int) -> list[tuple[int, int]]:
+    return [(n0, min(N, n0 + panel)) for n0 in range(0, N, panel)]
+
+
+@dataclass
+class PanelStats:
+    n_panels: int
+    bytes_broadcast: int
+
+
+def _emugemm_ex(handle, scheme: int):
+    import emugemm
+
+    def gemm(M, N, K, A, lda, B, ldb, C, ldc):
+        handle.sgemm_ex(M, N, K, A, lda, B, ldb, C, ldc, force=scheme,
+                        hints=emugemm.EmuHints(1.0, 1.0, 0, 0.0, 0))
+    return gemm
+
+
+def row_sharded(A_local: torch.Tensor, B: torch.Tensor, C_local: torch.Tensor, *, src: int = 0,
+                panel: int = 2048, gemm: Callable | None = None, handle=None, scheme: int = 3,
+                keep_b: bool = False, group=None) -> PanelStats:
+    """C_local = A_local * B with B broadcast from `src` in column panels.
+
+    A_local: (m x K) rows of A owned by this rank; B: (K x N), valid on `src` (on other ranks it is only written
+    when keep_b is set); C_local: (m x N). `gemm(M, N, K, A, lda, B, ldb, C, ldc)` computes one panel into the
+    column block of C_local (default: emugemm_sgemm_ex with `scheme` on `handle`)."""
+    if gemm is None:
+        gemm = _emugemm_ex(handle, scheme)
+    rank = dist.get_rank(group)
+    m, K = A_local.shape
+    N = B.shape[1]
+    plist = panels(N, panel)
+    bufs = []
+    works = []
+    for (n0, n1) in plist:
+        buf = B[:, n0:n1].contiguous() if rank == src else torch.empty((K, n1 - n0), dtype=B.dtype,
+                                                                       device=B.device)
+        bufs.append(buf)
+        works.append(dist.broadcast(buf, src=src, group=group, async_op=True))
+    for (n0, n1), buf, w in zip(plist, bufs, works):
+        w.wait()      # the compute stream waits for this panel; later broadcasts keep going
+        if m > 0:
+            gemm(m, n1 - n0, K, A_local, K, buf, n1 - n0, C_local[:, n0:n1], N)
+        if keep_b and rank != src:
+            B[:, n0:n1].copy_(buf)
+    return PanelStats(len(plist), sum(b.numel() * b.element_size() for b in bufs))
+
+
+def k_split(A_local: torch.Tensor, B_local: torch.Tensor, C: torch.Tensor | None, *, M: int, N: int,
+            partial: Callable | None = None, reduce: Callable | None = None, handle=None, scheme: int = 3,
+            chunks: int = 1, all_ranks: bool = False, group=None) -> torch.Tensor:
+    """C = sum over ranks of A_local * B_local, partials in FP64 summed by NCCL, one rounding to FP32.
+
+    A_local: (M x Kg), B_local: (Kg x N). Returns the FP64 sum (valid on rank 0, or on all ranks with
+    all_ranks=True); C (M x N, FP32) is written on the ranks where the sum is valid."""
+    if partial is None:
+        def partial(M_, N_, K_, A_, B_, P_):
+            handle.partial_f64(M_, N_, K_, A_, K_, B_, N_, P_, scheme, chunks)
+    if reduce is None:
+        def reduce(M_, N_, P_, C_):
+            handle.reduce_f64(M_, N_, 1, P_, C_)
+    Kg = A_local.shape[1]
+    P = torch.zeros((M, N), dtype=torch.float64, device=A_local.device)
+    if Kg > 0:
+        partial(M, N, Kg, A_local, B_local, P)
+    if all_ranks:
+        dist.all_reduce(P, op=dist.ReduceOp.SUM, group=group)
+    else:
+        dist.reduce(P, dst=0, op=dist.ReduceOp.SUM, group=group)
+    if (all_ranks or dist.get_rank(group) == 0) and C is not None:
+        reduce(M, N, P, C)
+    return P

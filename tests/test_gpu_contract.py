@@ -172,16 +172,25 @@ def test_c3_forced(cuda, handle, c3_data, K, force):
 
 @pytest.mark.parametrize("K", [65536, 262144])
 @pytest.mark.parametrize("tgt", [1e-6, 1e-7])
-def test_c3_auto_below_floor(cuda, handle, c3_data, K, tgt):
+@pytest.mark.parametrize("model", ["ref_mi250", "b200"])
+def test_c3_auto_below_floor(cuda, handle, c3_data, K, tgt, model):
+    """Targets below the bf16x3 floor never get bf16x3. With the reference constants they route to FP32_CHUNKED
+    (or TARGET UNREACHABLE, which still computes chunked); with the B200 constants the scaled fp16x3 is also a
+    legal answer where its model error meets the target."""
     torch = cuda
     A, B, dA, dB, R = c3_data[K]
     C = torch.empty((256, 256), device="cuda")
-    p, hn = handle.sgemm(256, 256, K, dA, dB, C, max_rel_err=tgt,
-                         hints=emugemm.EmuHints(-1, -1, 0, -1.0, 64))
-    handle.sync()
-    assert p.chosen == emugemm.FP32_CHUNKED
-    assert p.chunks > 1
-    check(p, rel(torch, C, R), tgt, config="C3", K=K, rho=hn.rho)
+    emugemm.set_model(model)
+    try:
+        p, hn = handle.sgemm(256, 256, K, dA, dB, C, max_rel_err=tgt,
+                             hints=emugemm.EmuHints(-1, -1, 0, -1.0, 64))
+        handle.sync()
+    finally:
+        emugemm.set_model("b200")
+    assert p.chosen != emugemm.BF16X3
+    if model == "ref_mi250":
+        assert p.chosen == emugemm.FP32_CHUNKED and p.chunks > 1
+    check(p, rel(torch, C, R), tgt, config="C3", model=model, K=K, rho=hn.rho)
 
 
 # ------------------------------------------------------------------------------------------------- C4
