@@ -189,6 +189,19 @@ emugemm_status_t emugemm_profile_begin(emugemm_handle_t handle);
 emugemm_status_t emugemm_profile_end(emugemm_handle_t handle, double* ms_by_kind, int* count_by_kind,
                                      int nkinds);
 
+/* bf16x3 emulated SGEMM that allocates nothing (no counterpart in the emugemm-cdna API). For callers that
+   cannot let a library call cudaMalloc -- plugins inside an application whose own pool has reserved the
+   device's memory, latency-critical paths that must not risk an allocation mid-run -- it computes the same
+   product as emugemm_sgemm with force_scheme = EMU_SCHEME_BF16X3, with the slices of A and B held in a fixed
+   64 MiB device array that every GPU loading the library keeps until the process exits. Limit:
+   (Mp + Np) * Kp <= 16 Mi with Mp, Np, Kp = M, N, K rounded up to 128, 256, 64 (e.g. M = N = 2048, K <= 4096);
+   larger sizes return EMUGEMM_STATUS_INVALID_SIZE. All calls on a device share the array: calls that overlap
+   on the GPU race, so order them (e.g. one stream). The first call on a device looks the array up with
+   cudaGetSymbolAddress; make that first call before any stream capture. Row-major, device pointers,
+   asynchronous on `stream` (a cudaStream_t; NULL = legacy default stream), current device must be sm_100. */
+emugemm_status_t emugemm_sgemm_bf16x3_noalloc(int M, int N, long K, const float* A, const float* B, float* C,
+                                              void* stream);
+
 /* Number of kernels this library launched since the process started (all handles). */
 unsigned long long emugemm_kernel_launch_count(void);
 
