@@ -157,9 +157,11 @@ static void prof_clear(Handle* h) {
 
 static long round_up(long x, long m) { return (x + m - 1) / m * m; }
 
-// bf16x3 / fp16x3 through the tensor-core kernel over pre-split slices.
+// bf16x3 / fp16x3 through the tensor-core kernel over pre-split slices. With a_reused (hints->a_is_reused) and
+// the same A (pointer, shape, leading dimension, scheme) as the split already held in the workspace, A is not
+// split again: the caller has declared A unchanged since that call.
 static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, long lda, const float* B, long ldb,
-                               float* C, long ldc, double* C64, long ldc64, bool fp16) {
+                               float* C, long ldc, double* C64, long ldc64, bool fp16, bool a_reused) {
     const int BN = tc_gemm_bn(fp16 ? 1 : 0);
     const long Mp = round_up(M, 128), Np = round_up(N, BN), Kp = round_up(K, 64);
     if (Mp > 0x7fffffffL || Np > 0x7fffffffL || Kp > 0x7fffffffL) return EMUGEMM_STATUS_INVALID_SIZE;
@@ -174,18 +176,32 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
         rexp = (int*)ws_get(h, kWsScaleA, (size_t)M * 4);
         cexp = (int*)ws_get(h, kWsScaleB, (size_t)N * 8);
         if (!rexp || !cexp) return EMUGEMM_STATUS_MEMORY_ERROR;
+    }
+    const int kind = fp16 ? 1 : 0;
+    Handle::ASplitKey key;
+    key.A = A; key.M = M; key.K = K; key.lda = lda; key.kind = kind; key.Mp = Mp; key.Kp = Kp;
+    key.ws0 = a0; key.ws1 = a1; key.rexp = rexp;
+    const Handle::ASplitKey& k0 = h->a_key;
+    const bool reuse = a_reused && k0.A == key.A && k0.M == key.M && k0.K == key.K && k0.lda == key.lda &&
+                       k0.kind == key.kind && k0.Mp == key.Mp && k0.Kp == key.Kp && k0.ws0 == key.ws0 &&
+                       k0.ws1 == key.ws1 && k0.rexp == key.rexp;
+    int e = 0;
+    if (fp16) {
         ProfScope ps(h, kProfScan);
-        int e = launch_row_exponents(A, M, K, lda, rexp, h->stream);
+        if (!reuse) e = launch_row_exponents(A, M, K, lda, rexp, h->stream);
         if (!e) e = launch_col_exponents(B, K, N, ldb, cexp, reinterpret_cast<unsigned*>(cexp + N), h->stream);
         if (e) return from_cuda(e);
     }
-    int e;
     {
         ProfScope ps(h, kProfSplit);
-        e = launch_split_rows(A, M, K, lda, (int)Mp, Kp, fp16 ? 1 : 0, rexp, a0, a1, h->stream);
-        if (!e) e = launch_split_cols(B, K, N, ldb, (int)Np, Kp, fp16 ? 1 : 0, cexp, b0, b1, h->stream);
+        if (!reuse) {
+            h->a_key = Handle::ASplitKey();   // invalid until the split below has been enqueued
+            e = launch_split_rows(A, M, K, lda, (int)Mp, Kp, kind, rexp, a0, a1, h->stream);
+        }
+        if (!e) e = launch_split_cols(B, K, N, ldb, (int)Np, Kp, kind, cexp, b0, b1, h->stream);
     }
     if (e) return from_cuda(e);
+    h->a_key = key;
     TcGemmArgs t;
     t.a_hi = a0; t.a_lo = a1; t.b_hi = b0; t.b_lo = b1;
     t.M = M; t.N = N; t.Mp = (int)Mp; t.Np = (int)Np; t.Kp = Kp;
@@ -228,7 +244,8 @@ static emugemm_status_t zero_out(Handle* h, int M, int N, float* C, long ldc, do
 }
 
 static emugemm_status_t dispatch(Handle* h, emu_scheme_t s, int chunks, int M, int N, long K, const float* A,
-                                 long lda, const float* B, long ldb, float* C, long ldc, double* C64, long ldc64) {
+                                 long lda, const float* B, long ldb, float* C, long ldc, double* C64, long ldc64,
+                                 bool a_reused = false) {
     if (M == 0 || N == 0) return EMUGEMM_STATUS_SUCCESS;
     if (K == 0) return zero_out(h, M, N, C, ldc, C64, ldc64);
     switch (s) {
@@ -236,8 +253,8 @@ static emugemm_status_t dispatch(Handle* h, emu_scheme_t s, int chunks, int M, i
         case EMU_SCHEME_FP32_CHUNKED: return run_fp32(h, M, N, K, A, lda, B, ldb, C, ldc, C64, ldc64, chunks);
         // A forced BF16X6 runs the bf16x3 kernel, as the reference does (src/emugemm.cpp:331).
         case EMU_SCHEME_BF16X3:
-        case EMU_SCHEME_BF16X6: return run_tc(h, M, N, K, A, lda, B, ldb, C, ldc, C64, ldc64, false);
-        case EMU_SCHEME_FP16X3: return run_tc(h, M, N, K, A, lda, B, ldb, C, ldc, C64, ldc64, true);
+        case EMU_SCHEME_BF16X6: return run_tc(h, M, N, K, A, lda, B, ldb, C, ldc, C64, ldc64, false, a_reused);
+        case EMU_SCHEME_FP16X3: return run_tc(h, M, N, K, A, lda, B, ldb, C, ldc, C64, ldc64, true, a_reused);
         default: return EMUGEMM_STATUS_NOT_IMPLEMENTED;
     }
 }
@@ -351,7 +368,8 @@ emugemm_status_t emugemm_sgemm_ex(emugemm_handle_t handle, int M, int N, long K,
     }
     emu_plan_t plan = emu::plan(emu::model(), M, N, K, req, &local);
     if (out_plan) *out_plan = plan;
-    return emu::dispatch(h, plan.chosen, plan.chunks, M, N, K, A, lda, B, ldb, C, ldc, nullptr, 0);
+    return emu::dispatch(h, plan.chosen, plan.chunks, M, N, K, A, lda, B, ldb, C, ldc, nullptr, 0,
+                         hints && hints->a_is_reused);
 }
 
 emugemm_status_t emugemm_sgemm(emugemm_handle_t handle, int M, int N, long K, const float* A, const float* B,

@@ -90,6 +90,12 @@ struct Handle {
     bool profiling = false;
     ProfRec* prof = nullptr;        // growable array of event pairs
     int prof_n = 0, prof_cap = 0;
+    // Identity of the A operand whose slices (and fp16 row exponents) the split workspace currently holds, so
+    // a call with hints->a_is_reused can skip re-splitting an unchanged A (src/emugemm.h:53 of emugemm-cdna).
+    struct ASplitKey {
+        const float* A = nullptr; int M = 0; long K = 0, lda = 0; int kind = -1; long Mp = 0, Kp = 0;
+        const void* ws0 = nullptr; const void* ws1 = nullptr; const void* rexp = nullptr;
+    } a_key;
 };
 
 // Profiler scope: records an event before and after the launches inside it when the handle profiles.

@@ -182,9 +182,10 @@ __global__ void __launch_bounds__(256) k_split_cols(const float* __restrict__ B,
         t[kk][tx] = (k < K && n < N) ? __ldg(B + (size_t)k * ldb + n) : 0.f;
     }
     __syncthreads();
-    // 64 columns x 8 groups of 8 k = 512 items, 2 per thread.
+    // 64 columns x 8 groups of 8 k = 512 items, 2 per thread. Eight consecutive lanes take the eight k-groups
+    // of one output row, so each warp store fills four whole 128-byte lines.
     for (int item = threadIdx.x; item < 512; item += 256) {
-        const int nn = item & 63, kg = item >> 6;
+        const int kg = item & 7, nn = item >> 3;
         const int n = n0 + nn;
         if (n >= Np) continue;
         int e = 0;

@@ -46,11 +46,17 @@ class PanelStats:
 
 
 def _emugemm_ex(handle, scheme: int):
+    """Panel GEMM through emugemm_sgemm_ex. The first panel splits A; later panels pass a_is_reused so the
+    library keeps A's slices instead of splitting the same rows again."""
     import emugemm
 
+    calls = [0]
+
     def gemm(M, N, K, A, lda, B, ldb, C, ldc):
+        reused = 1 if calls[0] > 0 else 0
+        calls[0] += 1
         handle.sgemm_ex(M, N, K, A, lda, B, ldb, C, ldc, force=scheme,
-                        hints=emugemm.EmuHints(1.0, 1.0, 0, 0.0, 0))
+                        hints=emugemm.EmuHints(1.0, 1.0, reused, 0.0, 0))
     return gemm
 
 

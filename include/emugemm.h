@@ -52,7 +52,8 @@ typedef struct {
 
 typedef struct {
     float  a_absmax, b_absmax;  /* < 0 means "unknown, please scan" (an O(MK+KN) pass) */
-    int    a_is_reused;         /* accepted for compatibility; no split cache is kept */
+    int    a_is_reused;         /* non-zero: A (same pointer, shape, lda) is unchanged since the previous
+                                   emulated call on this handle, so its hi/lo split is reused */
     float  rho;                 /* cancellation ratio || |A||B| ||_F / ||AB||_F; < 0 = estimate it,
                                    0 = do not estimate and plan with the iid model */
     int    rho_probes;          /* Rademacher probes of the estimate; 0 -> 64 */

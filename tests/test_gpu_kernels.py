@@ -302,3 +302,22 @@ def test_launch_counter_advances(cuda, handle):
     handle.sgemm(64, 64, 64, A, A, C, force=emugemm.BF16X3, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
     handle.sync()
     assert emugemm.launch_count() >= before + 3
+
+
+def test_a_is_reused_reuses_the_split(cuda, handle):
+    """hints.a_is_reused with an unchanged A: the second call skips A's split and gives the same bits."""
+    torch = cuda
+    A = datagen.normal((512, 768), 50)
+    B1 = datagen.normal((768, 384), 51)
+    B2 = datagen.normal((768, 384), 52)
+    dA, dB1, dB2 = dev(torch, A), dev(torch, B1), dev(torch, B2)
+    for force in (emugemm.BF16X3, emugemm.FP16X3):
+        ref = torch.empty((512, 384), device="cuda")
+        handle.sgemm(512, 384, 768, dA, dB2, ref, force=force, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+        out = torch.empty((512, 384), device="cuda")
+        handle.sgemm(512, 384, 768, dA, dB1, out, force=force, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+        handle.profile_begin()
+        handle.sgemm(512, 384, 768, dA, dB2, out, force=force, hints=emugemm.EmuHints(1, 1, 1, 0, 0))
+        prof = handle.profile_end()
+        assert torch.equal(out, ref)
+        assert prof["split"][1] == 1          # only B was split
