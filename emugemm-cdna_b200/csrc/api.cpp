@@ -10,6 +10,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -157,13 +158,24 @@ static void prof_clear(Handle* h) {
 
 static long round_up(long x, long m) { return (x + m - 1) / m * m; }
 
+// Tensor-core kernel for a shape: the tile table's code (1 = single-CTA, 2 = CTA pair) unless the environment
+// variable EMUGEMM_TC_KERNEL names one ("single" or "pair").
+static bool use_pair_kernel(int M, int N, long K, bool fp16) {
+    const char* v = std::getenv("EMUGEMM_TC_KERNEL");
+    if (v && std::strcmp(v, "pair") == 0) return true;
+    if (v && std::strcmp(v, "single") == 0) return false;
+    const int code = lookup_tile(M, N, K, fp16 ? 2 : 1).tc_variant;
+    return code == 2;
+}
+
 // bf16x3 / fp16x3 through the tensor-core kernel over pre-split slices. With a_reused (hints->a_is_reused) and
 // the same A (pointer, shape, leading dimension, scheme) as the split already held in the workspace, A is not
 // split again: the caller has declared A unchanged since that call.
 static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, long lda, const float* B, long ldb,
                                float* C, long ldc, double* C64, long ldc64, bool fp16, bool a_reused) {
-    const int BN = tc_gemm_bn(fp16 ? 1 : 0);
-    const long Mp = round_up(M, 128), Np = round_up(N, BN), Kp = round_up(K, 64);
+    const bool pair = use_pair_kernel(M, N, K, fp16);
+    const int BN = pair ? tc_pair_bn(fp16 ? 1 : 0) : tc_gemm_bn(fp16 ? 1 : 0);
+    const long Mp = round_up(M, pair ? 256 : 128), Np = round_up(N, BN), Kp = round_up(K, 64);
     if (Mp > 0x7fffffffL || Np > 0x7fffffffL || Kp > 0x7fffffffL) return EMUGEMM_STATUS_INVALID_SIZE;
     uint16_t* a0 = (uint16_t*)ws_get(h, kWsSplitA0, (size_t)Mp * Kp * 2);
     uint16_t* a1 = (uint16_t*)ws_get(h, kWsSplitA1, (size_t)Mp * Kp * 2);
@@ -211,7 +223,7 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
     t.err = h->err_dev;
     t.num_sms = h->num_sms;
     ProfScope ps(h, kProfTcGemm);
-    return from_cuda(launch_tc_gemm(t, h->stream));
+    return from_cuda(pair ? launch_tc_gemm_pair(t, h->stream) : launch_tc_gemm(t, h->stream));
 }
 
 static emugemm_status_t run_fp32(Handle* h, int M, int N, long K, const float* A, long lda, const float* B, long ldb,

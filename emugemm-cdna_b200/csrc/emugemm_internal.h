@@ -47,7 +47,7 @@ extern const char* const kReasonNative;
 // ---------------------------------------------------------------------------------------------------
 // tune.cpp: per-shape tile table
 struct TileChoice {
-    int tc_variant;     // tensor-core kernel variant: 0 = auto, 1 = fused in-smem split, 2 = pre-split
+    int tc_variant;     // tensor-core kernel: 0 = built-in choice, 1 = single-CTA, 2 = CTA pair (cta_group::2)
     int fp32_bm;        // FP32 SIMT tile edge: 0 = auto, 64 or 128
 };
 TileChoice lookup_tile(int M, int N, long K, int dtype /*0 fp32, 1 bf16, 2 fp16*/);
@@ -142,6 +142,9 @@ struct TcGemmArgs {
 };
 int launch_tc_gemm(const TcGemmArgs& a, void* stream);
 int tc_gemm_bn(int fp16);   // output tile width of the bf16x3 (0) / fp16x3 (1) kernel
+// k_tc_gemm2.cu: the same product on CTA pairs (cta_group::2); needs Mp % 256 == 0.
+int launch_tc_gemm_pair(const TcGemmArgs& a, void* stream);
+int tc_pair_bn(int fp16);
 
 // k_fp32_gemm.cu: FP32 SIMT GEMM with K-chunks summed in FP64.
 struct Fp32GemmArgs {

@@ -370,6 +370,12 @@ int launch_impl(const TcGemmArgs& a, void* stream) {
 
 }  // namespace
 
+bool tc_get_encode(PFN_cuTensorMapEncodeTiled_v12000* out) {
+    if (!get_encode()) return false;
+    *out = g_encode;
+    return true;
+}
+
 int tc_gemm_bn(int fp16) { return fp16 ? Cfg<true>::BN : Cfg<false>::BN; }
 
 int launch_tc_gemm(const TcGemmArgs& a, void* stream) {

@@ -1,0 +1,417 @@
+// k_tc_gemm2.cu - the 3-product emulated-FP32 GEMM on CTA pairs (tcgen05 cta_group::2).
+//
+// Same product, slices, promotion and epilogue as k_tc_gemm.cu (see there), but two CTAs of a cluster share one
+// 256 x BN output tile: each CTA loads 128 rows of A and BN/2 rows of the transposed B into its own shared
+// memory, the pair's leader issues tcgen05.mma.cta_group::2 (M = 256), which reads the other halves from the
+// peer, and each CTA's TMEM receives the accumulator of its own 128 rows. Per SM this halves the B operand's
+// shared-memory and L2 traffic for the same tensor work.
+//
+// Cross-CTA signalling uses explicit remote mbarrier arrivals (release at cluster scope), never a
+// multicast form:
+//   peer full[s]      -> the peer's MMA warp forwards it to the leader's peer_full[s]
+//   leader empty[s]   -> the leader's producer forwards it to the peer's empty[s] before refilling stage s
+//   leader tmem_full  -> one leader epilogue lane forwards it to the peer's tmem_full
+//   peer drains       -> every peer epilogue warp arrives on the leader's tmem_empty
+// Every wait is bounded; a CTA that gives up raises the abort flag of both CTAs, unwinds, and both meet at a
+// final cluster barrier before the pair's TMEM is freed.
+#include "device_utils.cuh"
+#include "emugemm_internal.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+namespace emu {
+
+bool tc_get_encode(PFN_cuTensorMapEncodeTiled_v12000* out);
+
+namespace {
+
+using namespace dev;
+
+constexpr int kBM = 128;             // rows per CTA (the pair covers 256)
+constexpr int kBK = 64;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kChunkKB = 128 / kBK;  // promotion every 128 values of K, as in k_tc_gemm.cu
+constexpr int kGroupM = 8;           // pair tiles: groups of 8 row blocks of 256
+
+template <bool FP16>
+struct Cfg2 {
+    static constexpr int BN = FP16 ? 128 : 256;      // pair tile width
+    static constexpr int BNH = BN / 2;               // rows of transposed B held by each CTA
+    static constexpr int A_BYTES = kBM * kBK * 2;
+    static constexpr int B_BYTES = BNH * kBK * 2;
+    static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    static constexpr int STAGES = (196608 / STAGE_BYTES) < 6 ? (196608 / STAGE_BYTES) : 6;
+    static constexpr int ACC_COLS = FP16 ? 2 * BN : BN;
+    static constexpr int HALF = BN / 2;              // columns per epilogue thread
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 512;
+    static constexpr uint32_t IDESC = idesc_f16(2 * kBM, BN, !FP16);
+};
+
+struct Ctl2 {
+    uint64_t full[8];
+    uint64_t empty[8];
+    uint64_t peer_full[8];     // leader only: the peer's stage has landed
+    uint64_t tmem_full[2];
+    uint64_t tmem_empty[2];    // leader only: 8 local + 8 peer epilogue warps
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+};
+
+struct KParams2 {
+    int M, N, num_m2, num_n, nk;   // num_m2: row blocks of 256
+    float* C; long ldc;
+    double* C64; long ldc64;
+    const int* row_exp; const int* col_exp;
+    unsigned* err;
+};
+
+__device__ __forceinline__ void tile_coords2(int t, int num_m2, int num_n, int& mb2, int& nb) {
+    const int per_group = kGroupM * num_n;
+    const int g = t / per_group;
+    const int first_m = g * kGroupM;
+    const int gm = min(num_m2 - first_m, kGroupM);
+    const int r = t - g * per_group;
+    mb2 = first_m + r % gm;
+    nb = r / gm;
+}
+
+__device__ __forceinline__ void drain_wait2(uint64_t* bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    unsigned long long t0 = globaltimer();
+    while (!mbar_try_wait(a, parity)) {
+        if (globaltimer() - t0 > 200000000ull) return;
+    }
+}
+
+// Raise the abort flag of both CTAs of the pair.
+__device__ __forceinline__ void abort_pair(Ctl2* ctl, uint32_t peer) {
+    ctl->abort = 1;
+    st_shared_cluster_u32(mapa_shared(smem_u32(&ctl->abort), peer), 1u);
+}
+
+template <bool FP16>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_tc_gemm_pair(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
+                   const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
+                   KParams2 p) {
+    using C_ = Cfg2<FP16>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Ctl2* ctl = reinterpret_cast<Ctl2*>(smem + C_::STAGES * C_::STAGE_BYTES);
+    volatile int* abort = &ctl->abort;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const uint32_t peer = rank ^ 1u;
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+    const int num_tiles = p.num_m2 * p.num_n;
+    const int nchunks = (p.nk + kChunkKB - 1) / kChunkKB;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C_::STAGES; ++s) {
+            mbar_init(&ctl->full[s], 1);
+            mbar_init(&ctl->empty[s], 1);
+            mbar_init(&ctl->peer_full[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&ctl->tmem_full[b], 1);
+            mbar_init(&ctl->tmem_empty[b], 2 * kEpiWarps);
+        }
+        mbar_init(&ctl->drain, 1);
+        ctl->abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tm_ahi);
+        prefetch_tmap(&tm_alo);
+        prefetch_tmap(&tm_bhi);
+        prefetch_tmap(&tm_blo);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(&ctl->tmem_base, 512);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();      // barriers of both CTAs initialised, TMEM of the pair allocated
+    tc_fence_after();
+    const uint32_t tmem_base = ctl->tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer (each CTA fills its own halves) ----------------
+            long it = 0;
+            bool ok = true;
+            const uint32_t peer_empty0 = mapa_shared(smem_u32(&ctl->empty[0]), peer);
+            for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+                int mb2, nb;
+                tile_coords2(t, p.num_m2, p.num_n, mb2, nb);
+                const int a_row = mb2 * 2 * kBM + (int)rank * kBM;
+                const int b_row = nb * C_::BN + (int)rank * C_::BNH;
+                for (int kb = 0; kb < p.nk; ++kb, ++it) {
+                    const int s = (int)(it % C_::STAGES);
+                    if (it >= C_::STAGES) {
+                        const uint32_t ph = (uint32_t)(((it / C_::STAGES) - 1) & 1);
+                        const bool ready = leader
+                            ? mbar_wait(&ctl->empty[s], ph, abort, p.err, kErrTimeoutProducer)
+                            : mbar_wait_cluster(&ctl->empty[s], ph, abort, p.err, kErrTimeoutProducer);
+                        if (!ready) { ok = false; break; }
+                        // the pair MMA that read stage s has completed: the peer's stage s is free too
+                        if (leader) mbar_arrive_cluster(peer_empty0 + (uint32_t)(s * sizeof(uint64_t)));
+                    }
+                    uint8_t* st = smem + s * C_::STAGE_BYTES;
+                    mbar_arrive_expect_tx(&ctl->full[s], C_::STAGE_BYTES);
+                    tma_load_2d(st, &tm_ahi, &ctl->full[s], kb * kBK, a_row);
+                    tma_load_2d(st + C_::A_BYTES, &tm_alo, &ctl->full[s], kb * kBK, a_row);
+                    tma_load_2d(st + 2 * C_::A_BYTES, &tm_bhi, &ctl->full[s], kb * kBK, b_row);
+                    tma_load_2d(st + 2 * C_::A_BYTES + C_::B_BYTES, &tm_blo, &ctl->full[s], kb * kBK, b_row);
+                }
+            }
+            if (!ok) {
+                abort_pair(ctl, peer);
+                const long first = it > C_::STAGES ? it - C_::STAGES : 0;
+                for (long j = first; j < it; ++j)
+                    drain_wait2(&ctl->full[j % C_::STAGES], (uint32_t)((j / C_::STAGES) & 1));
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            if (!leader) {
+                // ---------------- peer: forward "stage landed" to the leader ----------------
+                long it = 0;
+                bool ok = true;
+                const uint32_t lead_pf0 = mapa_shared(smem_u32(&ctl->peer_full[0]), 0);
+                for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+                    for (int kb = 0; kb < p.nk; ++kb, ++it) {
+                        const int s = (int)(it % C_::STAGES);
+                        const uint32_t ph = (uint32_t)((it / C_::STAGES) & 1);
+                        if (!mbar_wait(&ctl->full[s], ph, abort, p.err, kErrTimeoutMma)) { ok = false; break; }
+                        mbar_arrive_cluster(lead_pf0 + (uint32_t)(s * sizeof(uint64_t)));
+                    }
+                }
+                if (!ok) abort_pair(ctl, peer);
+            } else {
+                // ---------------- leader: pair MMA issuer ----------------
+                long it = 0, ch = 0;
+                bool ok = true;
+                for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+                    for (int kb0 = 0; kb0 < p.nk && ok; kb0 += kChunkKB, ++ch) {
+                        const int b = (int)(ch & 1);
+                        const uint32_t bph = (uint32_t)((ch >> 1) & 1);
+                        if (!mbar_wait_cluster(&ctl->tmem_empty[b], bph ^ 1u, abort, p.err, kErrTimeoutMma)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t d_main = tmem_base + (uint32_t)(b * C_::ACC_COLS);
+                        const uint32_t d_cross = FP16 ? d_main + (uint32_t)C_::BN : d_main;
+                        const int kb1 = min(p.nk, kb0 + kChunkKB);
+                        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                            const int s = (int)(it % C_::STAGES);
+                            const uint32_t ph = (uint32_t)((it / C_::STAGES) & 1);
+                            if (!mbar_wait(&ctl->full[s], ph, abort, p.err, kErrTimeoutMma) ||
+                                !mbar_wait_cluster(&ctl->peer_full[s], ph, abort, p.err, kErrTimeoutMma)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            const uint32_t st = smem_u32(smem + s * C_::STAGE_BYTES);
+                            const uint64_t a_hi = sdesc_kmajor(st, 128);
+                            const uint64_t a_lo = sdesc_kmajor(st + C_::A_BYTES, 128);
+                            const uint64_t b_hi = sdesc_kmajor(st + 2 * C_::A_BYTES, 128);
+                            const uint64_t b_lo = sdesc_kmajor(st + 2 * C_::A_BYTES + C_::B_BYTES, 128);
+#pragma unroll
+                            for (int ks = 0; ks < kBK / 16; ++ks) {
+                                const uint64_t adv = (uint64_t)(ks * 32) >> 4;
+                                const uint32_t acc = (kb != kb0 || ks != 0) ? 1u : 0u;
+                                mma_f16_ss_pair(d_cross, a_lo + adv, b_hi + adv, C_::IDESC, acc);
+                                mma_f16_ss_pair(d_cross, a_hi + adv, b_lo + adv, C_::IDESC, 1u);
+                                mma_f16_ss_pair(d_main, a_hi + adv, b_hi + adv, C_::IDESC, FP16 ? acc : 1u);
+                            }
+                            mma_commit_pair(&ctl->empty[s]);
+                        }
+                        if (!ok) break;
+                        mma_commit_pair(&ctl->tmem_full[b]);
+                    }
+                }
+                if (!ok) {
+                    abort_pair(ctl, peer);
+                    mma_commit_pair(&ctl->drain);
+                    drain_wait2(&ctl->drain, 0);
+                }
+            }
+        }
+    } else {
+        // ---------------- promotion + epilogue (warps 2..9 of each CTA) ----------------
+        const int sp = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int row_in_tile = (int)rank * kBM + sp * 32 + lane;
+        const int col0 = half * C_::HALF;
+        const uint32_t lane_off = (uint32_t)(sp * 32) << 16;
+        const uint32_t peer_tf0 = mapa_shared(smem_u32(&ctl->tmem_full[0]), peer);
+        const uint32_t lead_te0 = mapa_shared(smem_u32(&ctl->tmem_empty[0]), 0);
+        const bool forwarder = leader && warp == 2 && lane == 0;
+        long ch = 0;
+        bool ok = true;
+        for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+            int mb2, nb;
+            tile_coords2(t, p.num_m2, p.num_n, mb2, nb);
+            float sum[C_::HALF];
+#pragma unroll
+            for (int j = 0; j < C_::HALF; ++j) sum[j] = 0.f;
+            for (int c = 0; c < nchunks; ++c, ++ch) {
+                const int b = (int)(ch & 1);
+                const uint32_t bph = (uint32_t)((ch >> 1) & 1);
+                bool ready = leader ? mbar_wait(&ctl->tmem_full[b], bph, abort, p.err, kErrTimeoutEpilogue)
+                                    : mbar_wait_cluster(&ctl->tmem_full[b], bph, abort, p.err, kErrTimeoutEpilogue);
+                if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
+                if (forwarder) mbar_arrive_cluster(peer_tf0 + (uint32_t)(b * sizeof(uint64_t)));
+                tc_fence_after();
+                const uint32_t tb = tmem_base + lane_off + (uint32_t)(b * C_::ACC_COLS + col0);
+#pragma unroll
+                for (int q = 0; q < C_::HALF / 16; ++q) {
+                    uint32_t r[16];
+                    tmem_ld_32x32b_x16(tb + (uint32_t)(q * 16), r);
+                    if (FP16) {
+                        uint32_t x[16];
+                        tmem_ld_32x32b_x16(tb + (uint32_t)(C_::BN + q * 16), x);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            sum[q * 16 + j] += __uint_as_float(r[j]) + __uint_as_float(x[j]) * (1.0f / 2048.0f);
+                    } else {
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) sum[q * 16 + j] += __uint_as_float(r[j]);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(lead_te0 + (uint32_t)(b * sizeof(uint64_t)));
+            }
+            if (!ok) break;
+            const int m = mb2 * 2 * kBM + row_in_tile;
+            if (m < p.M) {
+                const int n0 = nb * C_::BN + col0;
+                if (FP16) {
+                    const int e_row = p.row_exp[m];
+#pragma unroll
+                    for (int j = 0; j < C_::HALF; ++j) {
+                        const int n = n0 + j;
+                        if (n < p.N) sum[j] = ldexpf(sum[j], e_row + p.col_exp[n]);
+                    }
+                }
+                if (p.C64) {
+                    double* crow = p.C64 + (size_t)m * p.ldc64;
+#pragma unroll
+                    for (int j = 0; j < C_::HALF; ++j)
+                        if (n0 + j < p.N) crow[n0 + j] = (double)sum[j];
+                } else {
+                    float* crow = p.C + (size_t)m * p.ldc;
+                    const bool vec = (n0 + C_::HALF <= p.N) && ((p.ldc & 3) == 0) &&
+                                     ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
+                    if (vec) {
+                        float4* c4 = reinterpret_cast<float4*>(crow + n0);
+#pragma unroll
+                        for (int j = 0; j < C_::HALF / 4; ++j)
+                            c4[j] = make_float4(sum[4 * j], sum[4 * j + 1], sum[4 * j + 2], sum[4 * j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < C_::HALF; ++j)
+                            if (n0 + j < p.N) crow[n0 + j] = sum[j];
+                    }
+                }
+            }
+        }
+        if (!ok && lane == 0) abort_pair(ctl, peer);
+    }
+
+    tc_fence_before();
+    cluster_sync_all();      // both CTAs finished: no remote arrival or MMA is still in flight
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, 512);
+    }
+}
+
+bool make_tmap2(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* m, const uint16_t* base, long Kp, int rows,
+                int box_rows) {
+    cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)Kp * 2};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool FP16>
+int launch_pair_impl(const TcGemmArgs& a, void* stream) {
+    using C_ = Cfg2<FP16>;
+    PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+    if (!tc_get_encode(&enc)) return (int)cudaErrorNotSupported;
+    if (a.Mp % (2 * kBM) || a.Np % C_::BN || a.Kp % kBK || a.Kp <= 0) return (int)cudaErrorInvalidValue;
+    CUtensorMap tah, tal, tbh, tbl;
+    if (!make_tmap2(enc, &tah, a.a_hi, a.Kp, a.Mp, kBM) || !make_tmap2(enc, &tal, a.a_lo, a.Kp, a.Mp, kBM) ||
+        !make_tmap2(enc, &tbh, a.b_hi, a.Kp, a.Np, C_::BNH) || !make_tmap2(enc, &tbl, a.b_lo, a.Kp, a.Np, C_::BNH))
+        return (int)cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(k_tc_gemm_pair<FP16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C_::SMEM_BYTES);
+    if (e != cudaSuccess) return (int)e;
+    KParams2 p;
+    p.M = a.M;
+    p.N = a.N;
+    p.num_m2 = a.Mp / (2 * kBM);
+    p.num_n = a.Np / C_::BN;
+    p.nk = (int)(a.Kp / kBK);
+    p.C = a.C;
+    p.ldc = a.ldc;
+    p.C64 = a.C64;
+    p.ldc64 = a.ldc64;
+    p.row_exp = a.row_exp;
+    p.col_exp = a.col_exp;
+    p.err = a.err;
+    const int tiles = p.num_m2 * p.num_n;
+
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C_::SMEM_BYTES;
+    cfg.stream = (cudaStream_t)stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    cfg.gridDim = dim3(2, 1, 1);
+    e = cudaOccupancyMaxActiveClusters(&clusters, k_tc_gemm_pair<FP16>, &cfg);
+    if (e != cudaSuccess || clusters <= 0) {
+        cudaGetLastError();
+        clusters = (a.num_sms > 0 ? a.num_sms : 148) / 2;
+    }
+    if (clusters > tiles) clusters = tiles;
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    e = cudaLaunchKernelEx(&cfg, k_tc_gemm_pair<FP16>, tah, tal, tbh, tbl, p);
+    count_launch();
+    if (e != cudaSuccess) return (int)e;
+    return (int)cudaGetLastError();
+}
+
+}  // namespace
+
+int tc_pair_bn(int fp16) { return fp16 ? Cfg2<true>::BN : Cfg2<false>::BN; }
+
+int launch_tc_gemm_pair(const TcGemmArgs& a, void* stream) {
+    return a.fp16 ? launch_pair_impl<true>(a, stream) : launch_pair_impl<false>(a, stream);
+}
+
+}  // namespace emu

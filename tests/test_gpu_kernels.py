@@ -321,3 +321,21 @@ def test_a_is_reused_reuses_the_split(cuda, handle):
         prof = handle.profile_end()
         assert torch.equal(out, ref)
         assert prof["split"][1] == 1          # only B was split
+
+
+@pytest.mark.parametrize("force", [emugemm.BF16X3, emugemm.FP16X3])
+@pytest.mark.parametrize("shape", [(256, 256, 128), (300, 520, 1000), (1024, 768, 2048), (1, 1, 1), (2048, 2048, 512)])
+def test_pair_kernel_matches_single_cta_kernel(cuda, handle, monkeypatch, force, shape):
+    """The CTA-pair kernel (cta_group::2) computes every output from the same slices and k-steps as the
+    single-CTA kernel: identical bits."""
+    torch = cuda
+    M, N, K = shape
+    A = datagen.normal((M, K), 60 + M)
+    B = datagen.normal((K, N), 61 + N)
+    out = {}
+    for variant in ("single", "pair"):
+        monkeypatch.setenv("EMUGEMM_TC_KERNEL", variant)
+        C, p, _ = run_sgemm(torch, handle, A, B, force=force, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+        out[variant] = C
+    assert np.isfinite(out["pair"]).all()
+    assert np.array_equal(out["pair"], out["single"])
