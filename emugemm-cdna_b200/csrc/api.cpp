@@ -158,14 +158,19 @@ static void prof_clear(Handle* h) {
 
 static long round_up(long x, long m) { return (x + m - 1) / m * m; }
 
-// Tensor-core kernel for a shape: the tile table's code (1 = single-CTA, 2 = CTA pair) unless the environment
-// variable EMUGEMM_TC_KERNEL names one ("single" or "pair").
-static bool use_pair_kernel(int M, int N, long K, bool fp16) {
+// Tensor-core kernel for a shape: the environment variable EMUGEMM_TC_KERNEL ("single" or "pair") if set, else
+// the tile table's code (1 = single-CTA, 2 = CTA pair), else the built-in choice: CTA pairs for bf16x3 when
+// the 256 x 256 pair tiles fill every pair of SMs at least once (measured at 8192^3: 2.34 ms against 2.43 ms
+// single-CTA), single-CTA 128-row tiles otherwise and for fp16x3 (3.24 ms against 3.40 ms for pairs).
+static bool use_pair_kernel(Handle* h, int M, int N, long K, bool fp16) {
     const char* v = std::getenv("EMUGEMM_TC_KERNEL");
     if (v && std::strcmp(v, "pair") == 0) return true;
     if (v && std::strcmp(v, "single") == 0) return false;
     const int code = lookup_tile(M, N, K, fp16 ? 2 : 1).tc_variant;
-    return code == 2;
+    if (code) return code == 2;
+    if (fp16) return false;
+    const long pair_tiles = ((M + 255) / 256) * (long)((N + 255) / 256);
+    return pair_tiles >= (h->num_sms > 0 ? h->num_sms : 148) / 2;
 }
 
 // bf16x3 / fp16x3 through the tensor-core kernel over pre-split slices. With a_reused (hints->a_is_reused) and
@@ -173,7 +178,7 @@ static bool use_pair_kernel(int M, int N, long K, bool fp16) {
 // split again: the caller has declared A unchanged since that call.
 static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, long lda, const float* B, long ldb,
                                float* C, long ldc, double* C64, long ldc64, bool fp16, bool a_reused) {
-    const bool pair = use_pair_kernel(M, N, K, fp16);
+    const bool pair = use_pair_kernel(h, M, N, K, fp16);
     const int BN = pair ? tc_pair_bn(fp16 ? 1 : 0) : tc_gemm_bn(fp16 ? 1 : 0);
     const long Mp = round_up(M, pair ? 256 : 128), Np = round_up(N, BN), Kp = round_up(K, 64);
     if (Mp > 0x7fffffffL || Np > 0x7fffffffL || Kp > 0x7fffffffL) return EMUGEMM_STATUS_INVALID_SIZE;

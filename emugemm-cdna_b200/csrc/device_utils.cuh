@@ -1,5 +1,5 @@
 // device_utils.cuh - sm_100a PTX wrappers used by the tensor-core kernels: mbarriers with bounded waits,
-// TMA tile loads (no cluster multicast anywhere), tcgen05 TMEM allocation, MMA, commit and loads.
+// TMA tile loads (each into the issuing CTA only), tcgen05 TMEM allocation, MMA, commit and loads.
 #pragma once
 
 #include <cstdint>
@@ -200,6 +200,24 @@ __device__ __forceinline__ void mma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc
 __device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
+}
+// Arrive on the barrier at the same shared-memory offset as `bar` in every CTA of `cta_mask` (a tcgen05.commit,
+// not a copy) once all pair MMAs issued so far by this thread have completed.
+__device__ __forceinline__ void mma_commit_pair_both(uint64_t* bar, uint16_t cta_mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(cta_mask)
+        : "memory");
+}
+// 2-D TMA tile load into this CTA's shared memory that completes on the pair leader's barrier (`leader_bar` is
+// that barrier's shared::cluster address), so the leader sees both halves of a stage on one barrier.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* tmap, uint32_t leader_bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+        "[%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(tmap), "r"(leader_bar), "r"(x), "r"(y)
+        : "memory");
 }
 
 // Arrive on `bar` once all previously issued tcgen05 operations of this thread have completed.

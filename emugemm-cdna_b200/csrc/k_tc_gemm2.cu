@@ -6,12 +6,12 @@
 // peer, and each CTA's TMEM receives the accumulator of its own 128 rows. Per SM this halves the B operand's
 // shared-memory and L2 traffic for the same tensor work.
 //
-// Cross-CTA signalling uses explicit remote mbarrier arrivals (release at cluster scope), never a
-// multicast form:
-//   peer full[s]      -> the peer's MMA warp forwards it to the leader's peer_full[s]
-//   leader empty[s]   -> the leader's producer forwards it to the peer's empty[s] before refilling stage s
-//   leader tmem_full  -> one leader epilogue lane forwards it to the peer's tmem_full
-//   peer drains       -> every peer epilogue warp arrives on the leader's tmem_empty
+// Cross-CTA signalling:
+//   both CTAs' TMA loads of a stage complete on the LEADER's full barrier (TMA .cta_group::2 form, each
+//   load writing only its own CTA), which the leader armed with the bytes of both halves;
+//   the leader's commits after a stage / a chunk arrive on the empty / tmem_full barriers of BOTH CTAs
+//   (tcgen05.commit to the CTA mask 0b11);
+//   every epilogue warp of both CTAs arrives on the leader's tmem_empty once it has drained a chunk.
 // Every wait is bounded; a CTA that gives up raises the abort flag of both CTAs, unwinds, and both meet at a
 // final cluster barrier before the pair's TMEM is freed.
 #include "device_utils.cuh"
@@ -55,7 +55,6 @@ struct Cfg2 {
 struct Ctl2 {
     uint64_t full[8];
     uint64_t empty[8];
-    uint64_t peer_full[8];     // leader only: the peer's stage has landed
     uint64_t tmem_full[2];
     uint64_t tmem_empty[2];    // leader only: 8 local + 8 peer epilogue warps
     uint64_t drain;
@@ -119,7 +118,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < C_::STAGES; ++s) {
             mbar_init(&ctl->full[s], 1);
             mbar_init(&ctl->empty[s], 1);
-            mbar_init(&ctl->peer_full[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&ctl->tmem_full[b], 1);
@@ -146,10 +144,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            // ---------------- TMA producer (each CTA fills its own halves) ----------------
+            // ---------------- TMA producer: each CTA fills its own halves, completing on the leader ----------------
             long it = 0;
             bool ok = true;
-            const uint32_t peer_empty0 = mapa_shared(smem_u32(&ctl->empty[0]), peer);
+            const uint32_t lead_full0 = mapa_shared(smem_u32(&ctl->full[0]), 0);
             for (int t = pair; t < num_tiles && ok; t += num_pairs) {
                 int mb2, nb;
                 tile_coords2(t, p.num_m2, p.num_n, mb2, nb);
@@ -157,95 +155,79 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int b_row = nb * C_::BN + (int)rank * C_::BNH;
                 for (int kb = 0; kb < p.nk; ++kb, ++it) {
                     const int s = (int)(it % C_::STAGES);
-                    if (it >= C_::STAGES) {
-                        const uint32_t ph = (uint32_t)(((it / C_::STAGES) - 1) & 1);
-                        const bool ready = leader
-                            ? mbar_wait(&ctl->empty[s], ph, abort, p.err, kErrTimeoutProducer)
-                            : mbar_wait_cluster(&ctl->empty[s], ph, abort, p.err, kErrTimeoutProducer);
-                        if (!ready) { ok = false; break; }
-                        // the pair MMA that read stage s has completed: the peer's stage s is free too
-                        if (leader) mbar_arrive_cluster(peer_empty0 + (uint32_t)(s * sizeof(uint64_t)));
+                    const uint32_t ph = (uint32_t)((it / C_::STAGES) & 1);
+                    // empty[s] of both CTAs is signalled by the leader's commit once the pair MMA read stage s
+                    if (!mbar_wait_cluster(&ctl->empty[s], ph ^ 1u, abort, p.err, kErrTimeoutProducer)) {
+                        ok = false;
+                        break;
                     }
+                    if (leader) mbar_arrive_expect_tx(&ctl->full[s], 2 * C_::STAGE_BYTES);
+                    const uint32_t fb = lead_full0 + (uint32_t)(s * sizeof(uint64_t));
                     uint8_t* st = smem + s * C_::STAGE_BYTES;
-                    mbar_arrive_expect_tx(&ctl->full[s], C_::STAGE_BYTES);
-                    tma_load_2d(st, &tm_ahi, &ctl->full[s], kb * kBK, a_row);
-                    tma_load_2d(st + C_::A_BYTES, &tm_alo, &ctl->full[s], kb * kBK, a_row);
-                    tma_load_2d(st + 2 * C_::A_BYTES, &tm_bhi, &ctl->full[s], kb * kBK, b_row);
-                    tma_load_2d(st + 2 * C_::A_BYTES + C_::B_BYTES, &tm_blo, &ctl->full[s], kb * kBK, b_row);
+                    tma_load_2d_pair(st, &tm_ahi, fb, kb * kBK, a_row);
+                    tma_load_2d_pair(st + C_::A_BYTES, &tm_alo, fb, kb * kBK, a_row);
+                    tma_load_2d_pair(st + 2 * C_::A_BYTES, &tm_bhi, fb, kb * kBK, b_row);
+                    tma_load_2d_pair(st + 2 * C_::A_BYTES + C_::B_BYTES, &tm_blo, fb, kb * kBK, b_row);
                 }
             }
             if (!ok) {
                 abort_pair(ctl, peer);
-                const long first = it > C_::STAGES ? it - C_::STAGES : 0;
-                for (long j = first; j < it; ++j)
-                    drain_wait2(&ctl->full[j % C_::STAGES], (uint32_t)((j / C_::STAGES) & 1));
+                // the leader's full barriers count both CTAs' loads: let those in flight land
+                if (leader) {
+                    const long first = it > C_::STAGES ? it - C_::STAGES : 0;
+                    for (long j = first; j < it; ++j)
+                        drain_wait2(&ctl->full[j % C_::STAGES], (uint32_t)((j / C_::STAGES) & 1));
+                }
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            if (!leader) {
-                // ---------------- peer: forward "stage landed" to the leader ----------------
-                long it = 0;
-                bool ok = true;
-                const uint32_t lead_pf0 = mapa_shared(smem_u32(&ctl->peer_full[0]), 0);
-                for (int t = pair; t < num_tiles && ok; t += num_pairs) {
-                    for (int kb = 0; kb < p.nk; ++kb, ++it) {
+        if (lane == 0 && leader) {
+            // ---------------- leader: pair MMA issuer ----------------
+            long it = 0, ch = 0;
+            bool ok = true;
+            for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+                for (int kb0 = 0; kb0 < p.nk && ok; kb0 += kChunkKB, ++ch) {
+                    const int b = (int)(ch & 1);
+                    const uint32_t bph = (uint32_t)((ch >> 1) & 1);
+                    if (!mbar_wait_cluster(&ctl->tmem_empty[b], bph ^ 1u, abort, p.err, kErrTimeoutMma)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d_main = tmem_base + (uint32_t)(b * C_::ACC_COLS);
+                    const uint32_t d_cross = FP16 ? d_main + (uint32_t)C_::BN : d_main;
+                    const int kb1 = min(p.nk, kb0 + kChunkKB);
+                    for (int kb = kb0; kb < kb1; ++kb, ++it) {
                         const int s = (int)(it % C_::STAGES);
                         const uint32_t ph = (uint32_t)((it / C_::STAGES) & 1);
-                        if (!mbar_wait(&ctl->full[s], ph, abort, p.err, kErrTimeoutMma)) { ok = false; break; }
-                        mbar_arrive_cluster(lead_pf0 + (uint32_t)(s * sizeof(uint64_t)));
-                    }
-                }
-                if (!ok) abort_pair(ctl, peer);
-            } else {
-                // ---------------- leader: pair MMA issuer ----------------
-                long it = 0, ch = 0;
-                bool ok = true;
-                for (int t = pair; t < num_tiles && ok; t += num_pairs) {
-                    for (int kb0 = 0; kb0 < p.nk && ok; kb0 += kChunkKB, ++ch) {
-                        const int b = (int)(ch & 1);
-                        const uint32_t bph = (uint32_t)((ch >> 1) & 1);
-                        if (!mbar_wait_cluster(&ctl->tmem_empty[b], bph ^ 1u, abort, p.err, kErrTimeoutMma)) {
+                        if (!mbar_wait_cluster(&ctl->full[s], ph, abort, p.err, kErrTimeoutMma)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        const uint32_t d_main = tmem_base + (uint32_t)(b * C_::ACC_COLS);
-                        const uint32_t d_cross = FP16 ? d_main + (uint32_t)C_::BN : d_main;
-                        const int kb1 = min(p.nk, kb0 + kChunkKB);
-                        for (int kb = kb0; kb < kb1; ++kb, ++it) {
-                            const int s = (int)(it % C_::STAGES);
-                            const uint32_t ph = (uint32_t)((it / C_::STAGES) & 1);
-                            if (!mbar_wait(&ctl->full[s], ph, abort, p.err, kErrTimeoutMma) ||
-                                !mbar_wait_cluster(&ctl->peer_full[s], ph, abort, p.err, kErrTimeoutMma)) {
-                                ok = false;
-                                break;
-                            }
-                            tc_fence_after();
-                            const uint32_t st = smem_u32(smem + s * C_::STAGE_BYTES);
-                            const uint64_t a_hi = sdesc_kmajor(st, 128);
-                            const uint64_t a_lo = sdesc_kmajor(st + C_::A_BYTES, 128);
-                            const uint64_t b_hi = sdesc_kmajor(st + 2 * C_::A_BYTES, 128);
-                            const uint64_t b_lo = sdesc_kmajor(st + 2 * C_::A_BYTES + C_::B_BYTES, 128);
+                        const uint32_t st = smem_u32(smem + s * C_::STAGE_BYTES);
+                        const uint64_t a_hi = sdesc_kmajor(st, 128);
+                        const uint64_t a_lo = sdesc_kmajor(st + C_::A_BYTES, 128);
+                        const uint64_t b_hi = sdesc_kmajor(st + 2 * C_::A_BYTES, 128);
+                        const uint64_t b_lo = sdesc_kmajor(st + 2 * C_::A_BYTES + C_::B_BYTES, 128);
 #pragma unroll
-                            for (int ks = 0; ks < kBK / 16; ++ks) {
-                                const uint64_t adv = (uint64_t)(ks * 32) >> 4;
-                                const uint32_t acc = (kb != kb0 || ks != 0) ? 1u : 0u;
-                                mma_f16_ss_pair(d_cross, a_lo + adv, b_hi + adv, C_::IDESC, acc);
-                                mma_f16_ss_pair(d_cross, a_hi + adv, b_lo + adv, C_::IDESC, 1u);
-                                mma_f16_ss_pair(d_main, a_hi + adv, b_hi + adv, C_::IDESC, FP16 ? acc : 1u);
-                            }
-                            mma_commit_pair(&ctl->empty[s]);
+                        for (int ks = 0; ks < kBK / 16; ++ks) {
+                            const uint64_t adv = (uint64_t)(ks * 32) >> 4;
+                            const uint32_t acc = (kb != kb0 || ks != 0) ? 1u : 0u;
+                            mma_f16_ss_pair(d_cross, a_lo + adv, b_hi + adv, C_::IDESC, acc);
+                            mma_f16_ss_pair(d_cross, a_hi + adv, b_lo + adv, C_::IDESC, 1u);
+                            mma_f16_ss_pair(d_main, a_hi + adv, b_hi + adv, C_::IDESC, FP16 ? acc : 1u);
                         }
-                        if (!ok) break;
-                        mma_commit_pair(&ctl->tmem_full[b]);
+                        mma_commit_pair_both(&ctl->empty[s], (uint16_t)0x3);
                     }
+                    if (!ok) break;
+                    mma_commit_pair_both(&ctl->tmem_full[b], (uint16_t)0x3);
                 }
-                if (!ok) {
-                    abort_pair(ctl, peer);
-                    mma_commit_pair(&ctl->drain);
-                    drain_wait2(&ctl->drain, 0);
-                }
+            }
+            if (!ok) {
+                abort_pair(ctl, peer);
+                mma_commit_pair(&ctl->drain);
+                drain_wait2(&ctl->drain, 0);
             }
         }
     } else {
@@ -255,9 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row_in_tile = (int)rank * kBM + sp * 32 + lane;
         const int col0 = half * C_::HALF;
         const uint32_t lane_off = (uint32_t)(sp * 32) << 16;
-        const uint32_t peer_tf0 = mapa_shared(smem_u32(&ctl->tmem_full[0]), peer);
         const uint32_t lead_te0 = mapa_shared(smem_u32(&ctl->tmem_empty[0]), 0);
-        const bool forwarder = leader && warp == 2 && lane == 0;
         long ch = 0;
         bool ok = true;
         for (int t = pair; t < num_tiles && ok; t += num_pairs) {
@@ -269,10 +249,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = 0; c < nchunks; ++c, ++ch) {
                 const int b = (int)(ch & 1);
                 const uint32_t bph = (uint32_t)((ch >> 1) & 1);
-                bool ready = leader ? mbar_wait(&ctl->tmem_full[b], bph, abort, p.err, kErrTimeoutEpilogue)
-                                    : mbar_wait_cluster(&ctl->tmem_full[b], bph, abort, p.err, kErrTimeoutEpilogue);
+                bool ready = mbar_wait_cluster(&ctl->tmem_full[b], bph, abort, p.err, kErrTimeoutEpilogue);
                 if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
-                if (forwarder) mbar_arrive_cluster(peer_tf0 + (uint32_t)(b * sizeof(uint64_t)));
                 tc_fence_after();
                 const uint32_t tb = tmem_base + lane_off + (uint32_t)(b * C_::ACC_COLS + col0);
 #pragma unroll

@@ -1,0 +1,123 @@
+"""Per-shape kernel tuner: writes the tile table that emugemm_init loads (the B200 counterpart of emugemm-cdna's
+bench/gen_tune_table.cpp: offline, resumable, shardable, header written once under an exclusive lock).
+
+For every (M, N, K, dtype) of the grid it times the candidate kernels through the C ABI and appends one row
+    arch,cuda_version,M,N,K,dtype,tile,best_ms,default_ms,gain
+where `tile` is the winner (bf16/fp16: 1 = single-CTA, 2 = CTA pair; fp32: SIMT tile edge 64 or 128),
+`default_ms` the built-in choice's time and `gain` = default_ms / best_ms. Rows already present for a key are
+skipped, so an interrupted run resumes; --shard i/n takes every n-th shape starting at i (one process per GPU).
+
+    python emugemm-cdna_b200/tune_tiles.py tiles_b200.csv [--shard 0/8] [--quick]
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import fcntl
+import itertools
+import os
+import pathlib
+import sys
+
+import torch
+
+HERE = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+import emugemm  # noqa: E402
+
+HEADER = "arch,cuda_version,M,N,K,dtype,tile,best_ms,default_ms,gain\n"
+DTYPES = {"bf16": emugemm.BF16X3, "fp16": emugemm.FP16X3, "fp32": emugemm.NATIVE_FP32}
+
+
+def existing_keys(path: pathlib.Path) -> set:
+    keys = set()
+    if path.exists():
+        with path.open() as f:
+            for row in csv.reader(f):
+                if len(row) == 10 and row[0] != "arch":
+                    keys.add((int(row[2]), int(row[3]), int(row[4]), row[5]))
+    return keys
+
+
+def append_row(path: pathlib.Path, row: str) -> None:
+    with path.open("a") as f:
+        fcntl.flock(f, fcntl.LOCK_EX)
+        if f.tell() == 0:
+            f.write(HEADER)
+        f.write(row)
+        f.flush()
+        fcntl.flock(f, fcntl.LOCK_UN)
+
+
+def time_call(h, fn, reps: int) -> float:
+    fn()
+    h.sync()
+    h.profile_begin()
+    for _ in range(reps):
+        fn()
+    p = h.profile_end()
+    tot = sum(v[0] for v in p.values() if v[1])
+    return tot / reps
+
+
+def tune_shape(h, M, N, K, dtype, reps):
+    A = torch.randn(M, K, device="cuda")
+    B = torch.randn(K, N, device="cuda")
+    C = torch.empty(M, N, device="cuda")
+    scheme = DTYPES[dtype]
+    hints = emugemm.EmuHints(1.0, 1.0, 0, 0.0, 0)
+    res = {}
+    if dtype == "fp32":
+        # the SIMT tile edge comes from the table only, so time both by loading a one-row table per candidate
+        for tile in (128, 64):
+            tmp = pathlib.Path(f"/tmp/emugemm_tile_{os.getpid()}.csv")
+            tmp.write_text(HEADER + f"{arch()},probe,{M},{N},{K},fp32,{tile},0,0,1\n")
+            emugemm.lib().emugemm_init(str(tmp).encode())
+            res[tile] = time_call(h, lambda: h.sgemm(M, N, K, A, B, C, force=scheme, hints=hints), reps)
+            tmp.unlink()
+        emugemm.lib().emugemm_shutdown()
+        default = 128 if ((M + 127) // 128) * ((N + 127) // 128) >= torch.cuda.get_device_properties(0).multi_processor_count else 64
+    else:
+        for tile, name in ((1, "single"), (2, "pair")):
+            os.environ["EMUGEMM_TC_KERNEL"] = name
+            res[tile] = time_call(h, lambda: h.sgemm(M, N, K, A, B, C, force=scheme, hints=hints), reps)
+        os.environ.pop("EMUGEMM_TC_KERNEL", None)
+        default = 1
+    best = min(res, key=res.get)
+    return best, res[best], res[default]
+
+
+def arch() -> str:
+    major, minor = torch.cuda.get_device_capability(0)
+    return f"sm_{major}{minor}" + ("a" if (major, minor) == (10, 0) else "")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("table")
+    ap.add_argument("--shard", default="0/1")
+    ap.add_argument("--quick", action="store_true")
+    ap.add_argument("--reps", type=int, default=5)
+    args = ap.parse_args()
+    i, n = (int(x) for x in args.shard.split("/"))
+    torch.cuda.set_device(0)
+    if args.quick:
+        grid = list(itertools.product((2048, 8192), (2048, 8192), (2048, 8192), ("bf16", "fp16")))
+    else:
+        sizes = (1024, 2048, 4096, 8192, 16384)
+        grid = list(itertools.product(sizes, sizes, (1024, 4096, 16384, 65536), ("bf16", "fp16", "fp32")))
+        grid = [g for g in grid if g[0] * g[1] * g[2] <= 8192 ** 3 * 4]
+    path = pathlib.Path(args.table)
+    done = existing_keys(path)
+    with emugemm.Handle() as h:
+        for j, (M, N, K, dt) in enumerate(grid):
+            if j % n != i or (M, N, K, dt) in done:
+                continue
+            best, best_ms, def_ms = tune_shape(h, M, N, K, dt, args.reps)
+            append_row(path, f"{arch()},{torch.version.cuda},{M},{N},{K},{dt},{best},{best_ms:.5f},{def_ms:.5f},"
+                             f"{def_ms / best_ms:.4f}\n")
+            print(M, N, K, dt, best, f"{best_ms:.4f}", f"{def_ms:.4f}", flush=True)
+
+
+if __name__ == "__main__":
+    main()
