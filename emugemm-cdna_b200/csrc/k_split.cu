@@ -176,11 +176,16 @@ __global__ void __launch_bounds__(256) k_split_cols(const float* __restrict__ B,
     const int n0 = blockIdx.x * 64;
     const long k0 = (long)blockIdx.y * 64;
     const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;   // 64 x 4
-    for (int kk = ty; kk < 64; kk += 4) {
-        const long k = k0 + kk;
+    // all 16 loads of a thread are issued before any is stored, so 16 are in flight at once
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const long k = k0 + ty + 4 * i;
         const int n = n0 + tx;
-        t[kk][tx] = (k < K && n < N) ? __ldg(B + (size_t)k * ldb + n) : 0.f;
+        v[i] = (k < K && n < N) ? __ldg(B + (size_t)k * ldb + n) : 0.f;
     }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) t[ty + 4 * i][tx] = v[i];
     __syncthreads();
     // 64 columns x 8 groups of 8 k = 512 items, 2 per thread. Eight consecutive lanes take the eight k-groups
     // of one output row, so each warp store fills four whole 128-byte lines.

@@ -18,9 +18,9 @@ namespace emu {
 // Chunk-cost envelope of the reference (src/emugemm.cpp:29-36): a step function of c.
 static const ChunkStep kRefChunkSteps[] = {{1, 1.00}, {4, 1.05}, {16, 1.95}, {64, 1.35}, {256, 1.85}};
 
-// B200 chunk cost of the FP32 kernel here: the chunk loop stays inside one kernel and only adds an FP64
-// accumulate per chunk, so the cost is flat until chunks become shorter than a few k-blocks.
-static const ChunkStep kB200ChunkSteps[] = {{1, 1.00}, {4, 1.00}, {16, 1.00}, {64, 1.02}, {256, 1.10}};
+// B200 chunk cost of the FP32 kernel here (4096 x 4096 x 65536, time at c / time at c = 1): the chunk loop stays
+// inside one kernel and only adds an FP64 accumulate per chunk: 1.006 (c=4), 1.032 (16), 1.120 (64), 1.468 (256).
+static const ChunkStep kB200ChunkSteps[] = {{1, 1.00}, {4, 1.01}, {16, 1.04}, {64, 1.13}, {256, 1.48}};
 
 static const ModelConsts kRefMI250 = {
     "ref_mi250",
@@ -36,26 +36,28 @@ static const ModelConsts kRefMI250 = {
     /*rho_factor_min*/ 0.0,
 };
 
-// B200 constants, fitted to this library's kernels on B200 against an FP64 ground truth (M = N = 256 or
-// 512, K = 256 ... 262144, N(0,1), U[-1,1] and bf16-exact inputs), each with a few percent of margin:
-//   a_fp32   FP32 SIMT chains measured at 1.80e-8 * sqrt(K/c) on U[-1,1] (1.78e-8 on N(0,1))
-//   bf16x3   error flat in K at 4.43-4.47e-6 on N(0,1) (3.9e-6 on U[-1,1]): the split's representation floor
-//            plus the truncation of 128-long tensor-core partial sums; the FP32 running sum adds ~1.1e-9 sqrt(K)
-//   fp16x3   3.5e-7 at short K growing as ~1.2e-9 sqrt(K) (6.7e-7 at K = 262144)
+// B200 constants, fitted by emugemm-cdna_b200/calibrate.py to this library's kernels on B200 against an FP64
+// ground truth (M = N = 256, K = 1024 ... 262144, N(0,1) and U[-1,1] data), each with margin:
+//   a_fp32   FP32 SIMT chains: err / sqrt(K/c) measured up to 1.96e-8
+//   bf16x3   error flat in K at 4.43-4.53e-6: the split's representation floor (4.4355e-6) plus the truncation
+//            of 128-long tensor-core partial sums; the FP32 running sum adds ~2e-9 sqrt(K)
+//   fp16x3   2.1e-7 at short K growing as ~1.6e-9 sqrt(K) (8.4e-7 at K = 262144)
 //   bf16x6   runs the bf16x3 kernel (as a forced BF16X6 does in the reference), so it gets bf16x3's numbers
-// Speed ratios are against this library's FP32 SIMT kernel, the NATIVE_FP32 path. fp16x3 scales each row of
-// A and column of B by a power of two before splitting, so its range test only excludes zero/non-finite.
+// Speed ratios: 8192^3 kernel time of the FP32 SIMT kernel (the NATIVE_FP32 path, 44.5 TFLOPS) over that of
+// the tensor-core kernel (bf16x3 11.7x, fp16x3 6.7x), rounded down; hbm_bps is the split's effective rate.
+// fp16x3 scales each row of A and column of B by a power of two before splitting, so its range test only
+// excludes zero and non-finite magnitudes.
 static const ModelConsts kB200 = {
     "b200",
-    /*a_fp32*/ 1.85e-8, /*a_lowp*/ 1.2e-9, /*a_fp16x3*/ 1.3e-9,
-    /*floor_bf16x3*/ 4.55e-6, /*floor_fp16x3*/ 3.7e-7, /*floor_bf16x6*/ 4.55e-6,
-    /*spd_bf16x3*/ 7.0, /*spd_fp16x3*/ 6.5, /*spd_bf16x6*/ 7.0,
+    /*a_fp32*/ 2.02e-8, /*a_lowp*/ 3.0e-9, /*a_fp16x3*/ 1.7e-9,
+    /*floor_bf16x3*/ 4.6e-6, /*floor_fp16x3*/ 2.6e-7, /*floor_bf16x6*/ 4.6e-6,
+    /*spd_bf16x3*/ 10.0, /*spd_fp16x3*/ 6.0, /*spd_bf16x6*/ 10.0,
     /*fp16_max*/ INFINITY, /*fp16_min*/ 0.0f,
-    kB200ChunkSteps, 5, /*chunk_cost_beyond*/ 1.5,
+    kB200ChunkSteps, 5, /*chunk_cost_beyond*/ 2.0,
     /*max_chunks*/ 256,
-    /*hbm_bps*/ 5.0e12, /*fp32_flops*/ 55.0e12,
+    /*hbm_bps*/ 4.3e12, /*fp32_flops*/ 44.5e12,
     /*overhead bytes per input element: native, chunked (scan), emulated (scan + split), fp16x3 (+ exponent
-      scan)*/ 0.0, 4.0, 12.0, 16.0,
+      scan)*/ 0.0, 4.0, 12.0, 20.0,
     /*rho_ref_coef*/ 0.64,
     /*rho_factor_min*/ 1.0,
 };
