@@ -14,6 +14,10 @@ reference: the emugemm-cdna path has no CPU implementation of its GEMM (its slic
            products, FP64 accumulation) on a bounded row sample with all host threads, rank 0 only.
 With N > 1 (torchrun) each rank computes its own 8192-row block of a (8192*N) x 8192 x 8192 product and B
 is broadcast from rank 0 with NCCL inside every step (weak scaling).
+Other workloads (--workload): `rows` = one S^3 product with the rows of A split over the ranks and B broadcast
+from rank 0 in column panels (strong scaling; S = 32768 is the sharded multi-GPU configuration); `ksplit` =
+S x S x --k with K split over the ranks, FP64 partial products summed by NCCL and rounded once (S = 4096,
+K = 1048576 is the long-K multi-GPU configuration).
 """
 from __future__ import annotations
 
@@ -46,6 +50,10 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
+    ap.add_argument("--workload", default="square", choices=["square", "rows", "ksplit"],
+                    help="square: S^3 per GPU (weak); rows: one S^3 product, rows over GPUs; "
+                         "ksplit: S x S x --k, K over GPUs")
+    ap.add_argument("--k", type=int, default=1048576, help="K of the ksplit workload")
     return ap.parse_args()
 
 
@@ -221,10 +229,11 @@ def ours(args) -> None:
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
+    import multigpu
+
     S = args.size
-    M, N, K = S, S, S
     scheme = SCHEMES[args.scheme]
     gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
 
@@ -233,22 +242,65 @@ def ours(args) -> None:
         e = torch.randint(-20, 21, shape, device="cuda", generator=gen).float()
         return torch.ldexp(x, e)
 
-    A = wide((M, K))
-    B = wide((K, N)) if rank == 0 else torch.empty((K, N), device="cuda")
-    C = torch.empty((M, N), device="cuda")
     stream = torch.cuda.current_stream()
     h = emugemm.Handle(stream=stream.cuda_stream)
     hints = lambda: emugemm.EmuHints(1.0, 1.0, 0, 0.0, 0)  # noqa: E731  (forced scheme: no scans, no rho)
+    wl = args.workload
 
-    if dist is not None:
-        import multigpu
+    if wl == "square":
+        # M = N = K = S per GPU; with N GPUs each rank owns S rows of an (S*N) x S x S product (weak scaling)
+        M, N, K = S, S, S
+        m_loc, k_loc = M, K
+        A = wide((M, K))
+        B = wide((K, N)) if rank == 0 else torch.empty((K, N), device="cuda")
+        C = torch.empty((M, N), device="cuda")
+        total_flop = 2.0 * M * N * K * world
+        scaling = "weak"
+        desc = f"{args.scheme} emulated SGEMM {S}^3 per GPU" + (", B broadcast from rank 0 (NCCL) each step"
+                                                                  if world > 1 else "")
+        if dist is not None:
+            def step():
+                # this rank's row block; B arrives from rank 0 in two column panels, each GEMM starting on arrival
+                multigpu.row_sharded(A, B, C, src=0, panel=(N + 1) // 2, handle=h, scheme=scheme)
+        else:
+            def step():
+                h.sgemm(M, N, K, A, B, C, force=scheme, hints=hints())
+    elif wl == "rows":
+        # one M = N = K = S product; rows of A split over the ranks, B broadcast from rank 0 (strong scaling)
+        M, N, K = S, S, S
+        r0, r1 = multigpu.row_range(M, rank, world)
+        m_loc, k_loc = r1 - r0, K
+        A = wide((m_loc, K))
+        B = wide((K, N)) if rank == 0 else torch.empty((K, N), device="cuda")
+        C = torch.empty((m_loc, N), device="cuda")
+        total_flop = 2.0 * M * N * K
+        scaling = "strong"
+        desc = f"{args.scheme} emulated SGEMM {S}^3, row blocks of A over {world} GPU(s), B broadcast in panels"
 
         def step():
-            # this rank's row block; B arrives from rank 0 in two column panels, each GEMM starting on arrival
-            multigpu.row_sharded(A, B, C, src=0, panel=(N + 1) // 2, handle=h, scheme=scheme)
+            if dist is not None:
+                multigpu.row_sharded(A, B, C, src=0, panel=(N + 1) // 2, handle=h, scheme=scheme)
+            else:
+                h.sgemm(m_loc, N, K, A, B, C, force=scheme, hints=hints())
     else:
+        # M = N = S, K = args.k split over the ranks; FP64 partials summed by NCCL, one rounding (strong scaling)
+        M, N, K = S, S, args.k
+        k0, k1 = multigpu.k_range(K, rank, world)
+        m_loc, k_loc = M, k1 - k0
+        A = wide((M, k_loc))
+        B = wide((k_loc, N))
+        C = torch.empty((M, N), device="cuda")
+        total_flop = 2.0 * M * N * K
+        scaling = "strong"
+        desc = f"{args.scheme} emulated SGEMM {M}x{N}x{K}, K split over {world} GPU(s), FP64 partials reduced"
+
         def step():
-            h.sgemm(M, N, K, A, B, C, force=scheme, hints=hints())
+            if dist is not None:
+                multigpu.k_split(A, B, C, M=M, N=N, handle=h, scheme=scheme)
+            else:
+                P = torch.empty((M, N), dtype=torch.float64, device="cuda")
+                h.partial_f64(M, N, k_loc, A, k_loc, B, N, P, scheme, 1)
+                h.reduce_f64(M, N, 1, P, C)
 
     for _ in range(args.warmup):
         step()
@@ -276,14 +328,14 @@ def ours(args) -> None:
         ms_total = float(t.item())
         dist.barrier()
     ms_step = ms_total / args.steps
-    flop_step = 2.0 * M * N * K * world
-    value = flop_step / (ms_step * 1e-3) / 1e12
+    value = total_flop / (ms_step * 1e-3) / 1e12
 
-    # dominant kernel: the tensor-core 3-product GEMM (3 * 2MNK tensor FLOPs per launch)
+    # dominant kernel: the tensor-core 3-product GEMM (3 * 2 * m * n * k tensor FLOPs per rank and step)
     gemm_ms, gemm_n = prof["tc_gemm"]
     gemm_avg = gemm_ms / max(gemm_n, 1)
     launches_per_step = max(1, gemm_n // max(1, args.steps))
-    tensor_tflops = (3 * 2.0 * M * N * K / launches_per_step / (gemm_avg * 1e-3) / 1e12) if gemm_n else None
+    rank_tensor_flop = 3 * 2.0 * m_loc * N * k_loc
+    tensor_tflops = (rank_tensor_flop / launches_per_step / (gemm_avg * 1e-3) / 1e12) if gemm_n else None
     burst, sustained, hbm, src = peaks()
     # a timed loop of more than half a second runs under the power cap: compare with the sustained peak
     long_loop = ms_total > 500.0
@@ -292,7 +344,7 @@ def ours(args) -> None:
 
     # end to end: host inputs (pinned), H2D + call + D2H of C inside every step
     e2e = None
-    if not args.no_e2e and world == 1:
+    if not args.no_e2e and world == 1 and wl == "square":
         hA = A.cpu().pin_memory()
         hB = B.cpu().pin_memory()
         hC = torch.empty((M, N), dtype=torch.float32).pin_memory()
@@ -307,7 +359,7 @@ def ours(args) -> None:
         for _ in range(2):
             e2e_step()
         torch.cuda.synchronize()
-        n_e2e = max(3, args.steps // 4)
+        n_e2e = max(3, min(30, args.steps // 4))
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(n_e2e):
@@ -320,12 +372,12 @@ def ours(args) -> None:
                "ms_per_step": e_ms}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu and wl == "square":
         cpu = cpu_fp64_baseline(S)
 
     # cuBLAS SGEMM on the same GPU and shape (strict FP32: no TF32), a comparison figure only
     cublas = None
-    if world == 1 and not args.no_cublas:
+    if world == 1 and not args.no_cublas and wl == "square":
         torch.backends.cuda.matmul.allow_tf32 = False
         torch.set_float32_matmul_precision("highest")
         for _ in range(3):
@@ -346,21 +398,20 @@ def ours(args) -> None:
         line = {
             "metric": "emulated-FP32 TFLOPS", "value": value, "unit": "TFLOPS", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "scaling": scaling, "vs_baseline": None, "dtype": "f32",
             "data": "synthetic N(0,1)*2^e, e~U{-20..20} (torch generator)",
-            "config": {"workload": f"{args.scheme} emulated SGEMM {S}^3 per GPU"
-                                   + (f", B broadcast from rank 0 (NCCL) each step" if world > 1 else ""),
-                       "M": M * world, "N": N, "K": K, "scheme": args.scheme, "force_scheme": scheme,
-                       "hints": "absmax given, rho=0 (no scans)", "l2": "inputs larger than L2 (268 MB each)",
-                       "parallelism": f"row blocks x{world}" if world > 1 else "single GPU"},
+            "config": {"workload": desc, "M": M * (world if wl == "square" else 1), "N": N, "K": K,
+                       "scheme": args.scheme, "force_scheme": scheme,
+                       "hints": "absmax given, rho=0 (no scans)", "l2": "inputs larger than L2",
+                       "parallelism": (f"{wl} x{world}" if world > 1 else "single GPU")},
             "roofline": {"bound": "tensor", "kernel": "k_tc_gemm", "achieved": tensor_tflops,
                          "peak": peak, "peak_source": f"{peak_name} ({src})", "unit": "TFLOP/s",
                          "frac": (tensor_tflops / peak) if tensor_tflops else None,
                          "frac_of_burst": (tensor_tflops / burst) if tensor_tflops else None,
-                         "flops_per_launch": 3 * 2.0 * M * N * K / launches_per_step, "kernel_ms": gemm_avg,
-                         "traffic": TRAFFIC.get((args.scheme, S)),
+                         "flops_per_launch": rank_tensor_flop / launches_per_step, "kernel_ms": gemm_avg,
+                         "traffic": TRAFFIC.get((args.scheme, S)) if wl == "square" else None,
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch at this size"
-                         if (args.scheme, S) in TRAFFIC else None},
+                         if (wl == "square" and (args.scheme, S) in TRAFFIC) else None},
             "kernel_ms": {k: (v[0] / v[1] if v[1] else None) for k, v in prof.items()},
             "cpu_baseline": cpu,
             "cublas_sgemm": cublas,
