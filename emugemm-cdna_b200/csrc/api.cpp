@@ -158,19 +158,24 @@ static void prof_clear(Handle* h) {
 
 static long round_up(long x, long m) { return (x + m - 1) / m * m; }
 
-// Tensor-core kernel for a shape: the environment variable EMUGEMM_TC_KERNEL ("single" or "pair") if set, else
-// the tile table's code (1 = single-CTA, 2 = CTA pair), else the built-in choice: CTA pairs for bf16x3 when
-// the 256 x 256 pair tiles fill every pair of SMs at least once (measured at 8192^3: 2.34 ms against 2.43 ms
-// single-CTA), single-CTA 128-row tiles otherwise and for fp16x3 (3.24 ms against 3.40 ms for pairs).
-static bool use_pair_kernel(Handle* h, int M, int N, long K, bool fp16) {
+// Tensor-core kernel for a shape: 1 = single-CTA, 2 = CTA pair, 3 = CTA pair with the split fused in (bf16x3).
+// The environment variable EMUGEMM_TC_KERNEL ("single", "pair", "fused") wins, then the tile table's code, then
+// the built-in choice: CTA pairs for bf16x3 when the 256 x 256 pair tiles fill every pair of SMs at least once
+// (measured at 8192^3: 2.34 ms against 2.43 ms single-CTA), single-CTA 128-row tiles otherwise and for fp16x3
+// (3.24 ms against 3.40 ms for pairs).
+static int tc_kernel_choice(Handle* h, int M, int N, long K, bool fp16) {
     const char* v = std::getenv("EMUGEMM_TC_KERNEL");
-    if (v && std::strcmp(v, "pair") == 0) return true;
-    if (v && std::strcmp(v, "single") == 0) return false;
-    const int code = lookup_tile(M, N, K, fp16 ? 2 : 1).tc_variant;
-    if (code) return code == 2;
-    if (fp16) return false;
-    const long pair_tiles = ((M + 255) / 256) * (long)((N + 255) / 256);
-    return pair_tiles >= (h->num_sms > 0 ? h->num_sms : 148) / 2;
+    int code = 0;
+    if (v && std::strcmp(v, "single") == 0) code = 1;
+    else if (v && std::strcmp(v, "pair") == 0) code = 2;
+    else if (v && std::strcmp(v, "fused") == 0) code = 3;
+    if (!code) code = lookup_tile(M, N, K, fp16 ? 2 : 1).tc_variant;
+    if (!code) {
+        const long pair_tiles = ((M + 255) / 256) * (long)((N + 255) / 256);
+        code = (!fp16 && pair_tiles >= (h->num_sms > 0 ? h->num_sms : 148) / 2) ? 2 : 1;
+    }
+    if (fp16 && code == 3) code = 2;
+    return code;
 }
 
 // bf16x3 / fp16x3 through the tensor-core kernel over pre-split slices. With a_reused (hints->a_is_reused) and
@@ -178,9 +183,16 @@ static bool use_pair_kernel(Handle* h, int M, int N, long K, bool fp16) {
 // split again: the caller has declared A unchanged since that call.
 static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, long lda, const float* B, long ldb,
                                float* C, long ldc, double* C64, long ldc64, bool fp16, bool a_reused) {
-    const bool pair = use_pair_kernel(h, M, N, K, fp16);
+    const int choice = tc_kernel_choice(h, M, N, K, fp16);
+    if (choice == 3) {
+        ProfScope ps(h, kProfTcGemm);
+        const int e = launch_tc_fused(A, lda, B, ldb, M, N, K, C, ldc, C64, ldc64, h->err_dev, h->num_sms, h->stream);
+        if (e != (int)cudaErrorNotSupported) return from_cuda(e);
+        // operands TMA cannot address (odd leading dimension or alignment): pre-split below
+    }
+    const bool pair = choice >= 2;
     const int BN = pair ? tc_pair_bn(fp16 ? 1 : 0) : tc_gemm_bn(fp16 ? 1 : 0);
-    const long Mp = round_up(M, pair ? 256 : 128), Np = round_up(N, BN), Kp = round_up(K, 64);
+    const long Mp = round_up(M, pair ? 256 : 128), Np = round_up(N, BN), Kp = slice_kp(K), KP = slice_panel(Kp);
     if (Mp > 0x7fffffffL || Np > 0x7fffffffL || Kp > 0x7fffffffL) return EMUGEMM_STATUS_INVALID_SIZE;
     uint16_t* a0 = (uint16_t*)ws_get(h, kWsSplitA0, (size_t)Mp * Kp * 2);
     uint16_t* a1 = (uint16_t*)ws_get(h, kWsSplitA1, (size_t)Mp * Kp * 2);
@@ -213,15 +225,15 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
         ProfScope ps(h, kProfSplit);
         if (!reuse) {
             h->a_key = Handle::ASplitKey();   // invalid until the split below has been enqueued
-            e = launch_split_rows(A, M, K, lda, (int)Mp, Kp, kind, rexp, a0, a1, h->stream);
+            e = launch_split_rows(A, M, K, lda, (int)Mp, Kp, KP, kind, rexp, a0, a1, h->stream);
         }
-        if (!e) e = launch_split_cols(B, K, N, ldb, (int)Np, Kp, kind, cexp, b0, b1, h->stream);
+        if (!e) e = launch_split_cols(B, K, N, ldb, (int)Np, Kp, KP, kind, cexp, b0, b1, h->stream);
     }
     if (e) return from_cuda(e);
     h->a_key = key;
     TcGemmArgs t;
     t.a_hi = a0; t.a_lo = a1; t.b_hi = b0; t.b_lo = b1;
-    t.M = M; t.N = N; t.Mp = (int)Mp; t.Np = (int)Np; t.Kp = Kp;
+    t.M = M; t.N = N; t.Mp = (int)Mp; t.Np = (int)Np; t.Kp = Kp; t.KP = KP;
     t.C = C; t.ldc = ldc; t.C64 = C64; t.ldc64 = ldc64;
     t.fp16 = fp16 ? 1 : 0;
     t.row_exp = rexp; t.col_exp = cexp;

@@ -47,7 +47,8 @@ extern const char* const kReasonNative;
 // ---------------------------------------------------------------------------------------------------
 // tune.cpp: per-shape tile table
 struct TileChoice {
-    int tc_variant;     // tensor-core kernel: 0 = built-in choice, 1 = single-CTA, 2 = CTA pair (cta_group::2)
+    int tc_variant;     // tensor-core kernel: 0 = built-in choice, 1 = single-CTA, 2 = CTA pair (cta_group::2),
+                        // 3 = CTA pair with the split fused in (bf16x3 only)
     int fp32_bm;        // FP32 SIMT tile edge: 0 = auto, 64 or 128
 };
 TileChoice lookup_tile(int M, int N, long K, int dtype /*0 fp32, 1 bf16, 2 fp16*/);
@@ -122,10 +123,20 @@ int launch_col_exponents(const float* B, long K, int N, long ldb, int* e_out, un
                          void* stream);
 // Pre-split into K-major 16-bit slices: rows x Kp (zero padded to rows_p x Kp).
 // kind 0 = bf16, 1 = scaled fp16 (hi = RNE(x*2^-e), lo = RNE((x*2^-e - hi)*2048)).
-int launch_split_rows(const float* A, int M, long K, long lda, int Mp, long Kp, int kind,
+// Slices are stored in K panels, [Kp / KP][rows][KP] 16-bit values, so that the rows one TMA box touches sit
+// 2 * KP bytes apart whatever K is. With plain rows of Kp values the bf16x3 kernel at M = N = 4096 ran at 43 % of
+// tensor peak for K = 2^20 (rows 2 MB apart) against 72 % for K = 2^19. KP = Kp up to kSlicePanelMax values of
+// K (one panel, plain rows), kSlicePanel beyond, with Kp rounded up to whole panels.
+constexpr long kSlicePanel = 8192, kSlicePanelMax = 16384;
+inline long slice_kp(long K) {
+    const long k = (K + 63) / 64 * 64;
+    return k <= kSlicePanelMax ? k : (k + kSlicePanel - 1) / kSlicePanel * kSlicePanel;
+}
+inline long slice_panel(long Kp) { return Kp <= kSlicePanelMax ? Kp : kSlicePanel; }
+int launch_split_rows(const float* A, int M, long K, long lda, int Mp, long Kp, long KP, int kind,
                       const int* row_exp, uint16_t* hi, uint16_t* lo, void* stream);
 // B (KxN, ldb) -> transposed K-major slices Np x Kp.
-int launch_split_cols(const float* B, long K, int N, long ldb, int Np, long Kp, int kind,
+int launch_split_cols(const float* B, long K, int N, long ldb, int Np, long Kp, long KP, int kind,
                       const int* col_exp, uint16_t* hi, uint16_t* lo, void* stream);
 
 // k_tc_gemm.cu: tensor-core 3-product GEMM over pre-split K-major slices.
@@ -133,6 +144,7 @@ struct TcGemmArgs {
     const uint16_t* a_hi; const uint16_t* a_lo;   // Mp x Kp
     const uint16_t* b_hi; const uint16_t* b_lo;   // Np x Kp
     int M, N, Mp, Np; long Kp;
+    long KP;                                       // K panel width (slice_panel(Kp))
     float* C; long ldc;
     double* C64; long ldc64;                       // when non-null: write FP64 instead of C
     int fp16;                                      // 0 = bf16x3, 1 = scaled fp16x3
@@ -145,6 +157,10 @@ int tc_gemm_bn(int fp16);   // output tile width of the bf16x3 (0) / fp16x3 (1) 
 // k_tc_gemm2.cu: the same product on CTA pairs (cta_group::2); needs Mp % 256 == 0.
 int launch_tc_gemm_pair(const TcGemmArgs& a, void* stream);
 int tc_pair_bn(int fp16);
+// k_tc_fused.cu: bf16x3 with the split fused into the CTA-pair GEMM (FP32 tiles by TMA, no slices in HBM).
+// Returns cudaErrorNotSupported unless lda, ldb are multiples of 4 and A, B are 16-byte aligned.
+int launch_tc_fused(const float* A, long lda, const float* B, long ldb, int M, int N, long K, float* C, long ldc,
+                    double* C64, long ldc64, unsigned* err, int num_sms, void* stream);
 
 // k_fp32_gemm.cu: FP32 SIMT GEMM with K-chunks summed in FP64.
 struct Fp32GemmArgs {

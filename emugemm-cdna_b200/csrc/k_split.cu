@@ -121,18 +121,22 @@ __global__ void k_col_exponents(const unsigned* __restrict__ colmax_bits, int N,
     if (n < N) e_out[n] = exponent_for_max(__uint_as_float(colmax_bits[n]));
 }
 
-// A (M x K, lda) -> hi/lo slices, K-major, Mp x Kp, zero padded. One thread per (row, 8 consecutive k).
+// A (M x K, lda) -> hi/lo slices, K-major in K panels ([Kp / KP][Mp][KP]), zero padded. One thread per
+// (row, 8 consecutive k); item g writes values 8g .. 8g+7 of the slice, so the stores are contiguous.
 template <int KIND>
-__global__ void k_split_rows(const float* __restrict__ A, int M, long K, long lda, int Mp, long Kp,
+__global__ void k_split_rows(const float* __restrict__ A, int M, long K, long lda, int Mp, long Kp, long KP,
                              const int* __restrict__ row_exp, uint16_t* __restrict__ hi,
                              uint16_t* __restrict__ lo) {
-    const long groups_per_row = Kp / 8;
-    const size_t total = (size_t)Mp * groups_per_row;
+    const long groups_per_row = KP / 8;
+    const size_t per_panel = (size_t)Mp * groups_per_row;
+    const size_t total = per_panel * (size_t)(Kp / KP);
     const bool vec = ((lda & 3) == 0) && ((reinterpret_cast<uintptr_t>(A) & 15) == 0);
     for (size_t g = (size_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
          g += (size_t)gridDim.x * blockDim.x) {
-        const int m = (int)(g / groups_per_row);
-        const long k0 = (long)(g - (size_t)m * groups_per_row) * 8;
+        const size_t panel = g / per_panel;
+        const size_t rem = g - panel * per_panel;
+        const int m = (int)(rem / groups_per_row);
+        const long k0 = (long)panel * KP + (long)(rem - (size_t)m * groups_per_row) * 8;
         float x[8];
         if (m < M && vec && k0 + 8 <= K) {
             const float4* p = reinterpret_cast<const float4*>(A + (size_t)m * lda + k0);
@@ -160,59 +164,66 @@ __global__ void k_split_rows(const float* __restrict__ A, int M, long K, long ld
             h4[j / 2] = (uint32_t)h0 | ((uint32_t)h1 << 16);
             l4[j / 2] = (uint32_t)l0 | ((uint32_t)l1 << 16);
         }
-        const size_t o = (size_t)m * Kp + k0;
+        const size_t o = g * 8;
         *reinterpret_cast<uint4*>(hi + o) = make_uint4(h4[0], h4[1], h4[2], h4[3]);
         *reinterpret_cast<uint4*>(lo + o) = make_uint4(l4[0], l4[1], l4[2], l4[3]);
     }
 }
 
-// B (K x N, ldb) -> transposed hi/lo slices, K-major, Np x Kp, zero padded. 64 x 64 tiles through shared
-// memory: coalesced reads along n, coalesced 16-byte writes along k.
+// B (K x N, ldb) -> transposed hi/lo slices, K-major in K panels ([Kp / KP][Np][KP]), zero padded. 64 x 64
+// tiles through shared memory: coalesced reads along n, coalesced 16-byte writes along k. blockIdx.y strides
+// over the k-tiles, so any K fits the grid's y limit.
 template <int KIND>
 __global__ void __launch_bounds__(256) k_split_cols(const float* __restrict__ B, long K, int N, long ldb,
-                                                    int Np, long Kp, const int* __restrict__ col_exp,
+                                                    int Np, long Kp, long KP, const int* __restrict__ col_exp,
                                                     uint16_t* __restrict__ hi, uint16_t* __restrict__ lo) {
     __shared__ float t[64][65];
     const int n0 = blockIdx.x * 64;
-    const long k0 = (long)blockIdx.y * 64;
     const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;   // 64 x 4
-    // all 16 loads of a thread are issued before any is stored, so 16 are in flight at once
-    float v[16];
+    for (long kt = blockIdx.y; kt < Kp / 64; kt += gridDim.y) {
+        const long k0 = kt * 64;
+        const long panel = k0 / KP;
+        uint16_t* const hi_p = hi + (size_t)panel * Np * KP + (k0 - panel * KP);
+        uint16_t* const lo_p = lo + (size_t)panel * Np * KP + (k0 - panel * KP);
+        // all 16 loads of a thread are issued before any is stored, so 16 are in flight at once
+        float v[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const long k = k0 + ty + 4 * i;
-        const int n = n0 + tx;
-        v[i] = (k < K && n < N) ? __ldg(B + (size_t)k * ldb + n) : 0.f;
-    }
-#pragma unroll
-    for (int i = 0; i < 16; ++i) t[ty + 4 * i][tx] = v[i];
-    __syncthreads();
-    // 64 columns x 8 groups of 8 k = 512 items, 2 per thread. Eight consecutive lanes take the eight k-groups
-    // of one output row, so each warp store fills four whole 128-byte lines.
-    for (int item = threadIdx.x; item < 512; item += 256) {
-        const int kg = item & 7, nn = item >> 3;
-        const int n = n0 + nn;
-        if (n >= Np) continue;
-        int e = 0;
-        if (KIND == 1 && n < N) e = col_exp[n];
-        uint32_t h4[4], l4[4];
-#pragma unroll
-        for (int j = 0; j < 8; j += 2) {
-            const float x0 = t[kg * 8 + j][nn], x1 = t[kg * 8 + j + 1][nn];
-            uint16_t h0, l0, h1, l1;
-            if (KIND == 0) {
-                split_bf16(x0, h0, l0);
-                split_bf16(x1, h1, l1);
-            } else {
-                split_f16(scale_pow2(x0, e), h0, l0);
-                split_f16(scale_pow2(x1, e), h1, l1);
-            }
-            h4[j / 2] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-            l4[j / 2] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+        for (int i = 0; i < 16; ++i) {
+            const long k = k0 + ty + 4 * i;
+            const int n = n0 + tx;
+            v[i] = (k < K && n < N) ? __ldg(B + (size_t)k * ldb + n) : 0.f;
         }
-        const size_t o = (size_t)n * Kp + k0 + kg * 8;
-        *reinterpret_cast<uint4*>(hi + o) = make_uint4(h4[0], h4[1], h4[2], h4[3]);
-        *reinterpret_cast<uint4*>(lo + o) = make_uint4(l4[0], l4[1], l4[2], l4[3]);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) t[ty + 4 * i][tx] = v[i];
+        __syncthreads();
+        // 64 columns x 8 groups of 8 k = 512 items, 2 per thread. Eight consecutive lanes take the eight k-groups
+        // of one output row, so each warp store fills four whole 128-byte lines.
+        for (int item = threadIdx.x; item < 512; item += 256) {
+            const int kg = item & 7, nn = item >> 3;
+            const int n = n0 + nn;
+            if (n >= Np) continue;
+            int e = 0;
+            if (KIND == 1 && n < N) e = col_exp[n];
+            uint32_t h4[4], l4[4];
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+                const float x0 = t[kg * 8 + j][nn], x1 = t[kg * 8 + j + 1][nn];
+                uint16_t h0, l0, h1, l1;
+                if (KIND == 0) {
+                    split_bf16(x0, h0, l0);
+                    split_bf16(x1, h1, l1);
+                } else {
+                    split_f16(scale_pow2(x0, e), h0, l0);
+                    split_f16(scale_pow2(x1, e), h1, l1);
+                }
+                h4[j / 2] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+                l4[j / 2] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+            }
+            const size_t o = (size_t)n * KP + kg * 8;
+            *reinterpret_cast<uint4*>(hi_p + o) = make_uint4(h4[0], h4[1], h4[2], h4[3]);
+            *reinterpret_cast<uint4*>(lo_p + o) = make_uint4(l4[0], l4[1], l4[2], l4[3]);
+        }
+        __syncthreads();   // the tile is rewritten by the next k-tile
     }
 }
 
@@ -277,27 +288,30 @@ int launch_col_exponents(const float* B, long K, int N, long ldb, int* e_out, un
     return (int)cudaGetLastError();
 }
 
-int launch_split_rows(const float* A, int M, long K, long lda, int Mp, long Kp, int kind, const int* row_exp,
-                      uint16_t* hi, uint16_t* lo, void* stream) {
+int launch_split_rows(const float* A, int M, long K, long lda, int Mp, long Kp, long KP, int kind,
+                      const int* row_exp, uint16_t* hi, uint16_t* lo, void* stream) {
     size_t total = (size_t)Mp * (Kp / 8);
     if (total == 0) return 0;
+    if (KP <= 0 || KP % 64 || Kp % KP) return (int)cudaErrorInvalidValue;
     int g = grid_for(total, 256, 148 * 32);
     if (kind == 0)
-        k_split_rows<0><<<g, 256, 0, (cudaStream_t)stream>>>(A, M, K, lda, Mp, Kp, row_exp, hi, lo);
+        k_split_rows<0><<<g, 256, 0, (cudaStream_t)stream>>>(A, M, K, lda, Mp, Kp, KP, row_exp, hi, lo);
     else
-        k_split_rows<1><<<g, 256, 0, (cudaStream_t)stream>>>(A, M, K, lda, Mp, Kp, row_exp, hi, lo);
+        k_split_rows<1><<<g, 256, 0, (cudaStream_t)stream>>>(A, M, K, lda, Mp, Kp, KP, row_exp, hi, lo);
     count_launch();
     return (int)cudaGetLastError();
 }
 
-int launch_split_cols(const float* B, long K, int N, long ldb, int Np, long Kp, int kind, const int* col_exp,
-                      uint16_t* hi, uint16_t* lo, void* stream) {
+int launch_split_cols(const float* B, long K, int N, long ldb, int Np, long Kp, long KP, int kind,
+                      const int* col_exp, uint16_t* hi, uint16_t* lo, void* stream) {
     if (Np == 0 || Kp == 0) return 0;
-    dim3 grid((unsigned)((Np + 63) / 64), (unsigned)(Kp / 64));
+    if (KP <= 0 || KP % 64 || Kp % KP) return (int)cudaErrorInvalidValue;
+    const long ktiles = Kp / 64;
+    dim3 grid((unsigned)((Np + 63) / 64), (unsigned)(ktiles < 65535 ? ktiles : 65535));
     if (kind == 0)
-        k_split_cols<0><<<grid, 256, 0, (cudaStream_t)stream>>>(B, K, N, ldb, Np, Kp, col_exp, hi, lo);
+        k_split_cols<0><<<grid, 256, 0, (cudaStream_t)stream>>>(B, K, N, ldb, Np, Kp, KP, col_exp, hi, lo);
     else
-        k_split_cols<1><<<grid, 256, 0, (cudaStream_t)stream>>>(B, K, N, ldb, Np, Kp, col_exp, hi, lo);
+        k_split_cols<1><<<grid, 256, 0, (cudaStream_t)stream>>>(B, K, N, ldb, Np, Kp, KP, col_exp, hi, lo);
     count_launch();
     return (int)cudaGetLastError();
 }

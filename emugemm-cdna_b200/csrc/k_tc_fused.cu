@@ -1,0 +1,480 @@
+// k_tc_fused.cu - bf16x3 emulated SGEMM with the hi/lo split fused into the GEMM (CTA pairs, cta_group::2).
+//
+// The pre-split path (k_split.cu + k_tc_gemm*.cu) writes the bf16 slices of A and B to HBM and reads them back.
+// Here TMA loads the caller's FP32 tiles straight into a shared-memory staging ring, converter warps split them
+// (hi = RNE_bf16(x), lo = RNE_bf16(x - hi): the rule of emugemm-cdna src/emugemm.cpp:143-145) into the UMMA
+// K-major layout with the 64-byte swizzle (B is transposed on the way), and the pair's leader issues the three
+// tcgen05 MMAs per k-step from those slices. The slices never exist in HBM.
+//
+// Per CTA (one of a pair sharing a 256 x 256 tile): 128 rows of A and 128 columns of B, k-blocks of 32.
+//   fp32 ring  kF32Stages x (A 128x32 + B 32x128 FP32)        TMA -> converters
+//   bf16 ring  kBfStages  x (A hi,lo 128x32 + B^T hi,lo 128x32) converters -> pair MMA
+// Warps (EMUGEMM_FUSED_WARPS = 16, the default): warpgroup 0 = TMA producer, MMA issuer (leader) / TMEM
+// allocator and two converter warps; warpgroups 1-2 = promotion + epilogue (as in k_tc_gemm2.cu); warpgroup 3 =
+// four converter warps. The register file is rebalanced per warpgroup with setmaxnreg, executed by every warp of
+// a warpgroup at the top of its branch: launch 512 threads x 128 = 65536 registers; epilogue warpgroups grow to
+// 176, the others shrink to 80 (2*128*176 + 2*128*80 = 65536). EMUGEMM_FUSED_WARPS = 12: warps 2..9 epilogue,
+// 10-11 converters, 168 registers each, no rebalancing.
+// Signalling: fp32 ring local to each CTA; bf16 stages of both CTAs are announced on the leader's bf_full
+// (one arrive per converter warp, the peer's remotely) after a generic->async proxy fence; the leader's commits free
+// the bf16 stages and publish TMEM chunks in both CTAs. All waits are bounded.
+#include "device_utils.cuh"
+#include "emugemm_internal.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace emu {
+
+bool tc_get_encode(PFN_cuTensorMapEncodeTiled_v12000* out);
+
+namespace {
+
+using namespace dev;
+
+#ifndef EMUGEMM_FUSED_WARPS
+#define EMUGEMM_FUSED_WARPS 16
+#endif
+constexpr int kWarps = EMUGEMM_FUSED_WARPS;
+constexpr int kThreads = 32 * kWarps;
+constexpr bool kRegSplit = (kWarps == 16);
+constexpr int kEpiFirst = kRegSplit ? 4 : 2;        // first epilogue warp
+constexpr int kEpiWarps = 8;
+constexpr int kConvWarps = kWarps - 2 - kEpiWarps;  // 6 or 2
+constexpr int kConvThreads = 32 * kConvWarps;
+constexpr int kRegEpi = 176, kRegOther = 80;        // setmaxnreg targets (16 warps)
+static_assert(!kRegSplit || 2 * 128 * kRegEpi + 2 * 128 * kRegOther == kThreads * 128, "register split");
+constexpr int kBM = 128;                            // rows per CTA
+constexpr int kBN = 256;                            // pair tile width
+constexpr int kBNH = 128;                           // columns of B per CTA
+constexpr int kBK = 32;                             // k-block (64-byte rows of bf16)
+constexpr int kChunkKB = 128 / kBK;                 // promotion every 128 values of K
+constexpr int kGroupM = 8;
+constexpr int kF32Stages = 3;
+constexpr int kBfStages = 3;
+constexpr int kF32A = kBM * kBK * 4;                // 16 KB
+constexpr int kF32B = kBK * kBNH * 4;               // 16 KB
+constexpr int kF32Stage = kF32A + kF32B;
+constexpr int kBfA = kBM * kBK * 2;                 // 8 KB per slice
+constexpr int kBfB = kBNH * kBK * 2;
+constexpr int kBfStage = 2 * kBfA + 2 * kBfB;       // 32 KB
+static_assert(kBfA == kBfB, "each lo slice sits kBfA bytes after its hi slice");
+constexpr int kAccCols = kBN;
+constexpr int kHalf = kBN / 2;
+constexpr int kSmemBytes = kF32Stages * kF32Stage + kBfStages * kBfStage + 1024 + 512;
+constexpr uint32_t kIdesc = idesc_f16(2 * kBM, kBN, true);
+
+struct CtlF {
+    uint64_t f32_full[kF32Stages];
+    uint64_t f32_empty[kF32Stages];
+    uint64_t bf_full[kBfStages];     // leader: every converter warp of both CTAs
+    uint64_t bf_empty[kBfStages];    // both: leader's commit
+    uint64_t tmem_full[2];
+    uint64_t tmem_empty[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+};
+
+struct KParamsF {
+    int M, N, num_m2, num_n, nk;
+    float* C; long ldc;
+    double* C64; long ldc64;
+    unsigned* err;
+};
+
+__device__ __forceinline__ void tile_coords_f(int t, int num_m2, int num_n, int& mb2, int& nb) {
+    const int per_group = kGroupM * num_n;
+    const int g = t / per_group;
+    const int first_m = g * kGroupM;
+    const int gm = min(num_m2 - first_m, kGroupM);
+    const int r = t - g * per_group;
+    mb2 = first_m + r % gm;
+    nb = r / gm;
+}
+
+__device__ __forceinline__ void drain_wait_f(uint64_t* bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    unsigned long long t0 = globaltimer();
+    while (!mbar_try_wait(a, parity)) {
+        if (globaltimer() - t0 > 200000000ull) return;
+    }
+}
+
+__device__ __forceinline__ void abort_pair_f(CtlF* ctl, uint32_t peer) {
+    ctl->abort = 1;
+    st_shared_cluster_u32(mapa_shared(smem_u32(&ctl->abort), peer), 1u);
+}
+
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// hi/lo bf16 slices of 8 consecutive values, packed 2 per 32-bit word (lower k in the low half).
+__device__ __forceinline__ void split8(const float (&x)[8], uint4& hi, uint4& lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat162 hb = __floats2bfloat162_rn(x[2 * j], x[2 * j + 1]);
+        const uint32_t hw = *reinterpret_cast<const uint32_t*>(&hb);
+        const float h0 = __uint_as_float(hw << 16), h1 = __uint_as_float(hw & 0xffff0000u);
+        const __nv_bfloat162 lb = __floats2bfloat162_rn(x[2 * j] - h0, x[2 * j + 1] - h1);
+        h[j] = hw;
+        l[j] = *reinterpret_cast<const uint32_t*>(&lb);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// byte offset of 16-byte chunk `c` of row `r` in a K-major tile with 64-byte rows and the 64-byte swizzle
+__device__ __forceinline__ uint32_t sw64(int r, int c) { return (uint32_t)(r * 64 + ((c ^ ((r >> 1) & 3)) << 4)); }
+
+__global__ void __launch_bounds__(kThreads, 1)
+    k_tc_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, KParamsF p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* f32 = smem;
+    uint8_t* bf = smem + kF32Stages * kF32Stage;
+    CtlF* ctl = reinterpret_cast<CtlF*>(bf + kBfStages * kBfStage);
+    volatile int* abort = &ctl->abort;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const uint32_t peer = rank ^ 1u;
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+    const int num_tiles = p.num_m2 * p.num_n;
+    const int nchunks = (p.nk + kChunkKB - 1) / kChunkKB;
+    const bool is_epi = warp >= kEpiFirst && warp < kEpiFirst + kEpiWarps;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kF32Stages; ++s) {
+            mbar_init(&ctl->f32_full[s], 1);
+            mbar_init(&ctl->f32_empty[s], kConvWarps);
+        }
+        for (int s = 0; s < kBfStages; ++s) {
+            mbar_init(&ctl->bf_full[s], 2 * kConvWarps);
+            mbar_init(&ctl->bf_empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&ctl->tmem_full[b], 1);
+            mbar_init(&ctl->tmem_empty[b], 2 * kEpiWarps);
+        }
+        mbar_init(&ctl->drain, 1);
+        ctl->abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tm_a);
+        prefetch_tmap(&tm_b);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(&ctl->tmem_base, 512);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();
+    tc_fence_after();
+    const uint32_t tmem_base = ctl->tmem_base;
+
+    if (!is_epi) {
+        if (kRegSplit) setmaxnreg_dec<kRegOther>();
+        if (warp == 0) {
+            if (lane == 0) {
+                // ---------------- TMA producer: FP32 tiles of this CTA's A rows and B columns ----------------
+                long it = 0;
+                bool ok = true;
+                for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+                    int mb2, nb;
+                    tile_coords_f(t, p.num_m2, p.num_n, mb2, nb);
+                    const int a_row = mb2 * 2 * kBM + (int)rank * kBM;
+                    const int b_col = nb * kBN + (int)rank * kBNH;
+                    for (int kb = 0; kb < p.nk; ++kb, ++it) {
+                        const int s = (int)(it % kF32Stages);
+                        const uint32_t ph = (uint32_t)((it / kF32Stages) & 1);
+                        if (!mbar_wait(&ctl->f32_empty[s], ph ^ 1u, abort, p.err, kErrTimeoutProducer)) { ok = false; break; }
+                        uint8_t* st = f32 + s * kF32Stage;
+                        mbar_arrive_expect_tx(&ctl->f32_full[s], kF32Stage);
+                        tma_load_2d(st, &tm_a, &ctl->f32_full[s], kb * kBK, a_row);
+                        tma_load_2d(st + kF32A, &tm_b, &ctl->f32_full[s], b_col, kb * kBK);
+                    }
+                }
+                if (!ok) {
+                    abort_pair_f(ctl, peer);
+                    const long first = it > kF32Stages ? it - kF32Stages : 0;
+                    for (long j = first; j < it; ++j)
+                        drain_wait_f(&ctl->f32_full[j % kF32Stages], (uint32_t)((j / kF32Stages) & 1));
+                }
+            }
+        } else if (warp == 1) {
+            if (lane == 0 && leader) {
+                // ---------------- leader: pair MMA issuer ----------------
+                long it = 0, ch = 0;
+                bool ok = true;
+                for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+                    for (int kb0 = 0; kb0 < p.nk && ok; kb0 += kChunkKB, ++ch) {
+                        const int b = (int)(ch & 1);
+                        const uint32_t bph = (uint32_t)((ch >> 1) & 1);
+                        if (!mbar_wait_cluster(&ctl->tmem_empty[b], bph ^ 1u, abort, p.err, kErrTimeoutMma)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t d = tmem_base + (uint32_t)(b * kAccCols);
+                        const int kb1 = min(p.nk, kb0 + kChunkKB);
+                        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                            const int s = (int)(it % kBfStages);
+                            const uint32_t ph = (uint32_t)((it / kBfStages) & 1);
+                            if (!mbar_wait_cluster(&ctl->bf_full[s], ph, abort, p.err, kErrTimeoutMma)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            const uint32_t st = smem_u32(bf + s * kBfStage);
+                            const uint64_t a_hi = sdesc_kmajor(st, 64);
+                            const uint64_t a_lo = sdesc_kmajor(st + kBfA, 64);
+                            const uint64_t b_hi = sdesc_kmajor(st + 2 * kBfA, 64);
+                            const uint64_t b_lo = sdesc_kmajor(st + 2 * kBfA + kBfB, 64);
+    #pragma unroll
+                            for (int ks = 0; ks < kBK / 16; ++ks) {
+                                const uint64_t adv = (uint64_t)(ks * 32) >> 4;
+                                const uint32_t acc = (kb != kb0 || ks != 0) ? 1u : 0u;
+                                mma_f16_ss_pair(d, a_lo + adv, b_hi + adv, kIdesc, acc);
+                                mma_f16_ss_pair(d, a_hi + adv, b_lo + adv, kIdesc, 1u);
+                                mma_f16_ss_pair(d, a_hi + adv, b_hi + adv, kIdesc, 1u);
+                            }
+                            mma_commit_pair_both(&ctl->bf_empty[s], (uint16_t)0x3);
+                        }
+                        if (!ok) break;
+                        mma_commit_pair_both(&ctl->tmem_full[b], (uint16_t)0x3);
+                    }
+                }
+                if (!ok) {
+                    abort_pair_f(ctl, peer);
+                    mma_commit_pair(&ctl->drain);
+                    drain_wait_f(&ctl->drain, 0);
+                }
+            }
+        } else {
+            // ---------------- converters: FP32 stage -> bf16 hi/lo stage (both operands K-major) ----------------
+            const int ct = (warp < kEpiFirst ? warp - 2 : warp - 2 - kEpiWarps) * 32 + lane;   // 0 .. kConvThreads-1
+            const uint32_t lead_bf_full0 = mapa_shared(smem_u32(&ctl->bf_full[0]), 0);
+            constexpr int kPer = (1024 + kConvThreads - 1) / kConvThreads;   // items per thread and k-block
+            constexpr int kBatch = 3;                                        // items loaded before any is stored
+            long it = 0;
+            bool ok = true;
+            for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+                for (int kb = 0; kb < p.nk; ++kb, ++it) {
+                    const int s = (int)(it % kF32Stages);
+                    const uint32_t ph = (uint32_t)((it / kF32Stages) & 1);
+                    const int q = (int)(it % kBfStages);
+                    const uint32_t qh = (uint32_t)((it / kBfStages) & 1);
+                    bool ready = mbar_wait(&ctl->f32_full[s], ph, abort, p.err, kErrTimeoutConvert) &&
+                                 mbar_wait_cluster(&ctl->bf_empty[q], qh ^ 1u, abort, p.err, kErrTimeoutConvert);
+                    if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
+                    const uint8_t* fa = f32 + s * kF32Stage;   // A: 128 rows x 32 floats, 128-byte swizzle
+                    const float* fb = reinterpret_cast<const float*>(fa + kF32A);   // B: 32 rows x 128 floats
+                    uint8_t* ob = bf + q * kBfStage;
+                    // 1024 items of 8 values: A rows x 4 k-groups (0..511), then B columns x 4 k-groups
+                    // (512..1023). A warp's 32 items are consecutive, so no warp mixes A and B; the 64-byte
+                    // swizzle makes both store patterns (4 lanes per A row, one lane per B column) conflict-free.
+    #pragma unroll
+                    for (int i0 = 0; i0 < kPer; i0 += kBatch) {
+                        float x[kBatch][8];
+                        uint32_t dst[kBatch];   // offset of the hi chunk in the stage; lo is kBfA further
+    #pragma unroll
+                        for (int i = 0; i < kBatch; ++i) {
+                            const int item = ct + (i0 + i) * kConvThreads;
+                            if (i0 + i >= kPer || item >= 1024) continue;
+                            if (item < 512) {
+                                const int r = item >> 2, g = item & 3;
+                                const uint8_t* row = fa + r * 128;
+                                const float4 u = *reinterpret_cast<const float4*>(row + (((2 * g) ^ (r & 7)) << 4));
+                                const float4 v = *reinterpret_cast<const float4*>(row + (((2 * g + 1) ^ (r & 7)) << 4));
+                                x[i][0] = u.x; x[i][1] = u.y; x[i][2] = u.z; x[i][3] = u.w;
+                                x[i][4] = v.x; x[i][5] = v.y; x[i][6] = v.z; x[i][7] = v.w;
+                                dst[i] = sw64(r, g);
+                            } else {
+                                const int i2 = item - 512;
+                                const int r = i2 & (kBNH - 1), g = i2 >> 7;   // column n of this CTA's B, k-group
+    #pragma unroll
+                                for (int j = 0; j < 8; ++j) x[i][j] = fb[(8 * g + j) * kBNH + r];
+                                dst[i] = (uint32_t)(2 * kBfA) + sw64(r, g);
+                            }
+                        }
+    #pragma unroll
+                        for (int i = 0; i < kBatch; ++i) {
+                            const int item = ct + (i0 + i) * kConvThreads;
+                            if (i0 + i >= kPer || item >= 1024) continue;
+                            uint4 hv, lv;
+                            split8(x[i], hv, lv);
+                            *reinterpret_cast<uint4*>(ob + dst[i]) = hv;
+                            *reinterpret_cast<uint4*>(ob + dst[i] + kBfA) = lv;
+                        }
+                    }
+                    // each thread makes its slice writes visible to the tensor cores' async proxy; the warp
+                    // barrier orders all lanes' writes before lane 0's release-arrive on the leader
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive_cluster(lead_bf_full0 + (uint32_t)(q * sizeof(uint64_t)));
+                        mbar_arrive(&ctl->f32_empty[s]);
+                    }
+                }
+            }
+            if (!ok && lane == 0) abort_pair_f(ctl, peer);
+        }
+    } else {
+        if (kRegSplit) setmaxnreg_inc<kRegEpi>();
+        // ---------------- promotion + epilogue ----------------
+        const int sp = warp & 3;
+        const int half = (warp - kEpiFirst) >> 2;
+        const int row_in_tile = (int)rank * kBM + sp * 32 + lane;
+        const int col0 = half * kHalf;
+        const uint32_t lane_off = (uint32_t)(sp * 32) << 16;
+        const uint32_t lead_te0 = mapa_shared(smem_u32(&ctl->tmem_empty[0]), 0);
+        long ch = 0;
+        bool ok = true;
+        for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+            int mb2, nb;
+            tile_coords_f(t, p.num_m2, p.num_n, mb2, nb);
+            float sum[kHalf];
+#pragma unroll
+            for (int j = 0; j < kHalf; ++j) sum[j] = 0.f;
+            for (int c = 0; c < nchunks; ++c, ++ch) {
+                const int b = (int)(ch & 1);
+                const uint32_t bph = (uint32_t)((ch >> 1) & 1);
+                bool ready = mbar_wait_cluster(&ctl->tmem_full[b], bph, abort, p.err, kErrTimeoutEpilogue);
+                if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t tb = tmem_base + lane_off + (uint32_t)(b * kAccCols + col0);
+#pragma unroll
+                for (int q = 0; q < kHalf / 16; ++q) {
+                    uint32_t r[16];
+                    tmem_ld_32x32b_x16(tb + (uint32_t)(q * 16), r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) sum[q * 16 + j] += __uint_as_float(r[j]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(lead_te0 + (uint32_t)(b * sizeof(uint64_t)));
+            }
+            if (!ok) break;
+            const int m = mb2 * 2 * kBM + row_in_tile;
+            if (m < p.M) {
+                const int n0 = nb * kBN + col0;
+                if (p.C64) {
+                    double* crow = p.C64 + (size_t)m * p.ldc64;
+#pragma unroll
+                    for (int j = 0; j < kHalf; ++j)
+                        if (n0 + j < p.N) crow[n0 + j] = (double)sum[j];
+                } else {
+                    float* crow = p.C + (size_t)m * p.ldc;
+                    const bool vec = (n0 + kHalf <= p.N) && ((p.ldc & 3) == 0) &&
+                                     ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
+                    if (vec) {
+                        float4* c4 = reinterpret_cast<float4*>(crow + n0);
+#pragma unroll
+                        for (int j = 0; j < kHalf / 4; ++j)
+                            c4[j] = make_float4(sum[4 * j], sum[4 * j + 1], sum[4 * j + 2], sum[4 * j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < kHalf; ++j)
+                            if (n0 + j < p.N) crow[n0 + j] = sum[j];
+                    }
+                }
+            }
+        }
+        if (!ok && lane == 0) abort_pair_f(ctl, peer);
+    }
+
+    tc_fence_before();
+    cluster_sync_all();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, 512);
+    }
+}
+
+}  // namespace
+
+// A: M x K row-major FP32 (lda), B: K x N row-major FP32 (ldb); needs lda % 4 == ldb % 4 == 0 and 16-byte
+// aligned A, B (TMA). Returns cudaErrorNotSupported when those do not hold, so the caller can pre-split instead.
+int launch_tc_fused(const float* A, long lda, const float* B, long ldb, int M, int N, long K, float* C, long ldc,
+                    double* C64, long ldc64, unsigned* err, int num_sms, void* stream) {
+    if ((lda & 3) || (ldb & 3) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
+        return (int)cudaErrorNotSupported;
+    PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+    if (!tc_get_encode(&enc)) return (int)cudaErrorNotSupported;
+    CUtensorMap ta, tb;
+    {
+        cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+        cuuint64_t strides[1] = {(cuuint64_t)lda * 4};
+        cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
+        cuuint32_t estr[2] = {1, 1};
+        if (enc(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(A), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return (int)cudaErrorInvalidValue;
+    }
+    {
+        cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)K};
+        cuuint64_t strides[1] = {(cuuint64_t)ldb * 4};
+        cuuint32_t box[2] = {(cuuint32_t)kBNH, (cuuint32_t)kBK};
+        cuuint32_t estr[2] = {1, 1};
+        if (enc(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(B), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return (int)cudaErrorInvalidValue;
+    }
+    cudaError_t e = cudaFuncSetAttribute(k_tc_fused, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return (int)e;
+    KParamsF p;
+    p.M = M;
+    p.N = N;
+    p.num_m2 = (M + 2 * kBM - 1) / (2 * kBM);
+    p.num_n = (N + kBN - 1) / kBN;
+    p.nk = (int)((K + kBK - 1) / kBK);
+    p.C = C;
+    p.ldc = ldc;
+    p.C64 = C64;
+    p.ldc64 = ldc64;
+    p.err = err;
+    const int tiles = p.num_m2 * p.num_n;
+
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = (cudaStream_t)stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(2, 1, 1);
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, k_tc_fused, &cfg);
+    if (e != cudaSuccess || clusters <= 0) {
+        cudaGetLastError();
+        clusters = (num_sms > 0 ? num_sms : 148) / 2;
+    }
+    if (clusters > tiles) clusters = tiles;
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    e = cudaLaunchKernelEx(&cfg, k_tc_fused, ta, tb, p);
+    count_launch();
+    if (e != cudaSuccess) return (int)e;
+    return (int)cudaGetLastError();
+}
+
+}  // namespace emu

@@ -78,6 +78,7 @@ struct Ctl {
 
 struct KParams {
     int M, N, num_m, num_n, nk;
+    int kpb;   // k-blocks per K panel of the slices
     float* C; long ldc;
     double* C64; long ldc64;
     const int* row_exp; const int* col_exp;
@@ -160,10 +161,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!mbar_wait(&ctl->empty[s], ph ^ 1u, abort, p.err, kErrTimeoutProducer)) { ok = false; break; }
                     uint8_t* st = smem + s * C_::STAGE_BYTES;
                     mbar_arrive_expect_tx(&ctl->full[s], C_::STAGE_BYTES);
-                    tma_load_2d(st, &tm_ahi, &ctl->full[s], kb * kBK, mb * kBM);
-                    tma_load_2d(st + C_::A_BYTES, &tm_alo, &ctl->full[s], kb * kBK, mb * kBM);
-                    tma_load_2d(st + 2 * C_::A_BYTES, &tm_bhi, &ctl->full[s], kb * kBK, nb * C_::BN);
-                    tma_load_2d(st + 2 * C_::A_BYTES + C_::B_BYTES, &tm_blo, &ctl->full[s], kb * kBK, nb * C_::BN);
+                    const int kz = kb / p.kpb, kx = (kb - kz * p.kpb) * kBK;
+                    tma_load_3d(st, &tm_ahi, &ctl->full[s], kx, mb * kBM, kz);
+                    tma_load_3d(st + C_::A_BYTES, &tm_alo, &ctl->full[s], kx, mb * kBM, kz);
+                    tma_load_3d(st + 2 * C_::A_BYTES, &tm_bhi, &ctl->full[s], kx, nb * C_::BN, kz);
+                    tma_load_3d(st + 2 * C_::A_BYTES + C_::B_BYTES, &tm_blo, &ctl->full[s], kx, nb * C_::BN, kz);
                 }
             }
             if (!ok) {
@@ -322,13 +324,14 @@ bool get_encode() {
     return g_encode != nullptr;
 }
 
-// rows x Kp 16-bit matrix, K-major; box = kBK (K) x box_rows, swizzled by the k-block's row width.
-bool make_tmap(CUtensorMap* m, const uint16_t* base, long Kp, int rows, int box_rows) {
-    cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)Kp * 2};
-    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(base), dims, strides, box,
+// 16-bit slice of `rows` rows in K panels ([Kp / KP][rows][KP]), K-major; box = kBK (K) x box_rows x 1 panel,
+// swizzled by the k-block's row width.
+bool make_tmap(CUtensorMap* m, const uint16_t* base, long Kp, long KP, int rows, int box_rows) {
+    cuuint64_t dims[3] = {(cuuint64_t)KP, (cuuint64_t)rows, (cuuint64_t)(Kp / KP)};
+    cuuint64_t strides[2] = {(cuuint64_t)KP * 2, (cuuint64_t)rows * (cuuint64_t)KP * 2};
+    cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint16_t*>(base), dims, strides, box,
                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                           kSwizzleBytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -339,10 +342,11 @@ template <bool FP16>
 int launch_impl(const TcGemmArgs& a, void* stream) {
     using C_ = Cfg<FP16>;
     if (!get_encode()) return (int)cudaErrorNotSupported;
-    if (a.Mp % kBM || a.Np % C_::BN || a.Kp % kBK || a.Kp <= 0) return (int)cudaErrorInvalidValue;
+    if (a.Mp % kBM || a.Np % C_::BN || a.Kp % kBK || a.Kp <= 0 || a.KP <= 0 || a.KP % kBK || a.Kp % a.KP)
+        return (int)cudaErrorInvalidValue;
     CUtensorMap tah, tal, tbh, tbl;
-    if (!make_tmap(&tah, a.a_hi, a.Kp, a.Mp, kBM) || !make_tmap(&tal, a.a_lo, a.Kp, a.Mp, kBM) ||
-        !make_tmap(&tbh, a.b_hi, a.Kp, a.Np, C_::BN) || !make_tmap(&tbl, a.b_lo, a.Kp, a.Np, C_::BN))
+    if (!make_tmap(&tah, a.a_hi, a.Kp, a.KP, a.Mp, kBM) || !make_tmap(&tal, a.a_lo, a.Kp, a.KP, a.Mp, kBM) ||
+        !make_tmap(&tbh, a.b_hi, a.Kp, a.KP, a.Np, C_::BN) || !make_tmap(&tbl, a.b_lo, a.Kp, a.KP, a.Np, C_::BN))
         return (int)cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(k_tc_gemm<FP16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C_::SMEM_BYTES);
@@ -353,6 +357,7 @@ int launch_impl(const TcGemmArgs& a, void* stream) {
     p.num_m = a.Mp / kBM;
     p.num_n = a.Np / C_::BN;
     p.nk = (int)(a.Kp / kBK);
+    p.kpb = (int)(a.KP / kBK);
     p.C = a.C;
     p.ldc = a.ldc;
     p.C64 = a.C64;

@@ -64,6 +64,7 @@ struct Ctl2 {
 
 struct KParams2 {
     int M, N, num_m2, num_n, nk;   // num_m2: row blocks of 256
+    int kpb;                       // k-blocks per K panel of the slices
     float* C; long ldc;
     double* C64; long ldc64;
     const int* row_exp; const int* col_exp;
@@ -164,10 +165,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (leader) mbar_arrive_expect_tx(&ctl->full[s], 2 * C_::STAGE_BYTES);
                     const uint32_t fb = lead_full0 + (uint32_t)(s * sizeof(uint64_t));
                     uint8_t* st = smem + s * C_::STAGE_BYTES;
-                    tma_load_2d_pair(st, &tm_ahi, fb, kb * kBK, a_row);
-                    tma_load_2d_pair(st + C_::A_BYTES, &tm_alo, fb, kb * kBK, a_row);
-                    tma_load_2d_pair(st + 2 * C_::A_BYTES, &tm_bhi, fb, kb * kBK, b_row);
-                    tma_load_2d_pair(st + 2 * C_::A_BYTES + C_::B_BYTES, &tm_blo, fb, kb * kBK, b_row);
+                    const int kz = kb / p.kpb, kx = (kb - kz * p.kpb) * kBK;
+                    tma_load_3d_pair(st, &tm_ahi, fb, kx, a_row, kz);
+                    tma_load_3d_pair(st + C_::A_BYTES, &tm_alo, fb, kx, a_row, kz);
+                    tma_load_3d_pair(st + 2 * C_::A_BYTES, &tm_bhi, fb, kx, b_row, kz);
+                    tma_load_3d_pair(st + 2 * C_::A_BYTES + C_::B_BYTES, &tm_blo, fb, kx, b_row, kz);
                 }
             }
             if (!ok) {
@@ -319,13 +321,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-bool make_tmap2(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* m, const uint16_t* base, long Kp, int rows,
-                int box_rows) {
-    cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)Kp * 2};
-    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(base), dims, strides, box, estr,
+// 16-bit slice in K panels ([Kp / KP][rows][KP]); box = kBK (K) x box_rows x 1 panel, 128-byte swizzle.
+bool make_tmap2(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* m, const uint16_t* base, long Kp, long KP,
+                int rows, int box_rows) {
+    cuuint64_t dims[3] = {(cuuint64_t)KP, (cuuint64_t)rows, (cuuint64_t)(Kp / KP)};
+    cuuint64_t strides[2] = {(cuuint64_t)KP * 2, (cuuint64_t)rows * (cuuint64_t)KP * 2};
+    cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint16_t*>(base), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -335,10 +338,12 @@ int launch_pair_impl(const TcGemmArgs& a, void* stream) {
     using C_ = Cfg2<FP16>;
     PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
     if (!tc_get_encode(&enc)) return (int)cudaErrorNotSupported;
-    if (a.Mp % (2 * kBM) || a.Np % C_::BN || a.Kp % kBK || a.Kp <= 0) return (int)cudaErrorInvalidValue;
+    if (a.Mp % (2 * kBM) || a.Np % C_::BN || a.Kp % kBK || a.Kp <= 0 || a.KP <= 0 || a.KP % kBK || a.Kp % a.KP)
+        return (int)cudaErrorInvalidValue;
     CUtensorMap tah, tal, tbh, tbl;
-    if (!make_tmap2(enc, &tah, a.a_hi, a.Kp, a.Mp, kBM) || !make_tmap2(enc, &tal, a.a_lo, a.Kp, a.Mp, kBM) ||
-        !make_tmap2(enc, &tbh, a.b_hi, a.Kp, a.Np, C_::BNH) || !make_tmap2(enc, &tbl, a.b_lo, a.Kp, a.Np, C_::BNH))
+    if (!make_tmap2(enc, &tah, a.a_hi, a.Kp, a.KP, a.Mp, kBM) || !make_tmap2(enc, &tal, a.a_lo, a.Kp, a.KP, a.Mp, kBM) ||
+        !make_tmap2(enc, &tbh, a.b_hi, a.Kp, a.KP, a.Np, C_::BNH) ||
+        !make_tmap2(enc, &tbl, a.b_lo, a.Kp, a.KP, a.Np, C_::BNH))
         return (int)cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(k_tc_gemm_pair<FP16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C_::SMEM_BYTES);
@@ -349,6 +354,7 @@ int launch_pair_impl(const TcGemmArgs& a, void* stream) {
     p.num_m2 = a.Mp / (2 * kBM);
     p.num_n = a.Np / C_::BN;
     p.nk = (int)(a.Kp / kBK);
+    p.kpb = (int)(a.KP / kBK);
     p.C = a.C;
     p.ldc = a.ldc;
     p.C64 = a.C64;

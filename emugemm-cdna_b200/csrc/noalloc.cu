@@ -11,7 +11,8 @@
 //   - The scratch array holds 64 MiB on every GPU that loads this library, from the moment the module is
 //     loaded (at the latest, this entry point's first call on the device) until the process exits. It
 //     fits (Mp + Np) * Kp <= 16 Mi, where Mp = M rounded up to 128, Np = N rounded up to 256 and
-//     Kp = K rounded up to 64 (for example M = N = 2048 with K up to 4096); larger problems are rejected
+//     Kp = K rounded up to 64, or to 8192 beyond K = 16384 (for example M = N = 2048 with K up to 4096);
+//     larger problems are rejected
 //     with EMUGEMM_STATUS_INVALID_SIZE and a message on stderr.
 //   - Every call on a device uses the same array. Calls whose kernels overlap on the GPU (different
 //     streams, or different host threads without ordering) race on it and produce wrong results; callers
@@ -97,7 +98,7 @@ extern "C" emugemm_status_t emugemm_sgemm_bf16x3_noalloc(int M, int N, long K, c
                    : EMUGEMM_STATUS_INTERNAL_ERROR;
     }
     const int BN = tc_gemm_bn(0);
-    const long Mp = round_up(M, 128), Np = round_up(N, BN), Kp = round_up(K, 64);
+    const long Mp = round_up(M, 128), Np = round_up(N, BN), Kp = slice_kp(K), KP = slice_panel(Kp);
     const size_t need = (size_t)(Mp + Np) * (size_t)Kp * 2 /*slices*/ * 2 /*bytes*/;
     if (need > kNoAllocScratchBytes) {
         std::fprintf(stderr,
@@ -115,12 +116,12 @@ extern "C" emugemm_status_t emugemm_sgemm_bf16x3_noalloc(int M, int N, long K, c
     uint16_t* b_lo = b_hi + (size_t)Np * Kp;
     unsigned* status = reinterpret_cast<unsigned*>(base + kNoAllocScratchBytes);
     if (cudaMemsetAsync(status, 0, sizeof(unsigned), st) != cudaSuccess) return EMUGEMM_STATUS_INTERNAL_ERROR;
-    int e = launch_split_rows(A, M, K, K, (int)Mp, Kp, 0, nullptr, a_hi, a_lo, stream);
-    if (!e) e = launch_split_cols(B, K, N, N, (int)Np, Kp, 0, nullptr, b_hi, b_lo, stream);
+    int e = launch_split_rows(A, M, K, K, (int)Mp, Kp, KP, 0, nullptr, a_hi, a_lo, stream);
+    if (!e) e = launch_split_cols(B, K, N, N, (int)Np, Kp, KP, 0, nullptr, b_hi, b_lo, stream);
     if (e) return EMUGEMM_STATUS_INTERNAL_ERROR;
     TcGemmArgs t;
     t.a_hi = a_hi; t.a_lo = a_lo; t.b_hi = b_hi; t.b_lo = b_lo;
-    t.M = M; t.N = N; t.Mp = (int)Mp; t.Np = (int)Np; t.Kp = Kp;
+    t.M = M; t.N = N; t.Mp = (int)Mp; t.Np = (int)Np; t.Kp = Kp; t.KP = KP;
     t.C = C; t.ldc = N; t.C64 = nullptr; t.ldc64 = 0;
     t.fp16 = 0;
     t.row_exp = nullptr; t.col_exp = nullptr;

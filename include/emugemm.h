@@ -195,7 +195,8 @@ emugemm_status_t emugemm_profile_end(emugemm_handle_t handle, double* ms_by_kind
    device's memory, latency-critical paths that must not risk an allocation mid-run -- it computes the same
    product as emugemm_sgemm with force_scheme = EMU_SCHEME_BF16X3, with the slices of A and B held in a fixed
    64 MiB device array that every GPU loading the library keeps until the process exits. Limit:
-   (Mp + Np) * Kp <= 16 Mi with Mp, Np, Kp = M, N, K rounded up to 128, 256, 64 (e.g. M = N = 2048, K <= 4096);
+   (Mp + Np) * Kp <= 16 Mi with Mp, Np, Kp = M, N, K rounded up to 128, 256, 64 (K: to 8192 beyond 16384;
+   e.g. M = N = 2048, K <= 4096);
    larger sizes return EMUGEMM_STATUS_INVALID_SIZE. All calls on a device share the array: calls that overlap
    on the GPU race, so order them (e.g. one stream). The first call on a device looks the array up with
    cudaGetSymbolAddress; make that first call before any stream capture. Row-major, device pointers,

@@ -130,8 +130,9 @@ def test_auto_chunked_plan_runs_chunked(cuda, handle):
 
 
 # ---------------------------------------------------------------------------------- tensor-core 3-product
+# K above 16384 stores the slices in K panels of 8192 (3 and 5 panels below, the last one partly padding)
 TC_SHAPES = [(128, 256, 64), (256, 512, 1024), (200, 300, 500), (1, 1, 1), (129, 257, 65), (1024, 1024, 1024),
-             (384, 768, 4096)]
+             (384, 768, 4096), (130, 260, 20000), (64, 96, 40000)]
 
 
 def _accum_bound(K):
@@ -157,7 +158,7 @@ def test_bf16x3_matches_slice_products(cuda, handle, shape):
     assert d <= _accum_bound(K)
 
 
-@pytest.mark.parametrize("shape", [(128, 128, 64), (200, 300, 500), (512, 256, 2048), (1, 1, 1)])
+@pytest.mark.parametrize("shape", [(128, 128, 64), (200, 300, 500), (512, 256, 2048), (1, 1, 1), (64, 128, 24000)])
 def test_fp16x3_scaled_matches_slice_products(cuda, handle, shape):
     torch = cuda
     M, N, K = shape
@@ -324,7 +325,8 @@ def test_a_is_reused_reuses_the_split(cuda, handle):
 
 
 @pytest.mark.parametrize("force", [emugemm.BF16X3, emugemm.FP16X3])
-@pytest.mark.parametrize("shape", [(256, 256, 128), (300, 520, 1000), (1024, 768, 2048), (1, 1, 1), (2048, 2048, 512)])
+@pytest.mark.parametrize("shape", [(256, 256, 128), (300, 520, 1000), (1024, 768, 2048), (1, 1, 1), (2048, 2048, 512),
+                                   (256, 256, 20000)])
 def test_pair_kernel_matches_single_cta_kernel(cuda, handle, monkeypatch, force, shape):
     """The CTA-pair kernel (cta_group::2) computes every output from the same slices and k-steps as the
     single-CTA kernel: identical bits."""
@@ -339,3 +341,48 @@ def test_pair_kernel_matches_single_cta_kernel(cuda, handle, monkeypatch, force,
         out[variant] = C
     assert np.isfinite(out["pair"]).all()
     assert np.array_equal(out["pair"], out["single"])
+
+
+@pytest.mark.parametrize("shape", [(256, 256, 128), (260, 516, 1004), (1024, 768, 2048), (2048, 2048, 512),
+                                   (384, 264, 96), (1, 1, 1), (33, 65, 129)])
+@pytest.mark.parametrize("gen", ["normal", "wide_range"])
+def test_fused_split_kernel_matches_presplit(cuda, handle, monkeypatch, shape, gen):
+    """bf16x3 with the split fused into the CTA-pair GEMM (FP32 tiles by TMA, hi/lo made in shared memory)
+    uses the same slices, k-steps and promotion points as the pre-split kernels: identical bits. Leading
+    dimensions TMA cannot address (not a multiple of 4 floats) fall back to the pre-split path."""
+    torch = cuda
+    M, N, K = shape
+    if gen == "normal":
+        A = datagen.normal((M, K), 70 + M)
+        B = datagen.normal((K, N), 71 + N)
+    else:
+        A = datagen.wide_range((M, K), 72 + M, emax=20)
+        B = datagen.wide_range((K, N), 73 + N, emax=20)
+    out, splits = {}, {}
+    for variant in ("pair", "fused"):
+        monkeypatch.setenv("EMUGEMM_TC_KERNEL", variant)
+        handle.profile_begin()
+        C, p, _ = run_sgemm(torch, handle, A, B, force=emugemm.BF16X3, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+        splits[variant] = handle.profile_end()["split"][1]
+        out[variant] = C
+    assert np.isfinite(out["fused"]).all()
+    assert np.array_equal(out["fused"], out["pair"])
+    fused_ran = K % 4 == 0 and N % 4 == 0
+    assert splits["fused"] == (0 if fused_ran else 1)   # one profiled scope covers both splits
+
+
+def test_fused_split_kernel_partial_f64(cuda, handle, monkeypatch):
+    """The FP64 partial output of the fused kernel (K-split building block) equals the pre-split kernel's."""
+    torch = cuda
+    M, N, K = 300, 260, 1536
+    A = dev(torch, datagen.normal((M, K), 80))
+    B = dev(torch, datagen.normal((K, N), 81))
+    out = {}
+    for variant in ("pair", "fused"):
+        monkeypatch.setenv("EMUGEMM_TC_KERNEL", variant)
+        P = torch.full((M, N), float("nan"), dtype=torch.float64, device="cuda")
+        handle.partial_f64(M, N, K, A, K, B, N, P, emugemm.BF16X3, 1)
+        handle.sync()
+        out[variant] = P.cpu().numpy()
+    assert np.isfinite(out["fused"]).all()
+    assert np.array_equal(out["fused"], out["pair"])
