@@ -17,7 +17,11 @@ is broadcast from rank 0 with NCCL inside every step (weak scaling).
 Other workloads (--workload): `rows` = one S^3 product with the rows of A split over the ranks and B broadcast
 from rank 0 in column panels (strong scaling; S = 32768 is the sharded multi-GPU configuration); `ksplit` =
 S x S x --k with K split over the ranks, FP64 partial products summed by NCCL and rounded once (S = 4096,
-K = 1048576 is the long-K multi-GPU configuration).
+K = 1048576 is the long-K multi-GPU configuration); `chunked` = FP32_CHUNKED at S x S x --k with --chunks
+K-chunks (FP32 FMA chains, chunk sums in FP64; S = 256, K = 262144 is the long-K accumulation configuration),
+U[-1,1] inputs, one partial + rounding per step; `rho` = the cancellation-ratio probe (--probes Hutchinson
+vectors) on an S x S x S product, one emugemm_estimate_rho per step. `chunked` and `rho` run as independent
+replicas under N > 1.
 """
 from __future__ import annotations
 
@@ -50,10 +54,12 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
-    ap.add_argument("--workload", default="square", choices=["square", "rows", "ksplit"],
+    ap.add_argument("--workload", default="square", choices=["square", "rows", "ksplit", "chunked", "rho"],
                     help="square: S^3 per GPU (weak); rows: one S^3 product, rows over GPUs; "
-                         "ksplit: S x S x --k, K over GPUs")
-    ap.add_argument("--k", type=int, default=1048576, help="K of the ksplit workload")
+                         "ksplit: S x S x --k, K over GPUs; chunked: FP32_CHUNKED S x S x --k; rho: rho probe S^3")
+    ap.add_argument("--k", type=int, default=1048576, help="K of the ksplit and chunked workloads")
+    ap.add_argument("--chunks", type=int, default=4, help="K-chunks of the chunked workload")
+    ap.add_argument("--probes", type=int, default=64, help="probe vectors of the rho workload")
     return ap.parse_args()
 
 
@@ -64,6 +70,15 @@ def peaks():
         return float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), \
             float(d["hbm_gbs"]), "measured"
     return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def ffma_peak() -> tuple[float, str]:
+    """Nominal FP32 FMA throughput: 148 SMs x 128 FP32 lanes x 2 FLOP per clock at the maximum SM clock."""
+    mhz = 1965.0
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        mhz = float(json.loads(p.read_text()).get("sm_max_mhz", mhz))
+    return 148 * 128 * 2 * mhz * 1e6 / 1e12, f"nominal FFMA (148 SMs x 128 lanes x 2 FLOP x {mhz:.0f} MHz)"
 
 
 class ClockSampler:
@@ -282,6 +297,36 @@ def ours(args) -> None:
                 multigpu.row_sharded(A, B, C, src=0, panel=(N + 1) // 2, handle=h, scheme=scheme)
             else:
                 h.sgemm(m_loc, N, K, A, B, C, force=scheme, hints=hints())
+    elif wl == "chunked":
+        # FP32_CHUNKED: M = N = S, K = args.k in args.chunks chunks; FP32 FMA chains per chunk, chunk sums in FP64,
+        # one rounding to FP32 (the partial + reduce pair that emugemm_sgemm runs for a chunked plan)
+        M, N, K = S, S, args.k
+        m_loc, k_loc = M, K
+        A = torch.rand((M, K), device="cuda", generator=gen) * 2 - 1
+        B = torch.rand((K, N), device="cuda", generator=gen) * 2 - 1
+        C = torch.empty((M, N), device="cuda")
+        P = torch.empty((M, N), dtype=torch.float64, device="cuda")
+        total_flop = 2.0 * M * N * K * world
+        scaling = "weak"
+        desc = f"FP32_CHUNKED {M}x{N}x{K}, c={args.chunks}" + (f", {world} independent replicas" if world > 1 else "")
+
+        def step():
+            h.partial_f64(M, N, K, A, K, B, N, P, 2, args.chunks)
+            h.reduce_f64(M, N, 1, P, C)
+    elif wl == "rho":
+        # rho = ||(|A||B|)||_F / ||AB||_F estimated with args.probes Rademacher vectors (signed and |.| products)
+        M, N, K = S, S, S
+        m_loc, k_loc = M, K
+        A = wide((M, K))
+        B = wide((K, N))
+        C = None
+        total_flop = 4.0 * args.probes * K * (M + N) * world
+        scaling = "weak"
+        desc = f"rho probe, {args.probes} probes, {S}^3" + (f", {world} independent replicas" if world > 1 else "")
+        rho_val = []
+
+        def step():
+            rho_val.append(h.estimate_rho(M, N, K, A, B, args.probes))
     else:
         # M = N = S, K = args.k split over the ranks; FP64 partials summed by NCCL, one rounding (strong scaling)
         M, N, K = S, S, args.k
@@ -330,17 +375,38 @@ def ours(args) -> None:
     ms_step = ms_total / args.steps
     value = total_flop / (ms_step * 1e-3) / 1e12
 
-    # dominant kernel: the tensor-core 3-product GEMM (3 * 2 * m * n * k tensor FLOPs per rank and step)
-    gemm_ms, gemm_n = prof["tc_gemm"]
+    # dominant kernel: the tensor-core 3-product GEMM (3 * 2 * m * n * k tensor FLOPs per rank and step), the FP32
+    # SIMT GEMM (2 * m * n * k) for the chunked workload, the skinny probe products (4 * P * K * (M + N)) for rho
+    if wl == "chunked":
+        kern_key, kern_name, bound = "fp32_gemm", "k_fp32_gemm", "fp32"
+        rank_tensor_flop = 2.0 * m_loc * N * k_loc
+    elif wl == "rho":
+        kern_key, kern_name, bound = "rho", "k_skinny", "fp32"
+        rank_tensor_flop = 4.0 * args.probes * K * (M + N)
+    else:
+        kern_key, kern_name, bound = "tc_gemm", "k_tc_gemm", "tensor"
+        rank_tensor_flop = 3 * 2.0 * m_loc * N * k_loc
+    gemm_ms, gemm_n = prof[kern_key]
     gemm_avg = gemm_ms / max(gemm_n, 1)
     launches_per_step = max(1, gemm_n // max(1, args.steps))
-    rank_tensor_flop = 3 * 2.0 * m_loc * N * k_loc
     tensor_tflops = (rank_tensor_flop / launches_per_step / (gemm_avg * 1e-3) / 1e12) if gemm_n else None
     burst, sustained, hbm, src = peaks()
     # a timed loop of more than half a second runs under the power cap: compare with the sustained peak
     long_loop = ms_total > 500.0
     peak = sustained if long_loop else burst
     peak_name = "bf16_tflops_sustained" if long_loop else "bf16_tflops"
+    peak_source = f"{peak_name} ({src})"
+    if bound == "fp32":
+        burst, peak_source = ffma_peak()
+        peak = burst
+    extra = {}
+    if wl == "rho":
+        # the probe reads A and B once each; its GB/s against the HBM copy bandwidth, for reference
+        rho_ms = prof["rho"][0] / max(1, args.steps)
+        extra = {"rho_probe": {"rho": rho_val[-1] if rho_val else None, "ms": rho_ms,
+                               "algorithmic_bytes": 4.0 * (M * K + K * N),
+                               "gbs": 4.0 * (M * K + K * N) / (rho_ms * 1e-3) / 1e9,
+                               "hbm_frac": 4.0 * (M * K + K * N) / (rho_ms * 1e-3) / 1e9 / hbm}}
 
     # end to end: host inputs (pinned), H2D + call + D2H of C inside every step
     e2e = None
@@ -396,16 +462,20 @@ def ours(args) -> None:
 
     if rank == 0:
         line = {
-            "metric": "emulated-FP32 TFLOPS", "value": value, "unit": "TFLOPS", "n_gpus": world,
+            "metric": ("rho-probe TFLOPS" if wl == "rho" else "emulated-FP32 TFLOPS"), "value": value,
+            "unit": "TFLOPS", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": scaling, "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic N(0,1)*2^e, e~U{-20..20} (torch generator)",
+            "data": ("synthetic U[-1,1] (torch generator)" if wl == "chunked"
+                     else "synthetic N(0,1)*2^e, e~U{-20..20} (torch generator)"),
             "config": {"workload": desc, "M": M * (world if wl == "square" else 1), "N": N, "K": K,
-                       "scheme": args.scheme, "force_scheme": scheme,
+                       "scheme": ("fp32_chunked" if wl == "chunked" else "rho_probe" if wl == "rho" else args.scheme),
+                       "force_scheme": (2 if wl == "chunked" else None if wl == "rho" else scheme),
+                       "chunks": args.chunks if wl == "chunked" else None,
                        "hints": "absmax given, rho=0 (no scans)", "l2": "inputs larger than L2",
                        "parallelism": (f"{wl} x{world}" if world > 1 else "single GPU")},
-            "roofline": {"bound": "tensor", "kernel": "k_tc_gemm", "achieved": tensor_tflops,
-                         "peak": peak, "peak_source": f"{peak_name} ({src})", "unit": "TFLOP/s",
+            "roofline": {"bound": bound, "kernel": kern_name, "achieved": tensor_tflops,
+                         "peak": peak, "peak_source": peak_source, "unit": "TFLOP/s",
                          "frac": (tensor_tflops / peak) if tensor_tflops else None,
                          "frac_of_burst": (tensor_tflops / burst) if tensor_tflops else None,
                          "flops_per_launch": rank_tensor_flop / launches_per_step, "kernel_ms": gemm_avg,
@@ -419,6 +489,7 @@ def ours(args) -> None:
             "clocks": clk.summary(),
             "gpu_launches": launches,
         }
+        line.update(extra)
         print(json.dumps(line), flush=True)
     h.close()
     if dist is not None:
