@@ -4,8 +4,8 @@ the square sweep, inputs N(0,1) * 2^e with e uniform in [-20, 20]), one call per
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--size S] [--scheme bf16x3]
 
 ours:      value = emulated TFLOPS (2*M*N*K per step) with A, B resident in HBM, CUDA events on the handle's
-           stream around the K timed steps, max over ranks; e2e = the same call with HOST inputs (pinned),
-           H2D of A and B and D2H of C inside every timed step. Extra keys: roofline of the dominant kernel
+           stream around the K timed steps, max over ranks; e2e = the same product through emugemm_sgemm_host
+           with HOST inputs (pinned): H2D of A and B and D2H of C inside every timed step. Extra keys: roofline of the dominant kernel
            (tensor-core GEMM, timed with CUDA events on its own stream), cpu_baseline (the oracle's host FP64
            GEMM on a bounded row sample, all host threads), clocks sampled during the timed region,
            gpu_launches (kernels this library launched inside the timed region).
@@ -291,10 +291,13 @@ def ours(args) -> None:
         total_flop = 2.0 * M * N * K
         scaling = "strong"
         desc = f"{args.scheme} emulated SGEMM {S}^3, row blocks of A over {world} GPU(s), B broadcast in panels"
+        # four column panels (multiples of 256): each panel's GEMM still runs whole waves of CTA-pair tiles, and
+        # the broadcast of panel j+1 overlaps the GEMM of panel j
+        rows_panel = ((N + 3) // 4 + 255) // 256 * 256
 
         def step():
             if dist is not None:
-                multigpu.row_sharded(A, B, C, src=0, panel=(N + 1) // 2, handle=h, scheme=scheme)
+                multigpu.row_sharded(A, B, C, src=0, panel=rows_panel, handle=h, scheme=scheme)
             else:
                 h.sgemm(m_loc, N, K, A, B, C, force=scheme, hints=hints())
     elif wl == "chunked":
@@ -367,10 +370,14 @@ def ours(args) -> None:
     prof = h.profile_end()
     launches = emugemm.launch_count() - launches0
     ms_total = ev0.elapsed_time(ev1)
+    rank_ms = None
     if dist is not None:
-        t = torch.tensor([ms_total], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_total = float(t.item())
+        # every rank's timed-region length (stragglers show here), and the max over ranks as the job's time
+        t = torch.zeros(world, device="cuda", dtype=torch.float64)
+        t[rank] = ms_total
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        rank_ms = [round(float(x) / args.steps, 3) for x in t.cpu()]
+        ms_total = float(t.max().item())
         dist.barrier()
     ms_step = ms_total / args.steps
     value = total_flop / (ms_step * 1e-3) / 1e12
@@ -391,8 +398,10 @@ def ours(args) -> None:
     launches_per_step = max(1, gemm_n // max(1, args.steps))
     tensor_tflops = (rank_tensor_flop / launches_per_step / (gemm_avg * 1e-3) / 1e12) if gemm_n else None
     burst, sustained, hbm, src = peaks()
-    # a timed loop of more than half a second runs under the power cap: compare with the sustained peak
-    long_loop = ms_total > 500.0
+    # a timed loop of more than half a second, or one whose clock samples show the power cap, runs under the power
+    # cap: compare with the sustained peak
+    clocks = clk.summary()
+    long_loop = ms_total > 500.0 or "sw_power_cap" in clocks["reasons"]
     peak = sustained if long_loop else burst
     peak_name = "bf16_tflops_sustained" if long_loop else "bf16_tflops"
     peak_source = f"{peak_name} ({src})"
@@ -408,19 +417,16 @@ def ours(args) -> None:
                                "gbs": 4.0 * (M * K + K * N) / (rho_ms * 1e-3) / 1e9,
                                "hbm_frac": 4.0 * (M * K + K * N) / (rho_ms * 1e-3) / 1e9 / hbm}}
 
-    # end to end: host inputs (pinned), H2D + call + D2H of C inside every step
+    # end to end: host inputs (pinned) through emugemm_sgemm_host, whose H2D of A and B and D2H of C are inside
+    # every step (B and C in column panels overlapped with the panel GEMMs)
     e2e = None
     if not args.no_e2e and world == 1 and wl == "square":
         hA = A.cpu().pin_memory()
         hB = B.cpu().pin_memory()
         hC = torch.empty((M, N), dtype=torch.float32).pin_memory()
-        dA, dB, dC = torch.empty_like(A), torch.empty_like(B), torch.empty_like(C)
 
         def e2e_step():
-            dA.copy_(hA, non_blocking=True)
-            dB.copy_(hB, non_blocking=True)
-            h.sgemm(M, N, K, dA, dB, dC, force=scheme, hints=hints())
-            hC.copy_(dC, non_blocking=True)
+            h.sgemm_host(M, N, K, hA, hB, hC, force=scheme, hints=hints())
 
         for _ in range(2):
             e2e_step()
@@ -486,9 +492,11 @@ def ours(args) -> None:
             "cpu_baseline": cpu,
             "cublas_sgemm": cublas,
             "e2e": e2e,
-            "clocks": clk.summary(),
+            "clocks": clocks,
             "gpu_launches": launches,
         }
+        if rank_ms is not None:
+            line["ms_per_step_by_rank"] = rank_ms
         line.update(extra)
         print(json.dumps(line), flush=True)
     h.close()

@@ -327,6 +327,10 @@ emugemm_status_t emugemm_destroy_handle(emugemm_handle_t handle) {
     if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
     emu::DeviceGuard g(h->device);
     cudaStreamSynchronize((cudaStream_t)h->stream);
+    for (void* ev : h->host_ev)
+        if (ev) cudaEventDestroy((cudaEvent_t)ev);
+    if (h->copy_in) cudaStreamDestroy((cudaStream_t)h->copy_in);
+    if (h->copy_out) cudaStreamDestroy((cudaStream_t)h->copy_out);
     for (int i = 0; i < emu::kWsCount; ++i)
         if (h->ws[i]) cudaFree(h->ws[i]);
     emu::prof_clear(h);
@@ -405,6 +409,97 @@ emugemm_status_t emugemm_sgemm(emugemm_handle_t handle, int M, int N, long K, co
                                float* C, const emu_request_t* req, emu_hints_t* hints, emu_plan_t* out_plan) {
     return emugemm_sgemm_ex(handle, M, N, K, A, K > 0 ? K : 1, B, N > 0 ? N : 1, C, N > 0 ? N : 1, req, hints,
                             out_plan);
+}
+
+emugemm_status_t emugemm_sgemm_host(emugemm_handle_t handle, int M, int N, long K, const float* A, const float* B,
+                                    float* C, const emu_request_t* req, emu_hints_t* hints, emu_plan_t* out_plan) {
+    Handle* h = reinterpret_cast<Handle*>(handle);
+    if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
+    if (M < 0 || N < 0 || K < 0) return EMUGEMM_STATUS_INVALID_SIZE;
+    if ((M > 0 && N > 0) && (!C || (K > 0 && (!A || !B)))) return EMUGEMM_STATUS_INVALID_POINTER;
+    emu::DeviceGuard g(h->device);
+    if (!g.ok) return EMUGEMM_STATUS_INTERNAL_ERROR;
+    if (M == 0 || N == 0) {
+        if (out_plan) {
+            emu_hints_t local = hints ? *hints : emu_hints_t{0.f, 0.f, 0, 0.f, 0};
+            *out_plan = emu::plan(emu::model(), M, N, K, req, &local);
+        }
+        return EMUGEMM_STATUS_SUCCESS;
+    }
+    cudaStream_t cs = (cudaStream_t)h->stream;
+    const size_t a_bytes = (size_t)M * K * 4, b_bytes = (size_t)K * N * 4, c_bytes = (size_t)M * N * 4;
+    float* dA = (float*)emu::ws_get(h, emu::kWsHostA, a_bytes ? a_bytes : 4);
+    float* dB = (float*)emu::ws_get(h, emu::kWsHostB, b_bytes ? b_bytes : 4);
+    float* dC = (float*)emu::ws_get(h, emu::kWsHostC, c_bytes);
+    if (!dA || !dB || !dC) return EMUGEMM_STATUS_MEMORY_ERROR;
+    if (!h->copy_in) {
+        if (cudaStreamCreateWithFlags((cudaStream_t*)&h->copy_in, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaStreamCreateWithFlags((cudaStream_t*)&h->copy_out, cudaStreamNonBlocking) != cudaSuccess) {
+            cudaGetLastError();
+            return EMUGEMM_STATUS_INTERNAL_ERROR;
+        }
+        for (void*& ev : h->host_ev)
+            if (cudaEventCreateWithFlags((cudaEvent_t*)&ev, cudaEventDisableTiming) != cudaSuccess) {
+                cudaGetLastError();
+                return EMUGEMM_STATUS_INTERNAL_ERROR;
+            }
+    }
+    cudaStream_t cin = (cudaStream_t)h->copy_in, cout = (cudaStream_t)h->copy_out;
+    cudaEvent_t* ev = reinterpret_cast<cudaEvent_t*>(h->host_ev);
+    cudaEvent_t ev_start = ev[0], ev_done = ev[1];
+    cudaEvent_t* ev_b = ev + 2;                          // panel j of B has arrived
+    cudaEvent_t* ev_c = ev + 2 + emu::kMaxHostPanels;    // panel j of C is computed
+    int e = 0;
+    // the copies must not overwrite the device operands while earlier work on the handle's stream reads them
+    e = cudaEventRecord(ev_start, cs);
+    if (!e) e = cudaStreamWaitEvent(cin, ev_start, 0);
+    if (!e) e = cudaStreamWaitEvent(cout, ev_start, 0);
+    if (e) return emu::from_cuda(e);
+
+    // Hints that ask for scans need all of A and B on the device first: copy, then the device entry point.
+    const bool measure = !hints || hints->a_absmax < 0 || hints->b_absmax < 0 || hints->rho < 0 || K == 0;
+    if (measure) {
+        if (a_bytes) e = cudaMemcpyAsync(dA, A, a_bytes, cudaMemcpyHostToDevice, cs);
+        if (!e && b_bytes) e = cudaMemcpyAsync(dB, B, b_bytes, cudaMemcpyHostToDevice, cs);
+        if (e) return emu::from_cuda(e);
+        emugemm_status_t s = emugemm_sgemm_ex(handle, M, N, K, dA, K > 0 ? K : 1, dB, N, dC, N, req, hints, out_plan);
+        if (s != EMUGEMM_STATUS_SUCCESS) return s;
+        return emu::from_cuda(cudaMemcpyAsync(C, dC, c_bytes, cudaMemcpyDeviceToHost, cs));
+    }
+
+    emu_hints_t local = *hints;
+    emu_plan_t plan = emu::plan(emu::model(), M, N, K, req, &local);
+    if (out_plan) *out_plan = plan;
+    // Column panels: A crosses PCIe once and is split once (later panels reuse its slices); panel j of B
+    // travels on copy_in, its GEMM runs on the handle's stream as soon as it has landed, and panel j of C
+    // travels back on copy_out while later panels of B arrive (PCIe carries both directions at once).
+    // Widths are multiples of 256 (whole CTA-pair tiles), about 8 panels.
+    long w = ((long)N + 7) / 8;
+    w = (w + 255) / 256 * 256;
+    if (w < 256) w = 256;
+    while ((N + w - 1) / w > emu::kMaxHostPanels) w += 256;
+    const int np = (int)((N + w - 1) / w);
+    e = cudaMemcpyAsync(dA, A, a_bytes, cudaMemcpyHostToDevice, cin);
+    for (int j = 0; j < np && !e; ++j) {
+        const long n0 = (long)j * w, wn = (n0 + w <= N) ? w : N - n0;
+        e = cudaMemcpy2DAsync(dB + n0, (size_t)N * 4, B + n0, (size_t)N * 4, (size_t)wn * 4, (size_t)K,
+                              cudaMemcpyHostToDevice, cin);
+        if (!e) e = cudaEventRecord(ev_b[j], cin);
+        if (!e) e = cudaStreamWaitEvent(cs, ev_b[j], 0);
+        if (e) break;
+        emugemm_status_t s = emu::dispatch(h, plan.chosen, plan.chunks, M, (int)wn, K, dA, K, dB + n0, N, dC + n0, N,
+                                           nullptr, 0, /*a_reused*/ j > 0);
+        if (s != EMUGEMM_STATUS_SUCCESS) return s;
+        e = cudaEventRecord(ev_c[j], cs);
+        if (!e) e = cudaStreamWaitEvent(cout, ev_c[j], 0);
+        if (!e)
+            e = cudaMemcpy2DAsync(C + n0, (size_t)N * 4, dC + n0, (size_t)N * 4, (size_t)wn * 4, (size_t)M,
+                                  cudaMemcpyDeviceToHost, cout);
+    }
+    // the call is complete, for the handle's stream, once the last panel of C has reached the host
+    if (!e) e = cudaEventRecord(ev_done, cout);
+    if (!e) e = cudaStreamWaitEvent(cs, ev_done, 0);
+    return emu::from_cuda(e);
 }
 
 double emugemm_estimate_rho(emugemm_handle_t handle, int M, int N, long K, const float* A, const float* B,

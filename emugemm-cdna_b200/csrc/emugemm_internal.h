@@ -49,7 +49,7 @@ extern const char* const kReasonNative;
 struct TileChoice {
     int tc_variant;     // tensor-core kernel: 0 = built-in choice, 1 = single-CTA, 2 = CTA pair (cta_group::2),
                         // 3 = CTA pair with the split fused in (bf16x3 only)
-    int fp32_bm;        // FP32 SIMT tile edge: 0 = auto, 64 or 128
+    int fp32_bm;        // FP32 SIMT tile edge: 0 = auto, 32, 64 or 128
 };
 TileChoice lookup_tile(int M, int N, long K, int dtype /*0 fp32, 1 bf16, 2 fp16*/);
 
@@ -71,8 +71,12 @@ enum WsSlot {
     kWsF64Acc,
     kWsRhoT1, kWsRhoT2, kWsRhoPart,
     kWsScalar,
+    kWsHostA, kWsHostB, kWsHostC,   // device copies of the operands of emugemm_sgemm_host
     kWsCount
 };
+
+// emugemm_sgemm_host: column panels of B and C streamed over PCIe, at most this many per call.
+constexpr int kMaxHostPanels = 16;
 
 // Kernel classes timed by the optional per-handle profiler (CUDA events on the handle's stream).
 enum ProfKind { kProfTcGemm = 0, kProfFp32Gemm, kProfSplit, kProfScan, kProfRho, kProfReduce, kProfCount };
@@ -97,6 +101,10 @@ struct Handle {
         const float* A = nullptr; int M = 0; long K = 0, lda = 0; int kind = -1; long Mp = 0, Kp = 0;
         const void* ws0 = nullptr; const void* ws1 = nullptr; const void* rexp = nullptr;
     } a_key;
+    // emugemm_sgemm_host: copy streams (H2D, D2H) and events, created on first use.
+    void* copy_in = nullptr;
+    void* copy_out = nullptr;
+    void* host_ev[2 * kMaxHostPanels + 2] = {};
 };
 
 // Profiler scope: records an event before and after the launches inside it when the handle profiles.

@@ -39,10 +39,11 @@ __global__ void __launch_bounds__(kThr) k_fp32_gemm(Params p) {
     __shared__ __align__(16) float As[2][kBKf][BM];
     __shared__ __align__(16) float Bs[2][kBKf][BN];
     constexpr int HM = TM / 2, HN = TN / 2;
-    constexpr int A_VEC = BM * kBKf / 4 / kThr;   // float4 per thread
-    constexpr int B_VEC = BN * kBKf / 4 / kThr;
-    constexpr int A_SC = BM * kBKf / kThr;        // scalars per thread
-    constexpr int B_SC = BN * kBKf / kThr;
+    constexpr int A_F4 = BM * kBKf / 4, B_F4 = BN * kBKf / 4;   // float4s per k-block tile
+    constexpr int A_VEC = (A_F4 + kThr - 1) / kThr;             // float4 per thread (the last may be idle)
+    constexpr int B_VEC = (B_F4 + kThr - 1) / kThr;
+    constexpr int A_SC = (BM * kBKf + kThr - 1) / kThr;         // scalars per thread
+    constexpr int B_SC = (BN * kBKf + kThr - 1) / kThr;
     static_assert(16 * TM == BM && 16 * TN == BN, "tile shape");
 
     const int tid = threadIdx.x;
@@ -67,7 +68,8 @@ __global__ void __launch_bounds__(kThr) k_fp32_gemm(Params p) {
                 const int m = m0 + row;
                 const long k = kb + kq * 4;
                 float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (m < p.M && k < kend) v = __ldg(reinterpret_cast<const float4*>(p.A + (size_t)m * p.lda + k));
+                if (f < A_F4 && m < p.M && k < kend)
+                    v = __ldg(reinterpret_cast<const float4*>(p.A + (size_t)m * p.lda + k));
                 ra[4 * j] = v.x; ra[4 * j + 1] = v.y; ra[4 * j + 2] = v.z; ra[4 * j + 3] = v.w;
             }
 #pragma unroll
@@ -77,7 +79,8 @@ __global__ void __launch_bounds__(kThr) k_fp32_gemm(Params p) {
                 const long k = kb + kk;
                 const int n = n0 + nq * 4;
                 float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (k < kend && n < p.N) v = __ldg(reinterpret_cast<const float4*>(p.B + (size_t)k * p.ldb + n));
+                if (f < B_F4 && k < kend && n < p.N)
+                    v = __ldg(reinterpret_cast<const float4*>(p.B + (size_t)k * p.ldb + n));
                 rb[4 * j] = v.x; rb[4 * j + 1] = v.y; rb[4 * j + 2] = v.z; rb[4 * j + 3] = v.w;
             }
         } else {
@@ -87,7 +90,7 @@ __global__ void __launch_bounds__(kThr) k_fp32_gemm(Params p) {
                 const int row = f / kBKf, kk = f % kBKf;
                 const int m = m0 + row;
                 const long k = kb + kk;
-                ra[j] = (m < p.M && k < kend) ? __ldg(p.A + (size_t)m * p.lda + k) : 0.f;
+                ra[j] = (f < BM * kBKf && m < p.M && k < kend) ? __ldg(p.A + (size_t)m * p.lda + k) : 0.f;
             }
 #pragma unroll
             for (int j = 0; j < B_SC; ++j) {
@@ -95,7 +98,7 @@ __global__ void __launch_bounds__(kThr) k_fp32_gemm(Params p) {
                 const int kk = f / BN, nn = f % BN;
                 const long k = kb + kk;
                 const int n = n0 + nn;
-                rb[j] = (k < kend && n < p.N) ? __ldg(p.B + (size_t)k * p.ldb + n) : 0.f;
+                rb[j] = (f < BN * kBKf && k < kend && n < p.N) ? __ldg(p.B + (size_t)k * p.ldb + n) : 0.f;
             }
         }
     };
@@ -105,6 +108,7 @@ __global__ void __launch_bounds__(kThr) k_fp32_gemm(Params p) {
             for (int j = 0; j < A_VEC; ++j) {
                 const int f = tid + j * kThr;
                 const int row = f >> 2, kq = f & 3;
+                if (f >= A_F4) continue;
 #pragma unroll
                 for (int e = 0; e < 4; ++e) As[buf][kq * 4 + e][row] = ra[4 * j + e];
             }
@@ -112,6 +116,7 @@ __global__ void __launch_bounds__(kThr) k_fp32_gemm(Params p) {
             for (int j = 0; j < B_VEC; ++j) {
                 const int f = tid + j * kThr;
                 const int kk = f / (BN / 4), nq = f % (BN / 4);
+                if (f >= B_F4) continue;
                 *reinterpret_cast<float4*>(&Bs[buf][kk][nq * 4]) =
                     make_float4(rb[4 * j], rb[4 * j + 1], rb[4 * j + 2], rb[4 * j + 3]);
             }
@@ -119,11 +124,13 @@ __global__ void __launch_bounds__(kThr) k_fp32_gemm(Params p) {
 #pragma unroll
             for (int j = 0; j < A_SC; ++j) {
                 const int f = tid + j * kThr;
+                if (f >= BM * kBKf) continue;
                 As[buf][f % kBKf][f / kBKf] = ra[j];
             }
 #pragma unroll
             for (int j = 0; j < B_SC; ++j) {
                 const int f = tid + j * kThr;
+                if (f >= BN * kBKf) continue;
                 Bs[buf][f / BN][f % BN] = rb[j];
             }
         }
@@ -208,23 +215,32 @@ struct Shape {
     int tiles;
 };
 
+// Chunk groups for `tiles` output tiles: enough CTAs for two per SM, at most one group per chunk.
+static int groups_for(int ce, long tiles, int sms) {
+    if (ce <= 1) return 1;
+    long want = (2L * sms + tiles - 1) / tiles;
+    if (want < 1) want = 1;
+    return (int)(want < ce ? want : ce);
+}
+
+// Tile edge: 128 when its tiles fill the GPU; else 64 when its tiles x chunk groups do; else 32 (2 x 2 chains
+// per thread), so that a product with few output tiles and few chunks (M = N = 256, c = 1) spreads its
+// FMA chains over more SMs. No chain changes with the tile edge.
 Shape shape_of(const Fp32GemmArgs& a) {
     Shape s;
     const int sms = a.num_sms > 0 ? a.num_sms : 148;
-    const long t128 = (long)((a.M + 127) / 128) * ((a.N + 127) / 128);
-    s.bm = a.bm ? a.bm : (t128 >= sms ? 128 : 64);
-    s.tiles = (int)((long)((a.M + s.bm - 1) / s.bm) * ((a.N + s.bm - 1) / s.bm));
     const int c = a.chunks < 1 ? 1 : a.chunks;
     s.kc = (a.K + c - 1) / c;
     if (s.kc < 1) s.kc = 1;
     s.ce = (int)((a.K + s.kc - 1) / s.kc);
     if (s.ce < 1) s.ce = 1;
-    int G = 1;
-    if (s.ce > 1) {
-        int want = (2 * sms + s.tiles - 1) / s.tiles;
-        G = want < 1 ? 1 : want;
-        if (G > s.ce) G = s.ce;
-    }
+    auto tiles_of = [&](int bm) { return (long)((a.M + bm - 1) / bm) * ((a.N + bm - 1) / bm); };
+    if (a.bm) s.bm = a.bm;
+    else if (tiles_of(128) >= sms) s.bm = 128;
+    else if (tiles_of(64) * groups_for(s.ce, tiles_of(64), sms) >= sms) s.bm = 64;
+    else s.bm = 32;
+    s.tiles = (int)tiles_of(s.bm);
+    const int G = groups_for(s.ce, s.tiles, sms);
     s.cpg = (s.ce + G - 1) / G;
     s.G = (s.ce + s.cpg - 1) / s.cpg;
     return s;
@@ -268,9 +284,14 @@ int launch_fp32_gemm(const Fp32GemmArgs& a, void* stream) {
     if (s.bm == 128) {
         if (vec) launch_cfg<128, 8, true>(p, grid, st);
         else launch_cfg<128, 8, false>(p, grid, st);
-    } else {
+    } else if (s.bm == 64) {
         if (vec) launch_cfg<64, 4, true>(p, grid, st);
         else launch_cfg<64, 4, false>(p, grid, st);
+    } else if (s.bm == 32) {
+        if (vec) launch_cfg<32, 2, true>(p, grid, st);
+        else launch_cfg<32, 2, false>(p, grid, st);
+    } else {
+        return (int)cudaErrorInvalidValue;
     }
     count_launch();
     cudaError_t e = cudaGetLastError();

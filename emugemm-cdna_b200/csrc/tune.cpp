@@ -6,7 +6,7 @@
 // dtype is fp32 | bf16 | fp16. `tile` is the kernel choice for that shape: for bf16/fp16 rows the
 // tensor-core kernel (1 = single-CTA 128-row tiles, 2 = CTA pairs on 256-row tiles, 3 = CTA pairs with the
 // split fused in), for fp32 rows the SIMT tile edge
-// (64 or 128). As in the reference, a row whose arch does not match the live device is rejected (a tile
+// (32, 64 or 128). As in the reference, a row whose arch does not match the live device is rejected (a tile
 // choice tuned on another GPU is not trusted), lines that do not parse as 10 fields are skipped (this
 // skips the header), and the lookup takes the nearest shape in log2 space if its distance is below 1.
 #include "emugemm_internal.h"
@@ -105,7 +105,7 @@ TileChoice lookup_tile(int M, int N, long K, int dtype) {
     if (M <= 0 || N <= 0 || K <= 0) return t;
     int v = lookup_raw(M, N, K, dtype);
     if (dtype == 0) {
-        if (v == 64 || v == 128) t.fp32_bm = v;
+        if (v == 32 || v == 64 || v == 128) t.fp32_bm = v;
     } else {
         if (v == 1 || v == 2 || v == 3) t.tc_variant = v;
     }

@@ -85,6 +85,8 @@ _SIGS = {
                               P(EmuRequest), P(EmuHints), P(EmuPlan)]),
     "emugemm_sgemm_ex": (c_int, [c_void_p, c_int, c_int, c_long, c_void_p, c_long, c_void_p, c_long,
                                  c_void_p, c_long, P(EmuRequest), P(EmuHints), P(EmuPlan)]),
+    "emugemm_sgemm_host": (c_int, [c_void_p, c_int, c_int, c_long, c_void_p, c_void_p, c_void_p,
+                                   P(EmuRequest), P(EmuHints), P(EmuPlan)]),
     "emugemm_sgemm_partial_f64": (c_int, [c_void_p, c_int, c_int, c_long, c_void_p, c_long, c_void_p,
                                           c_long, c_void_p, c_int, c_int]),
     "emugemm_reduce_f64": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
@@ -208,6 +210,18 @@ class Handle:
         code = lib().emugemm_sgemm(self.h, M, N, K, _ptr(A), _ptr(B), _ptr(C), ctypes.byref(req),
                                    ctypes.byref(hints) if use_hints else None, ctypes.byref(p))
         check("emugemm_sgemm", code)
+        return p, hints
+
+    def sgemm_host(self, M, N, K, A, B, C, max_rel_err=1e-5, force=AUTO, hints=None, use_hints=True):
+        """C = A*B through emugemm_sgemm_host: A, B, C are HOST buffers (pinned tensors or addresses)."""
+        req = EmuRequest(max_rel_err, force)
+        if use_hints and hints is None:
+            hints = EmuHints(-1.0, -1.0, 0, 0.0, 0)
+        p = EmuPlan()
+        check("emugemm_sgemm_host", lib().emugemm_sgemm_host(self.h, M, N, K, _ptr(A), _ptr(B), _ptr(C),
+                                                             ctypes.byref(req),
+                                                             ctypes.byref(hints) if use_hints else None,
+                                                             ctypes.byref(p)))
         return p, hints
 
     def sgemm_ex(self, M, N, K, A, lda, B, ldb, C, ldc, max_rel_err=1e-5, force=AUTO, hints=None):

@@ -3,7 +3,8 @@ bench/gen_tune_table.cpp: offline, resumable, shardable, header written once und
 
 For every (M, N, K, dtype) of the grid it times the candidate kernels through the C ABI and appends one row
     arch,cuda_version,M,N,K,dtype,tile,best_ms,default_ms,gain
-where `tile` is the winner (bf16/fp16: 1 = single-CTA, 2 = CTA pair; fp32: SIMT tile edge 64 or 128),
+where `tile` is the winner (bf16/fp16: 1 = single-CTA, 2 = CTA pair, 3 = fused split; fp32: SIMT tile edge 32, 64
+or 128),
 `default_ms` the built-in choice's time and `gain` = default_ms / best_ms. Rows already present for a key are
 skipped, so an interrupted run resumes; --shard i/n takes every n-th shape starting at i (one process per GPU).
 
@@ -67,24 +68,28 @@ def tune_shape(h, M, N, K, dtype, reps):
     scheme = DTYPES[dtype]
     hints = emugemm.EmuHints(1.0, 1.0, 0, 0.0, 0)
     res = {}
+
+    def timed():
+        return time_call(h, lambda: h.sgemm(M, N, K, A, B, C, force=scheme, hints=hints), reps)
+
     if dtype == "fp32":
-        # the SIMT tile edge comes from the table only, so time both by loading a one-row table per candidate
-        for tile in (128, 64):
+        # the SIMT tile edge comes from the table only, so time each by loading a one-row table per candidate
+        for tile in (128, 64, 32):
             tmp = pathlib.Path(f"/tmp/emugemm_tile_{os.getpid()}.csv")
             tmp.write_text(HEADER + f"{arch()},probe,{M},{N},{K},fp32,{tile},0,0,1\n")
             emugemm.lib().emugemm_init(str(tmp).encode())
-            res[tile] = time_call(h, lambda: h.sgemm(M, N, K, A, B, C, force=scheme, hints=hints), reps)
+            res[tile] = timed()
             tmp.unlink()
         emugemm.lib().emugemm_shutdown()
-        default = 128 if ((M + 127) // 128) * ((N + 127) // 128) >= torch.cuda.get_device_properties(0).multi_processor_count else 64
     else:
-        for tile, name in ((1, "single"), (2, "pair")):
+        kernels = ((1, "single"), (2, "pair"), (3, "fused")) if dtype == "bf16" else ((1, "single"), (2, "pair"))
+        for tile, name in kernels:
             os.environ["EMUGEMM_TC_KERNEL"] = name
-            res[tile] = time_call(h, lambda: h.sgemm(M, N, K, A, B, C, force=scheme, hints=hints), reps)
+            res[tile] = timed()
         os.environ.pop("EMUGEMM_TC_KERNEL", None)
-        default = 1
+    default_ms = timed()   # the built-in choice: no table row, no override
     best = min(res, key=res.get)
-    return best, res[best], res[default]
+    return best, res[best], default_ms
 
 
 def arch() -> str:

@@ -155,6 +155,22 @@ emugemm_status_t emugemm_sgemm_ex(emugemm_handle_t handle,
                                   const emu_request_t* req, emu_hints_t* hints,
                                   emu_plan_t* out_plan);
 
+/* emugemm_sgemm on HOST buffers (no emugemm-cdna counterpart; its callers copy to the device themselves):
+   A (MxK), B (KxN), C (MxN) row-major in host memory, pinned (cudaHostAlloc / cudaHostRegister) for the
+   copies to overlap. With every hint given (absmax >= 0, rho >= 0), A is copied to the device once and B and C
+   travel in column panels of about N/8 on two copy streams of the handle, each panel's GEMM starting as soon
+   as its panel of B has landed and its panel of C leaving while later panels of B arrive; A is split once.
+   Hints that ask for measurements (or NULL hints) copy all of A and B first and then run emugemm_sgemm.
+   C is identical to emugemm_sgemm's for BF16X3, FP16X3 and NATIVE_FP32; FP32_CHUNKED keeps the same FMA
+   chains, but its FP64 chunk groups follow the panel's tile count. Asynchronous on the handle's stream: C is
+   complete once that stream has been synchronized. The device copies of A, B, C live in the handle's
+   workspace. */
+emugemm_status_t emugemm_sgemm_host(emugemm_handle_t handle,
+                                    int M, int N, long K,
+                                    const float* A, const float* B, float* C,
+                                    const emu_request_t* req, emu_hints_t* hints,
+                                    emu_plan_t* out_plan);
+
 /* K-split partial: P(MxN, FP64, ld=N) = A(MxK) * B(KxN) computed with `scheme` (BF16X3, FP16X3,
    NATIVE_FP32 or FP32_CHUNKED with `chunks`), written in FP64 so that partials from several devices can
    be summed exactly enough (ncclFloat64) before one final rounding to FP32. */

@@ -386,3 +386,24 @@ def test_fused_split_kernel_partial_f64(cuda, handle, monkeypatch):
         out[variant] = P.cpu().numpy()
     assert np.isfinite(out["fused"]).all()
     assert np.array_equal(out["fused"], out["pair"])
+
+
+@pytest.mark.parametrize("force", [emugemm.BF16X3, emugemm.FP16X3, emugemm.NATIVE_FP32])
+@pytest.mark.parametrize("shape", [(1024, 2048, 512), (300, 520, 1000), (1, 1, 1), (257, 3000, 64)])
+def test_sgemm_host_matches_device(cuda, handle, force, shape):
+    """emugemm_sgemm_host (pinned host A, B, C; B and C in column panels overlapped with the GEMMs) gives the bits
+    of emugemm_sgemm on device copies of the same operands, with hints given (pipelined) and with NULL hints
+    (copy everything, then the device path)."""
+    torch = cuda
+    M, N, K = shape
+    A = datagen.wide_range((M, K), 90 + M, emax=10)
+    B = datagen.wide_range((K, N), 91 + N, emax=10)
+    want, _, _ = run_sgemm(torch, handle, A, B, force=force, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+    hA = torch.from_numpy(A).pin_memory()
+    hB = torch.from_numpy(B).pin_memory()
+    for hints, use in ((emugemm.EmuHints(1, 1, 0, 0, 0), True), (None, False)):
+        hC = torch.full((M, N), float("nan")).pin_memory()
+        p, _ = handle.sgemm_host(M, N, K, hA, hB, hC, force=force, hints=hints, use_hints=use)
+        handle.sync()
+        assert p.chosen == force
+        assert np.array_equal(hC.numpy(), want), (shape, use)
