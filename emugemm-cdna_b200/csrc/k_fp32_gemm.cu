@@ -18,7 +18,6 @@
 namespace emu {
 namespace {
 
-constexpr int kBKf = 16;
 constexpr int kThr = 256;
 
 struct Params {
@@ -34,7 +33,9 @@ struct Params {
     int G;
 };
 
-template <int BM, int BN, int TM, int TN, bool VEC>
+// kBKf: values of K per shared-memory stage (16; a 64-deep stage for the 32 tile measured slower: its
+// unrolled k-loop ran at 64 registers with spills).
+template <int BM, int BN, int TM, int TN, bool VEC, int kBKf>
 __global__ void __launch_bounds__(kThr) k_fp32_gemm(Params p) {
     __shared__ __align__(16) float As[2][kBKf][BM];
     __shared__ __align__(16) float Bs[2][kBKf][BN];
@@ -64,7 +65,7 @@ __global__ void __launch_bounds__(kThr) k_fp32_gemm(Params p) {
 #pragma unroll
             for (int j = 0; j < A_VEC; ++j) {
                 const int f = tid + j * kThr;
-                const int row = f >> 2, kq = f & 3;
+                const int row = f / (kBKf / 4), kq = f % (kBKf / 4);
                 const int m = m0 + row;
                 const long k = kb + kq * 4;
                 float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -107,7 +108,7 @@ __global__ void __launch_bounds__(kThr) k_fp32_gemm(Params p) {
 #pragma unroll
             for (int j = 0; j < A_VEC; ++j) {
                 const int f = tid + j * kThr;
-                const int row = f >> 2, kq = f & 3;
+                const int row = f / (kBKf / 4), kq = f % (kBKf / 4);
                 if (f >= A_F4) continue;
 #pragma unroll
                 for (int e = 0; e < 4; ++e) As[buf][kq * 4 + e][row] = ra[4 * j + e];
@@ -248,7 +249,7 @@ Shape shape_of(const Fp32GemmArgs& a) {
 
 template <int BM, int TM, bool VEC>
 void launch_cfg(const Params& p, dim3 grid, cudaStream_t st) {
-    k_fp32_gemm<BM, BM, TM, TM, VEC><<<grid, kThr, 0, st>>>(p);
+    k_fp32_gemm<BM, BM, TM, TM, VEC, 16><<<grid, kThr, 0, st>>>(p);
 }
 
 }  // namespace

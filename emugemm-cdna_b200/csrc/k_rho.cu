@@ -16,7 +16,9 @@
 namespace emu {
 namespace {
 
-constexpr int kRows = 64, kP = 64, kBJ = 32, kT = 256;
+constexpr int kRows = 128, kP = 64, kBJ = 32, kT = 256;
+constexpr int kTM = 8, kTN = 4;      // rows x probe columns per thread (16 x 16 threads)
+constexpr int kXs = kRows + 4;       // padded row of the transposed X tile (16-byte aligned reads)
 
 __device__ __forceinline__ float rademacher(unsigned i) {
     unsigned h = i ^ 0x5eedu;
@@ -30,57 +32,74 @@ __device__ __forceinline__ float rademacher(unsigned i) {
 
 // Ypart[s] (rows x P) = X[:, Js] * W[Js, :],  Yabs_part[s] = |X[:, Js]| * Wabs[Js, :].
 // OMEGA: W = Wabs = Omega (generated; J = N). Otherwise W, Wabs are J x P row-major.
+// Each thread owns 8 rows x 4 probe columns of both products (64 FMAs per j for three or four 16-byte shared
+// loads). X arrives as float4 along j (8 lanes per row: 128-byte global reads) and is stored transposed into
+// rows of kXs = 132 floats, read back as two float4 per thread. The transposed stores conflict 4 ways (bank
+// (16*jq + 4*e + rr) mod 32), which is a quarter of the inner loop's shared-memory wavefronts per k-block; with
+// the unpadded 64-row tile they conflicted 32 ways and cost more than the inner loop.
 template <bool OMEGA>
-__global__ void __launch_bounds__(kT) k_skinny(const float* __restrict__ X, long ld, long rows, long J, int P,
-                                               const float* __restrict__ W, const float* __restrict__ Wabs,
-                                               long j_per_split, float* __restrict__ Ypart,
-                                               float* __restrict__ Yabs_part) {
-    __shared__ __align__(16) float Xs[kBJ][kRows];
+__global__ void __launch_bounds__(kT, 2) k_skinny(const float* __restrict__ X, long ld, long rows, long J, int P,
+                                                  const float* __restrict__ W, const float* __restrict__ Wabs,
+                                                  long j_per_split, float* __restrict__ Ypart,
+                                                  float* __restrict__ Yabs_part) {
+    __shared__ __align__(16) float Xs[kBJ][kXs];
     __shared__ __align__(16) float Ws[kBJ][kP];
-    __shared__ __align__(16) float Was[kBJ][kP];
+    __shared__ __align__(16) float Was[OMEGA ? 1 : kBJ][kP];
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const long r0 = (long)blockIdx.x * kRows;
     const int p0 = blockIdx.y * kP;
     const int s = blockIdx.z;
     const long j_begin = (long)s * j_per_split;
     const long j_end = min(J, j_begin + j_per_split);
+    const bool vec = ((ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(X) & 15) == 0);
 
-    float acc[4][4] = {}, acca[4][4] = {};
+    float acc[kTM][kTN] = {}, acca[kTM][kTN] = {};
     for (long jb = j_begin; jb < j_end; jb += kBJ) {
-        for (int f = tid; f < kRows * kBJ; f += kT) {
-            const int rr = f / kBJ, jj = f % kBJ;
-            const long r = r0 + rr, j = jb + jj;
-            Xs[jj][rr] = (r < rows && j < j_end) ? __ldg(X + (size_t)r * ld + j) : 0.f;
+        // X tile: 128 rows x 32 j = 1024 float4, 4 per thread; lanes 8q..8q+7 read one row's 128 bytes
+#pragma unroll
+        for (int i = 0; i < kRows * kBJ / 4 / kT; ++i) {
+            const int f = tid + i * kT;
+            const int rr = f >> 3, jq = f & 7;
+            const long r = r0 + rr, j = jb + 4 * jq;
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
+            if (r < rows) {
+                if (vec && j + 3 < j_end) {
+                    const float4 t = __ldg(reinterpret_cast<const float4*>(X + (size_t)r * ld + j));
+                    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) v[e] = (j + e < j_end) ? __ldg(X + (size_t)r * ld + j + e) : 0.f;
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) Xs[4 * jq + e][rr] = v[e];
         }
         for (int f = tid; f < kBJ * kP; f += kT) {
             const int jj = f / kP, pp = f % kP;
             const long j = jb + jj;
             const int pc = p0 + pp;
-            float w = 0.f, wa = 0.f;
-            if (j < j_end && pc < P) {
-                if (OMEGA) {
-                    w = wa = rademacher((unsigned)((size_t)j * P + pc));
-                } else {
-                    w = __ldg(W + (size_t)j * P + pc);
-                    wa = __ldg(Wabs + (size_t)j * P + pc);
-                }
+            if (OMEGA) {
+                Ws[jj][pp] = (j < j_end && pc < P) ? rademacher((unsigned)((size_t)j * P + pc)) : 0.f;
+            } else {
+                const bool in = j < j_end && pc < P;
+                Ws[jj][pp] = in ? __ldg(W + (size_t)j * P + pc) : 0.f;
+                Was[jj][pp] = in ? __ldg(Wabs + (size_t)j * P + pc) : 0.f;
             }
-            Ws[jj][pp] = w;
-            Was[jj][pp] = wa;
         }
         __syncthreads();
-#pragma unroll 8
+#pragma unroll 4
         for (int jj = 0; jj < kBJ; ++jj) {
-            const float4 xv = *reinterpret_cast<const float4*>(&Xs[jj][ty * 4]);
-            const float4 wv = *reinterpret_cast<const float4*>(&Ws[jj][tx * 4]);
-            const float4 av = *reinterpret_cast<const float4*>(&Was[jj][tx * 4]);
-            const float x[4] = {xv.x, xv.y, xv.z, xv.w};
-            const float w[4] = {wv.x, wv.y, wv.z, wv.w};
-            const float a[4] = {av.x, av.y, av.z, av.w};
+            const float4 x0 = *reinterpret_cast<const float4*>(&Xs[jj][ty * kTM]);
+            const float4 x1 = *reinterpret_cast<const float4*>(&Xs[jj][ty * kTM + 4]);
+            const float4 wv = *reinterpret_cast<const float4*>(&Ws[jj][tx * kTN]);
+            const float4 av = OMEGA ? wv : *reinterpret_cast<const float4*>(&Was[OMEGA ? 0 : jj][tx * kTN]);
+            const float x[kTM] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            const float w[kTN] = {wv.x, wv.y, wv.z, wv.w};
+            const float a[kTN] = {av.x, av.y, av.z, av.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < kTM; ++i)
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
+                for (int q = 0; q < kTN; ++q) {
                     acc[i][q] = __fmaf_rn(x[i], w[q], acc[i][q]);
                     acca[i][q] = __fmaf_rn(fabsf(x[i]), a[q], acca[i][q]);
                 }
@@ -90,12 +109,12 @@ __global__ void __launch_bounds__(kT) k_skinny(const float* __restrict__ X, long
     float* Y = Ypart + (size_t)s * rows * P;
     float* Ya = Yabs_part + (size_t)s * rows * P;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const long r = r0 + ty * 4 + i;
+    for (int i = 0; i < kTM; ++i) {
+        const long r = r0 + ty * kTM + i;
         if (r >= rows) continue;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int pc = p0 + tx * 4 + q;
+        for (int q = 0; q < kTN; ++q) {
+            const int pc = p0 + tx * kTN + q;
             if (pc >= P) continue;
             Y[(size_t)r * P + pc] = acc[i][q];
             Ya[(size_t)r * P + pc] = acca[i][q];
