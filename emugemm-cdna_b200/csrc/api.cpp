@@ -158,8 +158,9 @@ static void prof_clear(Handle* h) {
 
 static long round_up(long x, long m) { return (x + m - 1) / m * m; }
 
-// Tensor-core kernel for a shape: 1 = single-CTA, 2 = CTA pair, 3 = CTA pair with the split fused in (bf16x3).
-// The environment variable EMUGEMM_TC_KERNEL ("single", "pair", "fused") wins, then the tile table's code, then
+// Tensor-core kernel for a shape: 1 = single-CTA, 2 = CTA pair, 3 = CTA pair with the split fused in, 4 = CTA pair
+// with A split into TMEM in the kernel (3 and 4: bf16x3). The environment variable EMUGEMM_TC_KERNEL ("single",
+// "pair", "fused", "fusea") wins, then the tile table's code, then
 // the built-in choice: CTA pairs for bf16x3 when the 256 x 256 pair tiles fill every pair of SMs at least once
 // (measured at 8192^3: 2.34 ms against 2.43 ms single-CTA), single-CTA 128-row tiles otherwise and for fp16x3
 // (3.24 ms against 3.40 ms for pairs).
@@ -169,12 +170,13 @@ static int tc_kernel_choice(Handle* h, int M, int N, long K, bool fp16) {
     if (v && std::strcmp(v, "single") == 0) code = 1;
     else if (v && std::strcmp(v, "pair") == 0) code = 2;
     else if (v && std::strcmp(v, "fused") == 0) code = 3;
+    else if (v && std::strcmp(v, "fusea") == 0) code = 4;
     if (!code) code = lookup_tile(M, N, K, fp16 ? 2 : 1).tc_variant;
     if (!code) {
         const long pair_tiles = ((M + 255) / 256) * (long)((N + 255) / 256);
         code = (!fp16 && pair_tiles >= (h->num_sms > 0 ? h->num_sms : 148) / 2) ? 2 : 1;
     }
-    if (fp16 && code == 3) code = 2;
+    if (fp16 && code >= 3) code = 2;
     return code;
 }
 
@@ -189,6 +191,22 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
         const int e = launch_tc_fused(A, lda, B, ldb, M, N, K, C, ldc, C64, ldc64, h->err_dev, h->num_sms, h->stream);
         if (e != (int)cudaErrorNotSupported) return from_cuda(e);
         // operands TMA cannot address (odd leading dimension or alignment): pre-split below
+    }
+    if (choice == 4 && (lda & 3) == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0) {
+        const long Np4 = round_up(N, tc_fused_a_bn()), Kp4 = slice_kp(K), KP4 = slice_panel(Kp4);
+        if (Np4 > 0x7fffffffL) return EMUGEMM_STATUS_INVALID_SIZE;
+        uint16_t* b0 = (uint16_t*)ws_get(h, kWsSplitB0, (size_t)Np4 * Kp4 * 2);
+        uint16_t* b1 = (uint16_t*)ws_get(h, kWsSplitB1, (size_t)Np4 * Kp4 * 2);
+        if (!b0 || !b1) return EMUGEMM_STATUS_MEMORY_ERROR;
+        int e = 0;
+        {
+            ProfScope ps(h, kProfSplit);
+            e = launch_split_cols(B, K, N, ldb, (int)Np4, Kp4, KP4, 0, nullptr, b0, b1, h->stream);
+        }
+        if (e) return from_cuda(e);
+        ProfScope ps(h, kProfTcGemm);
+        return from_cuda(launch_tc_fused_a(A, lda, b0, b1, M, N, (int)Np4, K, Kp4, KP4, C, ldc, C64, ldc64,
+                                           h->err_dev, h->num_sms, h->stream));
     }
     const bool pair = choice >= 2;
     const int BN = pair ? tc_pair_bn(fp16 ? 1 : 0) : tc_gemm_bn(fp16 ? 1 : 0);

@@ -48,7 +48,8 @@ extern const char* const kReasonNative;
 // tune.cpp: per-shape tile table
 struct TileChoice {
     int tc_variant;     // tensor-core kernel: 0 = built-in choice, 1 = single-CTA, 2 = CTA pair (cta_group::2),
-                        // 3 = CTA pair with the split fused in (bf16x3 only)
+                        // 3 = CTA pair with the split fused in, 4 = CTA pair with A split into TMEM in the
+                        // kernel and B pre-split (3 and 4: bf16x3 only)
     int fp32_bm;        // FP32 SIMT tile edge: 0 = auto, 32, 64 or 128
 };
 TileChoice lookup_tile(int M, int N, long K, int dtype /*0 fp32, 1 bf16, 2 fp16*/);
@@ -169,6 +170,13 @@ int tc_pair_bn(int fp16);
 // Returns cudaErrorNotSupported unless lda, ldb are multiples of 4 and A, B are 16-byte aligned.
 int launch_tc_fused(const float* A, long lda, const float* B, long ldb, int M, int N, long K, float* C, long ldc,
                     double* C64, long ldc64, unsigned* err, int num_sms, void* stream);
+// k_tc_fused_a.cu: bf16x3 on CTA pairs with A split in the kernel into TMEM and B's slices pre-split (b_hi, b_lo:
+// Np x Kp in K panels of KP, Np a multiple of tc_fused_a_bn()). cudaErrorNotSupported unless lda % 4 == 0 and A is
+// 16-byte aligned.
+int tc_fused_a_bn();
+int launch_tc_fused_a(const float* A, long lda, const uint16_t* b_hi, const uint16_t* b_lo, int M, int N, int Np,
+                      long K, long Kp, long KP, float* C, long ldc, double* C64, long ldc64, unsigned* err,
+                      int num_sms, void* stream);
 
 // k_fp32_gemm.cu: FP32 SIMT GEMM with K-chunks summed in FP64.
 struct Fp32GemmArgs {

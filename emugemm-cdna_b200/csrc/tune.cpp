@@ -5,7 +5,7 @@
 //     arch,cuda_version,M,N,K,dtype,tile,best_ms,default_ms,gain
 // dtype is fp32 | bf16 | fp16. `tile` is the kernel choice for that shape: for bf16/fp16 rows the
 // tensor-core kernel (1 = single-CTA 128-row tiles, 2 = CTA pairs on 256-row tiles, 3 = CTA pairs with the
-// split fused in), for fp32 rows the SIMT tile edge
+// split fused in, 4 = CTA pairs with A split into TMEM in the kernel), for fp32 rows the SIMT tile edge
 // (32, 64 or 128). As in the reference, a row whose arch does not match the live device is rejected (a tile
 // choice tuned on another GPU is not trusted), lines that do not parse as 10 fields are skipped (this
 // skips the header), and the lookup takes the nearest shape in log2 space if its distance is below 1.
@@ -107,7 +107,7 @@ TileChoice lookup_tile(int M, int N, long K, int dtype) {
     if (dtype == 0) {
         if (v == 32 || v == 64 || v == 128) t.fp32_bm = v;
     } else {
-        if (v == 1 || v == 2 || v == 3) t.tc_variant = v;
+        if (v >= 1 && v <= 4) t.tc_variant = v;
     }
     return t;
 }

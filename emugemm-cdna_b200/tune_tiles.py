@@ -3,8 +3,8 @@ bench/gen_tune_table.cpp: offline, resumable, shardable, header written once und
 
 For every (M, N, K, dtype) of the grid it times the candidate kernels through the C ABI and appends one row
     arch,cuda_version,M,N,K,dtype,tile,best_ms,default_ms,gain
-where `tile` is the winner (bf16/fp16: 1 = single-CTA, 2 = CTA pair, 3 = fused split; fp32: SIMT tile edge 32, 64
-or 128),
+where `tile` is the winner (bf16/fp16: 1 = single-CTA, 2 = CTA pair, 3 = fused split, 4 = A split into TMEM;
+fp32: SIMT tile edge 32, 64 or 128),
 `default_ms` the built-in choice's time and `gain` = default_ms / best_ms. Rows already present for a key are
 skipped, so an interrupted run resumes; --shard i/n takes every n-th shape starting at i (one process per GPU).
 
@@ -82,7 +82,8 @@ def tune_shape(h, M, N, K, dtype, reps):
             tmp.unlink()
         emugemm.lib().emugemm_shutdown()
     else:
-        kernels = ((1, "single"), (2, "pair"), (3, "fused")) if dtype == "bf16" else ((1, "single"), (2, "pair"))
+        kernels = (((1, "single"), (2, "pair"), (3, "fused"), (4, "fusea")) if dtype == "bf16"
+                   else ((1, "single"), (2, "pair")))
         for tile, name in kernels:
             os.environ["EMUGEMM_TC_KERNEL"] = name
             res[tile] = timed()

@@ -343,13 +343,15 @@ def test_pair_kernel_matches_single_cta_kernel(cuda, handle, monkeypatch, force,
     assert np.array_equal(out["pair"], out["single"])
 
 
+@pytest.mark.parametrize("variant", ["fused", "fusea"])
 @pytest.mark.parametrize("shape", [(256, 256, 128), (260, 516, 1004), (1024, 768, 2048), (2048, 2048, 512),
-                                   (384, 264, 96), (1, 1, 1), (33, 65, 129)])
+                                   (384, 264, 96), (1, 1, 1), (33, 65, 129), (260, 500, 20000)])
 @pytest.mark.parametrize("gen", ["normal", "wide_range"])
-def test_fused_split_kernel_matches_presplit(cuda, handle, monkeypatch, shape, gen):
-    """bf16x3 with the split fused into the CTA-pair GEMM (FP32 tiles by TMA, hi/lo made in shared memory)
-    uses the same slices, k-steps and promotion points as the pre-split kernels: identical bits. Leading
-    dimensions TMA cannot address (not a multiple of 4 floats) fall back to the pre-split path."""
+def test_fused_split_kernel_matches_presplit(cuda, handle, monkeypatch, variant, shape, gen):
+    """bf16x3 with the split fused into the CTA-pair GEMM uses the same slices, k-steps and promotion points as
+    the pre-split kernels: identical bits. `fused`: FP32 tiles of A and B by TMA, hi/lo made in shared memory;
+    `fusea`: A's hi/lo made in the kernel and written into TMEM, B pre-split. Leading dimensions TMA cannot address
+    (not a multiple of 4 floats) fall back to the pre-split path."""
     torch = cuda
     M, N, K = shape
     if gen == "normal":
@@ -359,33 +361,37 @@ def test_fused_split_kernel_matches_presplit(cuda, handle, monkeypatch, shape, g
         A = datagen.wide_range((M, K), 72 + M, emax=20)
         B = datagen.wide_range((K, N), 73 + N, emax=20)
     out, splits = {}, {}
-    for variant in ("pair", "fused"):
-        monkeypatch.setenv("EMUGEMM_TC_KERNEL", variant)
+    for v in ("pair", variant):
+        monkeypatch.setenv("EMUGEMM_TC_KERNEL", v)
         handle.profile_begin()
         C, p, _ = run_sgemm(torch, handle, A, B, force=emugemm.BF16X3, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
-        splits[variant] = handle.profile_end()["split"][1]
-        out[variant] = C
-    assert np.isfinite(out["fused"]).all()
-    assert np.array_equal(out["fused"], out["pair"])
-    fused_ran = K % 4 == 0 and N % 4 == 0
-    assert splits["fused"] == (0 if fused_ran else 1)   # one profiled scope covers both splits
+        splits[v] = handle.profile_end()["split"][1]
+        out[v] = C
+    assert np.isfinite(out[variant]).all()
+    assert np.array_equal(out[variant], out["pair"])
+    if variant == "fused":
+        fused_ran = K % 4 == 0 and N % 4 == 0
+        assert splits["fused"] == (0 if fused_ran else 1)   # one profiled scope covers both splits
+    else:
+        assert splits["fusea"] == 1                           # B's split (or both, on the fallback)
 
 
-def test_fused_split_kernel_partial_f64(cuda, handle, monkeypatch):
-    """The FP64 partial output of the fused kernel (K-split building block) equals the pre-split kernel's."""
+@pytest.mark.parametrize("variant", ["fused", "fusea"])
+def test_fused_split_kernel_partial_f64(cuda, handle, monkeypatch, variant):
+    """The FP64 partial output of the fused kernels (K-split building block) equals the pre-split kernel's."""
     torch = cuda
     M, N, K = 300, 260, 1536
     A = dev(torch, datagen.normal((M, K), 80))
     B = dev(torch, datagen.normal((K, N), 81))
     out = {}
-    for variant in ("pair", "fused"):
-        monkeypatch.setenv("EMUGEMM_TC_KERNEL", variant)
+    for variant_ in ("pair", variant):
+        monkeypatch.setenv("EMUGEMM_TC_KERNEL", variant_)
         P = torch.full((M, N), float("nan"), dtype=torch.float64, device="cuda")
         handle.partial_f64(M, N, K, A, K, B, N, P, emugemm.BF16X3, 1)
         handle.sync()
-        out[variant] = P.cpu().numpy()
-    assert np.isfinite(out["fused"]).all()
-    assert np.array_equal(out["fused"], out["pair"])
+        out[variant_] = P.cpu().numpy()
+    assert np.isfinite(out[variant]).all()
+    assert np.array_equal(out[variant], out["pair"])
 
 
 @pytest.mark.parametrize("force", [emugemm.BF16X3, emugemm.FP16X3, emugemm.NATIVE_FP32])
