@@ -15,9 +15,11 @@
 // a warpgroup at the top of its branch: launch 512 threads x 128 = 65536 registers; epilogue warpgroups grow to
 // 176, the others shrink to 80 (2*128*176 + 2*128*80 = 65536). EMUGEMM_FUSED_WARPS = 12: warps 2..9 epilogue,
 // 10-11 converters, 168 registers each, no rebalancing.
-// Signalling: fp32 ring local to each CTA; bf16 stages of both CTAs are announced on the leader's bf_full
-// (one arrive per converter warp, the peer's remotely) after a generic->async proxy fence; the leader's commits free
-// the bf16 stages and publish TMEM chunks in both CTAs. All waits are bounded.
+// Signalling: fp32 ring local to each CTA; bf16 stages of both CTAs are announced on the leader's bf_full after a
+// generic->async proxy fence: the leader's converter warps arrive locally (one arming 16 bytes per peer converter
+// warp), the peer's each send a 16-byte cp.async.bulk that completes those bytes on the leader's barrier (a
+// thread-issued remote arrive with release at cluster scope stalls its warp for ~1200 cycles). The leader's commits
+// free the bf16 stages and publish TMEM chunks in both CTAs. All waits are bounded.
 #include "device_utils.cuh"
 #include "emugemm_internal.h"
 
@@ -69,13 +71,15 @@ constexpr uint32_t kIdesc = idesc_f16(2 * kBM, kBN, true);
 struct CtlF {
     uint64_t f32_full[kF32Stages];
     uint64_t f32_empty[kF32Stages];
-    uint64_t bf_full[kBfStages];     // leader: every converter warp of both CTAs
+    uint64_t bf_full[kBfStages];     // leader: its converter warps arrive; the peer's deliver 16 bytes each
     uint64_t bf_empty[kBfStages];    // both: leader's commit
     uint64_t tmem_full[2];
     uint64_t tmem_empty[2];
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
+    alignas(16) uint32_t sig_src[4];              // source of the peer's 16-byte signals (contents unused)
+    alignas(16) uint32_t sig_dst[kConvWarps][4];  // leader: landing slots, one per peer converter warp
 };
 
 struct KParamsF {
@@ -161,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&ctl->f32_empty[s], kConvWarps);
         }
         for (int s = 0; s < kBfStages; ++s) {
-            mbar_init(&ctl->bf_full[s], 2 * kConvWarps);
+            mbar_init(&ctl->bf_full[s], kConvWarps);
             mbar_init(&ctl->bf_empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -243,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const uint64_t a_lo = sdesc_kmajor(st + kBfA, 64);
                             const uint64_t b_hi = sdesc_kmajor(st + 2 * kBfA, 64);
                             const uint64_t b_lo = sdesc_kmajor(st + 2 * kBfA + kBfB, 64);
-    #pragma unroll
+#pragma unroll
                             for (int ks = 0; ks < kBK / 16; ++ks) {
                                 const uint64_t adv = (uint64_t)(ks * 32) >> 4;
                                 const uint32_t acc = (kb != kb0 || ks != 0) ? 1u : 0u;
@@ -267,6 +271,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             // ---------------- converters: FP32 stage -> bf16 hi/lo stage (both operands K-major) ----------------
             const int ct = (warp < kEpiFirst ? warp - 2 : warp - 2 - kEpiWarps) * 32 + lane;   // 0 .. kConvThreads-1
             const uint32_t lead_bf_full0 = mapa_shared(smem_u32(&ctl->bf_full[0]), 0);
+            const int cw = ct >> 5;   // converter warp index
+            const uint32_t lead_slot = mapa_shared(smem_u32(&ctl->sig_dst[cw][0]), 0);
+            const uint32_t sig_src = smem_u32(&ctl->sig_src[0]);
             constexpr int kPer = (1024 + kConvThreads - 1) / kConvThreads;   // items per thread and k-block
             constexpr int kBatch = 3;                                        // items loaded before any is stored
             long it = 0;
@@ -286,11 +293,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // 1024 items of 8 values: A rows x 4 k-groups (0..511), then B columns x 4 k-groups
                     // (512..1023). A warp's 32 items are consecutive, so no warp mixes A and B; the 64-byte
                     // swizzle makes both store patterns (4 lanes per A row, one lane per B column) conflict-free.
-    #pragma unroll
+#pragma unroll
                     for (int i0 = 0; i0 < kPer; i0 += kBatch) {
                         float x[kBatch][8];
                         uint32_t dst[kBatch];   // offset of the hi chunk in the stage; lo is kBfA further
-    #pragma unroll
+#pragma unroll
                         for (int i = 0; i < kBatch; ++i) {
                             const int item = ct + (i0 + i) * kConvThreads;
                             if (i0 + i >= kPer || item >= 1024) continue;
@@ -305,12 +312,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                             } else {
                                 const int i2 = item - 512;
                                 const int r = i2 & (kBNH - 1), g = i2 >> 7;   // column n of this CTA's B, k-group
-    #pragma unroll
+#pragma unroll
                                 for (int j = 0; j < 8; ++j) x[i][j] = fb[(8 * g + j) * kBNH + r];
                                 dst[i] = (uint32_t)(2 * kBfA) + sw64(r, g);
                             }
                         }
-    #pragma unroll
+#pragma unroll
                         for (int i = 0; i < kBatch; ++i) {
                             const int item = ct + (i0 + i) * kConvThreads;
                             if (i0 + i >= kPer || item >= 1024) continue;
@@ -321,11 +328,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                     // each thread makes its slice writes visible to the tensor cores' async proxy; the warp
-                    // barrier orders all lanes' writes before lane 0's release-arrive on the leader
+                    // barrier orders all lanes' writes before lane 0's signal to the leader
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        mbar_arrive_cluster(lead_bf_full0 + (uint32_t)(q * sizeof(uint64_t)));
+                        if (leader) {
+                            if (cw == 0) mbar_arrive_expect_tx(&ctl->bf_full[q], 16 * kConvWarps);
+                            else mbar_arrive(&ctl->bf_full[q]);
+                        } else {
+                            bulk_signal_cluster(lead_slot, sig_src, 16, lead_bf_full0 + (uint32_t)(q * sizeof(uint64_t)));
+                        }
                         mbar_arrive(&ctl->f32_empty[s]);
                     }
                 }
