@@ -64,6 +64,9 @@ struct Cfg {
     static constexpr int HALF = BN / 2;                     // columns per epilogue thread
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*control*/;
     static constexpr uint32_t IDESC = idesc_f16(kBM, BN, !FP16);
+    // fp16: A_hi x [B_hi | B_lo] as one MMA of twice the width (the two B slices are adjacent in the stage and the
+    // two accumulators adjacent in TMEM), so A_hi is read from shared memory once per k16 step instead of twice
+    static constexpr uint32_t IDESC2 = idesc_f16(kBM, 2 * BN, !FP16);
 };
 
 struct Ctl {
@@ -203,9 +206,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int ks = 0; ks < kBK / 16; ++ks) {
                             const uint64_t adv = (uint64_t)(ks * 32) >> 4;   // 16 elements = 32 bytes along K
                             const uint32_t acc = (kb != kb0 || ks != 0) ? 1u : 0u;
-                            mma_f16_ss(d_cross, a_lo + adv, b_hi + adv, C_::IDESC, acc);
-                            mma_f16_ss(d_cross, a_hi + adv, b_lo + adv, C_::IDESC, 1u);
-                            mma_f16_ss(d_main, a_hi + adv, b_hi + adv, C_::IDESC, FP16 ? acc : 1u);
+                            if (FP16) {
+                                // columns [main, main+BN) += hi*hi, [main+BN, main+2BN) = cross += hi*lo; then lo*hi
+                                mma_f16_ss(d_main, a_hi + adv, b_hi + adv, C_::IDESC2, acc);
+                                mma_f16_ss(d_cross, a_lo + adv, b_hi + adv, C_::IDESC, 1u);
+                            } else {
+                                mma_f16_ss(d_cross, a_lo + adv, b_hi + adv, C_::IDESC, acc);
+                                mma_f16_ss(d_cross, a_hi + adv, b_lo + adv, C_::IDESC, 1u);
+                                mma_f16_ss(d_main, a_hi + adv, b_hi + adv, C_::IDESC, 1u);
+                            }
                         }
                         mma_commit(&ctl->empty[s]);
                     }

@@ -328,8 +328,10 @@ def test_a_is_reused_reuses_the_split(cuda, handle):
 @pytest.mark.parametrize("shape", [(256, 256, 128), (300, 520, 1000), (1024, 768, 2048), (1, 1, 1), (2048, 2048, 512),
                                    (256, 256, 20000)])
 def test_pair_kernel_matches_single_cta_kernel(cuda, handle, monkeypatch, force, shape):
-    """The CTA-pair kernel (cta_group::2) computes every output from the same slices and k-steps as the
-    single-CTA kernel: identical bits."""
+    """bf16x3: the CTA-pair kernel (cta_group::2) computes every output from the same slices and k-steps as the
+    single-CTA kernel: identical bits. fp16x3: the single-CTA kernel forms hi*hi and hi*lo with one MMA of twice the
+    width (A_hi x [B_hi | B_lo]), so its cross terms accumulate in another order; both kernels must then sit
+    within the accumulation bound of the exact slice products."""
     torch = cuda
     M, N, K = shape
     A = datagen.normal((M, K), 60 + M)
@@ -340,7 +342,14 @@ def test_pair_kernel_matches_single_cta_kernel(cuda, handle, monkeypatch, force,
         C, p, _ = run_sgemm(torch, handle, A, B, force=force, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
         out[variant] = C
     assert np.isfinite(out["pair"]).all()
-    assert np.array_equal(out["pair"], out["single"])
+    if force == emugemm.BF16X3:
+        assert np.array_equal(out["pair"], out["single"])
+    else:
+        Rh = oracle.slice_product(A, B, kind=1)
+        R = oracle.gemm_f64(A, B)
+        for v in ("pair", "single"):
+            d = np.linalg.norm(out[v].astype(np.float64) - Rh) / max(np.linalg.norm(R), 1e-300)
+            assert d <= _accum_bound(K), (v, d)
 
 
 @pytest.mark.parametrize("variant", ["fused", "fusea"])
