@@ -82,15 +82,17 @@ def ffma_peak() -> tuple[float, str]:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 100 ms by a reader thread; only samples that arrive
-    between mark_start() and mark_end() (the timed region) are summarised."""
+    """nvidia-smi clocks and throttle reasons of the job's GPUs sampled every 100 ms by one process and a reader
+    thread (on rank 0 only; the other ranks pass enabled=False); only samples that arrive between mark_start() and
+    mark_end() (the timed region) are summarised, over all the GPUs sampled."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, indices, enabled: bool = True):
+        self.indices = list(indices)
+        self.enabled = enabled
         self.proc = None
         self.lines = []
         self.t0 = self.t1 = None
@@ -98,9 +100,11 @@ class ClockSampler:
     def __enter__(self):
         import threading
 
+        if not self.enabled:
+            return self
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+            self.proc = subprocess.Popen(["nvidia-smi", "--id=" + ",".join(str(i) for i in self.indices),
+                                          f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -342,11 +346,12 @@ def ours(args) -> None:
         scaling = "strong"
         desc = f"{args.scheme} emulated SGEMM {M}x{N}x{K}, K split over {world} GPU(s), FP64 partials reduced"
 
+        P = torch.empty((M, N), dtype=torch.float64, device="cuda")
+
         def step():
             if dist is not None:
-                multigpu.k_split(A, B, C, M=M, N=N, handle=h, scheme=scheme)
+                multigpu.k_split(A, B, C, M=M, N=N, handle=h, scheme=scheme, P=P)
             else:
-                P = torch.empty((M, N), dtype=torch.float64, device="cuda")
                 h.partial_f64(M, N, k_loc, A, k_loc, B, N, P, scheme, 1)
                 h.reduce_f64(M, N, 1, P, C)
 
@@ -359,7 +364,8 @@ def ours(args) -> None:
     launches0 = emugemm.launch_count()
     h.profile_begin()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    # one sampler process, on rank 0, for every GPU of the job (eight samplers competed for the host's cores)
+    with ClockSampler(range(world) if world > 1 else [local], enabled=(rank == 0)) as clk:
         clk.mark_start()
         ev0.record(stream)
         for _ in range(args.steps):

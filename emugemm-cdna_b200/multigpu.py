@@ -92,11 +92,12 @@ def row_sharded(A_local: torch.Tensor, B: torch.Tensor, C_local: torch.Tensor, *
 
 def k_split(A_local: torch.Tensor, B_local: torch.Tensor, C: torch.Tensor | None, *, M: int, N: int,
             partial: Callable | None = None, reduce: Callable | None = None, handle=None, scheme: int = 3,
-            chunks: int = 1, all_ranks: bool = False, group=None) -> torch.Tensor:
+            chunks: int = 1, all_ranks: bool = False, group=None, P: torch.Tensor | None = None) -> torch.Tensor:
     """C = sum over ranks of A_local * B_local, partials in FP64 summed by NCCL, one rounding to FP32.
 
     A_local: (M x Kg), B_local: (Kg x N). Returns the FP64 sum (valid on rank 0, or on all ranks with
-    all_ranks=True); C (M x N, FP32) is written on the ranks where the sum is valid."""
+    all_ranks=True); C (M x N, FP32) is written on the ranks where the sum is valid. P: optional (M x N) FP64
+    buffer for the partial and the sum, reused across calls (the partial overwrites all of it)."""
     if partial is None:
         def partial(M_, N_, K_, A_, B_, P_):
             handle.partial_f64(M_, N_, K_, A_, K_, B_, N_, P_, scheme, chunks)
@@ -104,9 +105,12 @@ def k_split(A_local: torch.Tensor, B_local: torch.Tensor, C: torch.Tensor | None
         def reduce(M_, N_, P_, C_):
             handle.reduce_f64(M_, N_, 1, P_, C_)
     Kg = A_local.shape[1]
-    P = torch.zeros((M, N), dtype=torch.float64, device=A_local.device)
+    if P is None:
+        P = torch.zeros((M, N), dtype=torch.float64, device=A_local.device)
     if Kg > 0:
         partial(M, N, Kg, A_local, B_local, P)
+    else:
+        P.zero_()
     if all_ranks:
         dist.all_reduce(P, op=dist.ReduceOp.SUM, group=group)
     else:

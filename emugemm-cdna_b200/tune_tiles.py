@@ -112,7 +112,7 @@ def main():
     else:
         sizes = (1024, 2048, 4096, 8192, 16384)
         grid = list(itertools.product(sizes, sizes, (1024, 4096, 16384, 65536), ("bf16", "fp16", "fp32")))
-        grid = [g for g in grid if g[0] * g[1] * g[2] <= 8192 ** 3 * 4]
+        grid = [g for g in grid if g[0] * g[1] * g[2] <= 8192 ** 3 * 2]
     path = pathlib.Path(args.table)
     done = existing_keys(path)
     with emugemm.Handle() as h:

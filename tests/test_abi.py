@@ -4,6 +4,7 @@ The tile-table loader's arch rejection (src/emugemm.cpp:107-128) is exercised wi
 from __future__ import annotations
 
 import ctypes
+import pathlib
 import subprocess
 import sys
 
@@ -109,3 +110,22 @@ def test_reference_table_is_rejected_on_b200():
     assert lib.emugemm_init_for_arch(str(ref_csv).encode(), b"gfx90a:sramecc+:xnack-") == 0
     assert lib.emugemm_tune_rows() == 820
     lib.emugemm_shutdown()
+
+
+def test_committed_b200_tile_table():
+    """The per-shape B200 table that tune_tiles.py measured: every row valid for sm_100a, rejected for another
+    arch, and the lookup returns the measured winners."""
+    lib = emugemm.lib()
+    table = str(pathlib.Path(__file__).resolve().parent.parent / "emugemm-cdna_b200" / "tiles_b200.csv")
+    try:
+        assert lib.emugemm_init_for_arch(table.encode(), b"sm_100a") == 0
+        assert lib.emugemm_tune_rows() == 261
+        assert lib.emugemm_tune_lookup(2048, 1024, 16384, 1) == 4        # bf16x3: A split into TMEM
+        assert lib.emugemm_tune_lookup(1024, 1024, 16384, 1) == 2        # bf16x3: CTA pairs
+        assert lib.emugemm_tune_lookup(16384, 16384, 1024, 1) == 1       # bf16x3, short K: single CTA
+        assert lib.emugemm_tune_lookup(8192, 8192, 4096, 2) == 1         # fp16x3: single CTA
+        assert lib.emugemm_tune_lookup(1024, 2048, 4096, 0) == 128       # FP32 tile edge
+        assert lib.emugemm_init_for_arch(table.encode(), b"sm_90a") == 0
+        assert lib.emugemm_tune_rows() == 0
+    finally:
+        lib.emugemm_shutdown()
