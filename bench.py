@@ -357,15 +357,17 @@ def ours(args) -> None:
 
     for _ in range(args.warmup):
         step()
-    torch.cuda.synchronize()
-    if dist is not None:
-        dist.barrier()
-    torch.cuda.synchronize()
-    launches0 = emugemm.launch_count()
-    h.profile_begin()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # one sampler process, on rank 0, for every GPU of the job (eight samplers competed for the host's cores)
+    # One sampler process, on rank 0, for every GPU of the job. It is started (and has delivered its first sample)
+    # before the barrier, so that every rank leaves the barrier and starts its clock together: a rank that starts
+    # timing while another still waits for its sampler measures that wait inside its first collective.
     with ClockSampler(range(world) if world > 1 else [local], enabled=(rank == 0)) as clk:
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        launches0 = emugemm.launch_count()
+        h.profile_begin()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         clk.mark_start()
         ev0.record(stream)
         for _ in range(args.steps):
