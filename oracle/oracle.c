@@ -1,6 +1,6 @@
 /* oracle.c - CPU restatement of the emugemm hot path, used ONLY as test infrastructure: by tests/, by
- * __graft_entry__.smoke() as the checker, and by bench.py's cpu_baseline / reference leg. Nothing in the
- * library links or calls it.
+ * __graft_entry__.smoke() to check the device result, and by bench.py's cpu_baseline / reference leg. Nothing
+ * in the library links or calls it.
  *
  * Each function restates the emugemm-cdna algorithm it checks (file:line in that project):
  *   orc_split_bf16 / orc_split_f16   src/emugemm.cpp:143-148   (bf16: RNE as in CUDA/HIP __float2bfloat16)

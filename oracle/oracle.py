@@ -1,7 +1,7 @@
 """Test infrastructure: Python access to the CPU oracle (liboracle.so, from oracle.c) and to the
 reference's own planner (_ref/libemuref.so, compiled from emugemm-cdna's src/emugemm.cpp by the Makefile
-here). Only tests/, __graft_entry__.smoke() and bench.py's CPU baseline leg use this module, as the
-checker; the library never does.
+here). Only tests/, __graft_entry__.smoke() and bench.py's CPU baseline leg use this module, to check
+results and to time the CPU path; the library never does.
 
 Parity status: the split rule, absmax, exponent rule, FP32 chunk chains and the Hutchinson estimate are
 restated from the reference source; the planner is pinned against the reference planner itself (golden

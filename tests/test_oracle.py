@@ -1,4 +1,4 @@
-"""Pins of the CPU oracle before it is trusted as the checker of the GPU kernels.
+"""Pins of the CPU oracle before it is trusted to check the GPU kernels.
 
 - split rule: known-answer bit patterns, and the identities hi + lo == x for every x whose residual fits
 - bf16x3 representation floor: with exact FP64 slice products the normwise error of iid N(0,1) data is
