@@ -46,7 +46,7 @@ static const ModelConsts kRefMI250 = {
 // Speed ratios: 8192^3 kernel time of the FP32 SIMT kernel (the NATIVE_FP32 path, 44.5 TFLOPS) over that of
 // the tensor-core kernel (bf16x3 11.7x, fp16x3 6.7x), rounded down; hbm_bps is the split's effective rate.
 // fp16x3 scales each row of A and column of B by a power of two before splitting, so its range test only
-// excludes zero and non-finite magnitudes.
+// excludes zero and non-finite magnitudes. The measurements and raw fits are in calibration_b200.json.
 static const ModelConsts kB200 = {
     "b200",
     /*a_fp32*/ 2.02e-8, /*a_lowp*/ 3.0e-9, /*a_fp16x3*/ 1.7e-9,
