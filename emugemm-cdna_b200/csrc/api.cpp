@@ -164,6 +164,36 @@ static long round_up(long x, long m) { return (x + m - 1) / m * m; }
 // table (tiles_b200.csv): bf16x3 on CTA pairs when K > 1024 (pairs won at every K >= 4096 of the table, by up to
 // 17 % at small M, N; single-CTA tiles won at K = 1024, by up to 9 %), fp16x3 on single-CTA 128 x 128 tiles (all
 // 87 fp16 shapes of the table).
+// EMUGEMM_LOG (set and not "0"): one stderr line per GEMM with the plan (scheme, chunks, predicted error, reason)
+// and one per tensor-core launch with the kernel chosen. The reference's observable decision record is plan.reason;
+// this makes it and the kernel choice visible without changing the API.
+static bool log_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("EMUGEMM_LOG");
+        return e && *e && std::strcmp(e, "0") != 0;
+    }();
+    return on;
+}
+
+static const char* scheme_name(emu_scheme_t s) {
+    switch (s) {
+        case EMU_SCHEME_AUTO: return "AUTO";
+        case EMU_SCHEME_NATIVE_FP32: return "NATIVE_FP32";
+        case EMU_SCHEME_FP32_CHUNKED: return "FP32_CHUNKED";
+        case EMU_SCHEME_BF16X3: return "BF16X3";
+        case EMU_SCHEME_FP16X3: return "FP16X3";
+        case EMU_SCHEME_BF16X6: return "BF16X6";
+        default: return "?";
+    }
+}
+
+static void log_plan(const char* entry, int M, int N, long K, const emu_plan_t& p, const emu_hints_t& hn) {
+    if (!log_enabled()) return;
+    std::fprintf(stderr, "emugemm: %s M=%d N=%d K=%ld scheme=%s chunks=%d predicted_err=%.4e rho=%g reason=\"%s\"\n",
+                 entry, M, N, K, scheme_name(p.chosen), p.chunks, p.predicted_err, (double)hn.rho,
+                 p.reason ? p.reason : "");
+}
+
 static int tc_kernel_choice(Handle* h, int M, int N, long K, bool fp16) {
     const char* v = std::getenv("EMUGEMM_TC_KERNEL");
     int code = 0;
@@ -174,6 +204,11 @@ static int tc_kernel_choice(Handle* h, int M, int N, long K, bool fp16) {
     if (!code) code = lookup_tile(M, N, K, fp16 ? 2 : 1).tc_variant;
     if (!code) code = (!fp16 && K > 1024) ? 2 : 1;
     if (fp16 && code >= 3) code = 2;
+    if (log_enabled()) {
+        static const char* names[] = {"?", "single", "pair", "fused", "fusea"};
+        std::fprintf(stderr, "emugemm: tensor-core kernel=%s (%s) M=%d N=%d K=%ld\n", names[code], fp16 ? "fp16x3" : "bf16x3",
+                     M, N, K);
+    }
     return code;
 }
 
@@ -416,6 +451,7 @@ emugemm_status_t emugemm_sgemm_ex(emugemm_handle_t handle, int M, int N, long K,
     }
     emu_plan_t plan = emu::plan(emu::model(), M, N, K, req, &local);
     if (out_plan) *out_plan = plan;
+    emu::log_plan("sgemm", M, N, K, plan, local);
     return emu::dispatch(h, plan.chosen, plan.chunks, M, N, K, A, lda, B, ldb, C, ldc, nullptr, 0,
                          hints && hints->a_is_reused);
 }
@@ -485,6 +521,7 @@ emugemm_status_t emugemm_sgemm_host(emugemm_handle_t handle, int M, int N, long 
     emu_hints_t local = *hints;
     emu_plan_t plan = emu::plan(emu::model(), M, N, K, req, &local);
     if (out_plan) *out_plan = plan;
+    emu::log_plan("sgemm_host", M, N, K, plan, local);
     // Column panels: A crosses PCIe once and is split once (later panels reuse its slices); panel j of B
     // travels on copy_in, its GEMM runs on the handle's stream as soon as it has landed, and panel j of C
     // travels back on copy_out while later panels of B arrive (PCIe carries both directions at once).

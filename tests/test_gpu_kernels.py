@@ -422,3 +422,31 @@ def test_sgemm_host_matches_device(cuda, handle, force, shape):
         handle.sync()
         assert p.chosen == force
         assert np.array_equal(hC.numpy(), want), (shape, use)
+
+
+def test_log_lines(cuda):
+    """EMUGEMM_LOG=1: one stderr line per GEMM with the plan (scheme, chunks, predicted error, reason) and one per
+    tensor-core launch with the kernel chosen."""
+    import subprocess
+    import sys
+    import textwrap
+
+    code = textwrap.dedent("""
+        import sys, torch
+        sys.path.insert(0, "emugemm-cdna_b200")
+        import emugemm
+        A = torch.randn(256, 512, device="cuda"); B = torch.randn(512, 384, device="cuda")
+        C = torch.empty(256, 384, device="cuda")
+        with emugemm.Handle() as h:
+            h.sgemm(256, 384, 512, A, B, C, force=emugemm.BF16X3, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+            h.sync()
+    """)
+    import os
+    import pathlib
+    root = pathlib.Path(__file__).resolve().parent.parent
+    env = dict(os.environ, EMUGEMM_LOG="1")
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    lines = [l for l in r.stderr.splitlines() if l.startswith("emugemm: ")]
+    assert any("sgemm M=256 N=384 K=512 scheme=BF16X3 chunks=1" in l and 'reason="forced"' in l for l in lines), lines
+    assert any("tensor-core kernel=single (bf16x3) M=256 N=384 K=512" in l for l in lines), lines
