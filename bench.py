@@ -427,8 +427,12 @@ def ours(args) -> None:
 
     # end to end: host inputs (pinned) through emugemm_sgemm_host, whose H2D of A and B and D2H of C are inside
     # every step (B and C in column panels overlapped with the panel GEMMs)
+    # With N GPUs every rank runs emugemm_sgemm_host on its own pinned rows of A and its own pinned copy of B (the
+    # host-buffer product of its row block, no collective); the job's time is the slowest rank's.
     e2e = None
-    if not args.no_e2e and world == 1 and wl == "square":
+    if not args.no_e2e and wl == "square":
+        if dist is not None:
+            dist.broadcast(B, src=0)
         hA = A.cpu().pin_memory()
         hB = B.cpu().pin_memory()
         hC = torch.empty((M, N), dtype=torch.float32).pin_memory()
@@ -439,6 +443,9 @@ def ours(args) -> None:
         for _ in range(2):
             e2e_step()
         torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
         n_e2e = max(3, min(30, args.steps // 4))
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -447,9 +454,14 @@ def ours(args) -> None:
         e1.record(stream)
         torch.cuda.synchronize()
         e_ms = e0.elapsed_time(e1) / n_e2e
-        e2e = {"value": 2.0 * M * N * K / (e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
-               "h2d_bytes_per_step": int(hA.numel() * 4 + hB.numel() * 4), "d2h_bytes_per_step": int(hC.numel() * 4),
-               "ms_per_step": e_ms}
+        if dist is not None:
+            t = torch.tensor([e_ms], device="cuda", dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e2e = {"value": 2.0 * M * N * K * world / (e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
+               "h2d_bytes_per_step": int(hA.numel() * 4 + hB.numel() * 4) * world,
+               "d2h_bytes_per_step": int(hC.numel() * 4) * world, "ms_per_step": e_ms,
+               "path": "emugemm_sgemm_host per rank: pinned host A rows and B in, C rows out, inside every step"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and wl == "square":
