@@ -450,3 +450,30 @@ def test_log_lines(cuda):
     lines = [l for l in r.stderr.splitlines() if l.startswith("emugemm: ")]
     assert any("sgemm M=256 N=384 K=512 scheme=BF16X3 chunks=1" in l and 'reason="forced"' in l for l in lines), lines
     assert any("tensor-core kernel=single (bf16x3) M=256 N=384 K=512" in l for l in lines), lines
+
+
+def test_committed_tile_table_dispatch(cuda, handle, monkeypatch):
+    """With the measured B200 table loaded, a shape whose row names the fused-A kernel runs it (the log says so)
+    and gives the pair kernel's bits; without the table the built-in choice runs."""
+    import pathlib
+
+    torch = cuda
+    lib = emugemm.lib()
+    table = pathlib.Path(__file__).resolve().parent.parent / "emugemm-cdna_b200" / "tiles_b200.csv"
+    M, N, K = 2048, 1024, 16384
+    assert lib.emugemm_tune_lookup(M, N, K, 1) == 0          # no table yet
+    A = datagen.normal((M, K), 97)
+    B = datagen.normal((K, N), 98)
+    monkeypatch.setenv("EMUGEMM_TC_KERNEL", "pair")
+    ref, _, _ = run_sgemm(torch, handle, A, B, force=emugemm.BF16X3, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+    monkeypatch.delenv("EMUGEMM_TC_KERNEL")
+    try:
+        assert lib.emugemm_init(str(table).encode()) == 0
+        assert lib.emugemm_tune_lookup(M, N, K, 1) == 4
+        n0 = emugemm.launch_count()
+        C, p, _ = run_sgemm(torch, handle, A, B, force=emugemm.BF16X3, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+        launches = emugemm.launch_count() - n0
+    finally:
+        lib.emugemm_shutdown()
+    assert launches == 2                   # B's split and the fused-A GEMM (the pre-split path launches 3)
+    assert np.array_equal(C, ref)
