@@ -197,6 +197,134 @@ __global__ void __launch_bounds__(kThr) k_fp32_gemm(Params p) {
     }
 }
 
+// 32 x 32 and 64 x 64 tiles (2 x 2 / 4 x 4 chains per thread) with the operands streamed through a cp.async ring,
+// for products with few output tiles (C3: M = N = 256) and mid-size ones. (At the 128 tile the register-staged
+// k_fp32_gemm stays: the ring version measured 41.8 against 44.5 TFLOP/s at 8192^3.) A register-staged k-block of prefetch left
+// the global-load latency exposed on every k-block when a thread has few FMAs per loaded value; the ring keeps
+// STAGES - 1 k-blocks of 16 in flight. Shared tiles keep the global layouts (A [m][k], B [k][n]): per four k a
+// thread reads its TM rows of A as float4 along k and, per k, its TM columns of B as one vector, then runs the
+// same chains (k ascending per element) with the same FP64 folds as k_fp32_gemm. Needs the VEC conditions
+// (16-byte aligned rows, K, N and the chunk length multiples of 4), so no 16-byte copy straddles a bound.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc, bool valid) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+    const int n = valid ? 16 : 0;   // 0 source bytes: the 16 destination bytes are zero-filled
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(gsrc), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int BM, int STAGES>
+__global__ void __launch_bounds__(kThr) k_fp32_gemm_cp(Params p) {
+    constexpr int TM = BM / 16;                          // chains per thread along m and along n
+    constexpr int A_CH = BM * 4, CH = 8 * BM;            // 16-byte copies: A (BM rows x 4), A + B
+    constexpr int CPT = CH / kThr;                       // copies per thread per k-block
+    static_assert(CH % kThr == 0 && (TM == 2 || TM == 4 || TM == 8), "tile shape");
+    __shared__ __align__(16) float As[STAGES][BM][16];   // [m][k]
+    __shared__ __align__(16) float Bs[STAGES][16][BM];   // [k][n]
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BM;
+    const int g = blockIdx.z;
+    const int c_first = g * p.cpg;
+    const int c_last = min(p.ce, c_first + p.cpg);
+    double* Wg = p.W ? p.W + (size_t)g * p.M * p.N : nullptr;
+
+    for (int ci = c_first; ci < c_last; ++ci) {
+        const long kbeg = (long)ci * p.kc;
+        const long kend = min(p.K, kbeg + p.kc);
+        const long nkb = (kend - kbeg + 15) / 16;
+        auto issue = [&](long kt) {
+            const int st = (int)(kt % STAGES);
+            const long k = kbeg + kt * 16;
+#pragma unroll
+            for (int c = 0; c < CPT; ++c) {
+                const int f = tid + c * kThr;
+                if (f < A_CH) {
+                    const int r = f >> 2, q = f & 3;
+                    const int m = m0 + r;
+                    const long kk = k + q * 4;
+                    const bool v = m < p.M && kk < kend;
+                    cp_async16(&As[st][r][q * 4], v ? (const void*)(p.A + (size_t)m * p.lda + kk) : (const void*)p.A,
+                               v);
+                } else {
+                    const int f2 = f - A_CH;
+                    const int kr = f2 / (BM / 4), q = f2 % (BM / 4);
+                    const long kk = k + kr;
+                    const int n = n0 + q * 4;
+                    const bool v = kk < kend && n < p.N;
+                    cp_async16(&Bs[st][kr][q * 4], v ? (const void*)(p.B + (size_t)kk * p.ldb + n) : (const void*)p.B,
+                               v);
+                }
+            }
+        };
+        float acc[TM][TM];
+#pragma unroll
+        for (int i = 0; i < TM; ++i)
+#pragma unroll
+            for (int j = 0; j < TM; ++j) acc[i][j] = 0.f;
+        for (int kt = 0; kt < STAGES - 1; ++kt) {
+            if (kt < nkb) issue(kt);
+            cp_async_commit();
+        }
+        for (long kt = 0; kt < nkb; ++kt) {
+            if (kt + STAGES - 1 < nkb) issue(kt + STAGES - 1);
+            cp_async_commit();
+            cp_async_wait<STAGES - 1>();   // k-block kt has landed (this thread's copies)
+            __syncthreads();               // ... and every thread's
+            const int st = (int)(kt % STAGES);
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4) {
+                float4 a[TM];
+#pragma unroll
+                for (int i = 0; i < TM; ++i) a[i] = *reinterpret_cast<const float4*>(&As[st][ty * TM + i][k4 * 4]);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    float b[TM];
+                    if (TM == 2) {
+                        const float2 v = *reinterpret_cast<const float2*>(&Bs[st][k4 * 4 + kk][tx * TM]);
+                        b[0] = v.x; b[1] = v.y;
+                    } else {
+#pragma unroll
+                        for (int h = 0; h < TM / 4; ++h) {
+                            const float4 v = *reinterpret_cast<const float4*>(&Bs[st][k4 * 4 + kk][tx * TM + 4 * h]);
+                            b[4 * h] = v.x; b[4 * h + 1] = v.y; b[4 * h + 2] = v.z; b[4 * h + 3] = v.w;
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < TM; ++i) {
+                        const float av = kk == 0 ? a[i].x : kk == 1 ? a[i].y : kk == 2 ? a[i].z : a[i].w;
+#pragma unroll
+                        for (int j = 0; j < TM; ++j) acc[i][j] = __fmaf_rn(av, b[j], acc[i][j]);
+                    }
+                }
+            }
+            __syncthreads();               // stage st is refilled by a later iteration
+        }
+        cp_async_wait<0>();
+        // fold this chunk's FP32 partials into the FP64 sum of the group (as in k_fp32_gemm)
+        const bool first = (ci == c_first), last = (ci == c_last - 1);
+#pragma unroll
+        for (int i = 0; i < TM; ++i) {
+            const int m = m0 + ty * TM + i;
+            if (m >= p.M) continue;
+#pragma unroll
+            for (int j = 0; j < TM; ++j) {
+                const int n = n0 + tx * TM + j;
+                if (n >= p.N) continue;
+                const size_t wi = (size_t)m * p.N + n;
+                const double s = first ? (double)acc[i][j] : Wg[wi] + (double)acc[i][j];
+                if (last && p.G == 1) {
+                    if (p.C64) p.C64[(size_t)m * p.ldc64 + n] = s;
+                    else p.C[(size_t)m * p.ldc + n] = (float)s;
+                } else {
+                    Wg[wi] = s;
+                }
+            }
+        }
+    }
+}
+
 __global__ void k_reduce_f64(const double* __restrict__ P, int G, int M, int N, long ldp_plane, float* C,
                              long ldc, double* C64, long ldc64) {
     const size_t total = (size_t)M * N;
@@ -287,10 +415,10 @@ int launch_fp32_gemm(const Fp32GemmArgs& a, void* stream) {
         if (vec) launch_cfg<128, 8, true>(p, grid, st);
         else launch_cfg<128, 8, false>(p, grid, st);
     } else if (s.bm == 64) {
-        if (vec) launch_cfg<64, 4, true>(p, grid, st);
+        if (vec) k_fp32_gemm_cp<64, 5><<<grid, kThr, 0, st>>>(p);
         else launch_cfg<64, 4, false>(p, grid, st);
     } else if (s.bm == 32) {
-        if (vec) launch_cfg<32, 2, true>(p, grid, st);
+        if (vec) k_fp32_gemm_cp<32, 8><<<grid, kThr, 0, st>>>(p);
         else launch_cfg<32, 2, false>(p, grid, st);
     } else {
         return (int)cudaErrorInvalidValue;
