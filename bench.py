@@ -129,6 +129,10 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self.proc:
+            if self.t1 is not None:   # a timed region shorter than the interval: wait for the sample after it
+                deadline = time.time() + 0.3
+                while time.time() < deadline and not any(t > self.t1 for t, _ in self.lines[-2:]):
+                    time.sleep(0.02)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -136,11 +140,23 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
+        """Median SM clock, max clock and active reasons over the samples taken inside the timed region; when the
+        region is shorter than the sampling interval, over the samples nearest to it (the last one before it
+        and the first one after it, each within 0.3 s), marked "window": "nearest"."""
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for t, line in self.lines:
-            if self.t0 is not None and not (self.t0 <= t <= (self.t1 or t)):
-                continue
+        lines = self.lines
+        window = "timed region"
+        if self.t0 is not None:
+            t1 = self.t1 or time.time()
+            inside = [(t, l) for t, l in lines if self.t0 <= t <= t1]
+            if not inside:
+                before = [(t, l) for t, l in lines if self.t0 - 0.3 <= t < self.t0][-1:]
+                after = [(t, l) for t, l in lines if t1 < t <= t1 + 0.3][:1]
+                inside = before + after
+                window = "nearest"
+            lines = inside
+        for t, line in lines:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
@@ -153,7 +169,7 @@ class ClockSampler:
                 if v.lower().startswith("active"):
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "window": window}
 
 
 def cpu_threads() -> int:

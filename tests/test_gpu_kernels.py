@@ -196,14 +196,17 @@ def test_bf16x3_deterministic(cuda, handle):
 
 
 # --------------------------------------------------------------------------------------------- rho
-@pytest.mark.parametrize("shape", [(64, 48, 256), (256, 256, 2048), (130, 70, 1000)])
-def test_rho_estimate_matches_oracle(cuda, handle, shape):
+# (130,70,1000) and 30 probes take the synchronous-load kernel; the others the cp.async ring (16-aligned
+# J), (130,96,1000) one of each, (128,64,4000) several K splits with a short last one.
+@pytest.mark.parametrize("shape,probes", [((64, 48, 256), 64), ((256, 256, 2048), 64), ((130, 70, 1000), 64),
+                                          ((130, 96, 1000), 64), ((128, 64, 4000), 64), ((256, 256, 2048), 30)])
+def test_rho_estimate_matches_oracle(cuda, handle, shape, probes):
     torch = cuda
     M, N, K = shape
     A = datagen.normal((M, K), 5)
     B = datagen.normal((K, N), 6)
-    r = handle.estimate_rho(M, N, K, dev(torch, A), dev(torch, B), 64)
-    ro, _ = oracle.rho_hutchinson(A, B, 64)
+    r = handle.estimate_rho(M, N, K, dev(torch, A), dev(torch, B), probes)
+    ro, _ = oracle.rho_hutchinson(A, B, probes)
     assert r == pytest.approx(ro, rel=1e-4)
 
 
