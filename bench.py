@@ -72,6 +72,23 @@ def peaks():
     return 1590.0, 1400.0, 6650.0, "fallback"
 
 
+def tc_kernel_name(M: int, N: int, K: int, scheme: str) -> str:
+    """The tensor-core kernel the library picks for this shape: EMUGEMM_TC_KERNEL, else the tile table's code, else
+    the built-in rule (CTA pairs for bf16x3 with K > 1024); fp16x3 has no fused variants."""
+    import emugemm
+
+    fp16 = scheme == "fp16x3"
+    env = os.environ.get("EMUGEMM_TC_KERNEL", "")
+    code = {"single": 1, "pair": 2, "fused": 3, "fusea": 4}.get(env) or \
+        emugemm.lib().emugemm_tune_lookup(M, N, K, 2 if fp16 else 1)
+    if not code:
+        code = 2 if (not fp16 and K > 1024) else 1
+    if fp16 and code >= 3:
+        code = 2
+    return {1: "k_tc_gemm", 2: "k_tc_gemm_pair", 3: "k_tc_fused",
+            4: "k_tc_fused_a (+ k_split_cols of B)"}.get(code, "k_tc_gemm")
+
+
 def ffma_peak() -> tuple[float, str]:
     """Nominal FP32 FMA throughput: 148 SMs x 128 FP32 lanes x 2 FLOP per clock at the maximum SM clock."""
     mhz = 1965.0
@@ -254,6 +271,9 @@ def ours(args) -> None:
 
     import emugemm
 
+    # the measured B200 tile table, loaded as the reference's harnesses load theirs (emugemm_init before any GEMM)
+    emugemm.lib().emugemm_init(str(ROOT / "emugemm-cdna_b200" / "tiles_b200.csv").encode())
+
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -409,13 +429,13 @@ def ours(args) -> None:
     # dominant kernel: the tensor-core 3-product GEMM (3 * 2 * m * n * k tensor FLOPs per rank and step), the FP32
     # SIMT GEMM (2 * m * n * k) for the chunked workload, the skinny probe products (4 * P * K * (M + N)) for rho
     if wl == "chunked":
-        kern_key, kern_name, bound = "fp32_gemm", "k_fp32_gemm", "fp32"
+        kern_key, kern_name, bound = "fp32_gemm", "k_fp32_gemm / k_fp32_gemm_cp (+ k_reduce_f64)", "fp32"
         rank_tensor_flop = 2.0 * m_loc * N * k_loc
     elif wl == "rho":
-        kern_key, kern_name, bound = "rho", "k_skinny", "fp32"
+        kern_key, kern_name, bound = "rho", "rho probe (k_omega, k_skinny_cp x2, k_combine[_sq], k_final)", "fp32"
         rank_tensor_flop = 4.0 * args.probes * K * (M + N)
     else:
-        kern_key, kern_name, bound = "tc_gemm", "k_tc_gemm", "tensor"
+        kern_key, kern_name, bound = "tc_gemm", tc_kernel_name(m_loc, N, k_loc, args.scheme), "tensor"
         rank_tensor_flop = 3 * 2.0 * m_loc * N * k_loc
     gemm_ms, gemm_n = prof[kern_key]
     gemm_avg = gemm_ms / max(gemm_n, 1)
@@ -429,9 +449,18 @@ def ours(args) -> None:
     peak = sustained if long_loop else burst
     peak_name = "bf16_tflops_sustained" if long_loop else "bf16_tflops"
     peak_source = f"{peak_name} ({src})"
+    peak_probe = None
     if bound == "fp32":
-        burst, peak_source = ffma_peak()
-        peak = burst
+        # FP32 SIMT kernels: against the FFMA rate measured on this GPU by emugemm_peak_probe (run after the timed
+        # region), else the nominal rate
+        nominal, nominal_src = ffma_peak()
+        try:
+            peak_probe = h.peak_probe(5)
+            burst = peak = peak_probe["ffma_tflops"]
+            peak_source = f"measured FFMA (emugemm_peak_probe, median of 5; {nominal_src}: {nominal:.1f})"
+        except Exception as exc:  # noqa: BLE001 - the nominal figure stands in, and the line says so
+            burst = peak = nominal
+            peak_source = f"{nominal_src} (peak probe failed: {exc})"
     extra = {}
     if wl == "rho":
         # the probe reads A and B once each; its GB/s against the HBM copy bandwidth, for reference
@@ -525,6 +554,7 @@ def ours(args) -> None:
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch at this size"
                          if (wl == "square" and (args.scheme, S) in TRAFFIC) else None},
             "kernel_ms": {k: (v[0] / v[1] if v[1] else None) for k, v in prof.items()},
+            **({"peak_probe": peak_probe} if peak_probe else {}),
             "cpu_baseline": cpu,
             "cublas_sgemm": cublas,
             "e2e": e2e,

@@ -411,6 +411,22 @@ emugemm_status_t emugemm_sync(emugemm_handle_t handle) {
     return emu::sync_check(h);
 }
 
+emugemm_status_t emugemm_peak_probe(emugemm_handle_t handle, int reps, double* rates, int n) {
+    Handle* h = reinterpret_cast<Handle*>(handle);
+    if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
+    if (!rates && n > 0) return EMUGEMM_STATUS_INVALID_POINTER;
+    if (reps < 1 || n < 0) return EMUGEMM_STATUS_INVALID_VALUE;
+    emu::DeviceGuard g(h->device);
+    emugemm_status_t s = emu::sync_check(h);
+    if (s != EMUGEMM_STATUS_SUCCESS) return s;
+    double r[EMU_PEAK_COUNT] = {};
+    const int e = emu::run_peak_probe(reps, h->num_sms, h->err_dev, h->err_host, h->stream, r);
+    if (e == -1) return emu::take_device_error(h);
+    if (e) return emu::from_cuda(e);
+    for (int i = 0; i < n && i < EMU_PEAK_COUNT; ++i) rates[i] = r[i];
+    return EMUGEMM_STATUS_SUCCESS;
+}
+
 void emugemm_shutdown(void) { emu::tune_clear(); }
 
 emugemm_status_t emugemm_sgemm_ex(emugemm_handle_t handle, int M, int N, long K, const float* A, long lda,

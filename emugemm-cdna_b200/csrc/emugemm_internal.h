@@ -121,6 +121,11 @@ void count_launch(unsigned n = 1);
 // ---------------------------------------------------------------------------------------------------
 // Kernel launchers (return a cudaError_t as int; 0 = success).
 
+// k_peak.cu: rates[0..5] = tcgen05 bf16 / fp16 / tf32 TFLOP/s, FFMA, DFMA TFLOP/s, copy GB/s (medians of
+// `reps` interleaved runs). Returns a cudaError_t, or -1 when a tensor-core wait timed out.
+int run_peak_probe(int reps, int num_sms, unsigned* err_dev, const unsigned* err_host, void* stream,
+                   double* rates);
+
 // k_split.cu
 int launch_split_bf16(const float* X, size_t n, uint16_t* hi, uint16_t* lo, void* stream);
 int launch_split_f16(const float* X, size_t n, uint16_t* hi, uint16_t* lo, void* stream);

@@ -96,6 +96,7 @@ _SIGS = {
     "emugemm_estimate_rho": (c_double, [c_void_p, c_int, c_int, c_long, c_void_p, c_void_p, c_int]),
     "emugemm_set_model": (c_int, [ctypes.c_char_p]),
     "emugemm_get_model": (ctypes.c_char_p, []),
+    "emugemm_peak_probe": (c_int, [c_void_p, c_int, P(ctypes.c_double), c_int]),
     "emugemm_absmax": (c_int, [c_void_p, c_void_p, c_size_t, P(c_float)]),
     "emugemm_split_bf16": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     "emugemm_split_f16": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
@@ -244,6 +245,15 @@ class Handle:
 
     def estimate_rho(self, M, N, K, A, B, probes=64) -> float:
         return lib().emugemm_estimate_rho(self.h, M, N, K, _ptr(A), _ptr(B), probes)
+
+    PEAK_NAMES = ("tc_bf16_tflops", "tc_fp16_tflops", "tc_tf32_tflops", "ffma_tflops", "dfma_tflops", "copy_gbs")
+
+    def peak_probe(self, reps: int = 7) -> dict:
+        """Measured peak rates of this GPU (emugemm_peak_probe): tcgen05 bf16 / fp16 / tf32 and FFMA / DFMA in
+        TFLOP/s, device copy in GB/s; medians of `reps` interleaved runs."""
+        out = (ctypes.c_double * len(self.PEAK_NAMES))()
+        check("emugemm_peak_probe", lib().emugemm_peak_probe(self.h, reps, out, len(self.PEAK_NAMES)))
+        return dict(zip(self.PEAK_NAMES, list(out)))
 
     def absmax(self, X, n: int) -> float:
         out = c_float()

@@ -186,6 +186,23 @@ emugemm_status_t emugemm_reduce_f64(emugemm_handle_t handle, int M, int N, int G
 /* Synchronise the handle's stream; returns TIMEOUT if a kernel of this handle gave up a bounded wait. */
 emugemm_status_t emugemm_sync(emugemm_handle_t handle);
 
+/* Peak rates of the handle's GPU, measured by micro-kernels run `reps` times each, interleaved round-robin,
+   median kept (no function of the emugemm-cdna API; the counterpart of its bench/mfma_peak2.cpp probe).
+   rates[EMU_PEAK_TC_*]: tcgen05 MMA TFLOP/s with operands resident in shared memory (bf16, fp16, tf32;
+   FP32 accumulation); rates[EMU_PEAK_FFMA] / [EMU_PEAK_DFMA]: FP32 / FP64 FMA TFLOP/s; rates[EMU_PEAK_HBM_COPY]:
+   device copy GB/s (read + written bytes). Fills the first min(n, EMU_PEAK_COUNT) entries; takes about
+   reps * 4 ms and 2 GiB of device memory while it runs. */
+enum {
+    EMU_PEAK_TC_BF16 = 0,
+    EMU_PEAK_TC_FP16 = 1,
+    EMU_PEAK_TC_TF32 = 2,
+    EMU_PEAK_FFMA = 3,
+    EMU_PEAK_DFMA = 4,
+    EMU_PEAK_HBM_COPY = 5,
+    EMU_PEAK_COUNT = 6
+};
+emugemm_status_t emugemm_peak_probe(emugemm_handle_t handle, int reps, double* rates, int n);
+
 /* emugemm_init with an explicit live arch string instead of the current device's, so the table parser
    and its arch rejection can be exercised without a GPU. */
 emugemm_status_t emugemm_init_for_arch(const char* tune_csv_path, const char* live_arch);

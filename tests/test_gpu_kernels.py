@@ -480,3 +480,19 @@ def test_committed_tile_table_dispatch(cuda, handle, monkeypatch):
         lib.emugemm_shutdown()
     assert launches == 2                   # B's split and the fused-A GEMM (the pre-split path launches 3)
     assert np.array_equal(C, ref)
+
+
+# --------------------------------------------------------------------------------------------- peak probe
+def test_peak_probe(cuda, handle):
+    """emugemm_peak_probe (the counterpart of bench/mfma_peak2.cpp): every instrument ran and its rate is
+    physically plausible for one B200: bf16 = fp16 on the tensor cores, tf32 at half their rate, FFMA near
+    148 SMs x 128 lanes x 2 FLOP x clock, the copy below the HBM3e nominal 8 TB/s."""
+    r = handle.peak_probe(3)
+    assert 800 < r["tc_bf16_tflops"] < 2400
+    assert 0.9 < r["tc_fp16_tflops"] / r["tc_bf16_tflops"] < 1.1
+    assert 0.35 < r["tc_tf32_tflops"] / r["tc_bf16_tflops"] < 0.65
+    assert 30 < r["ffma_tflops"] < 80
+    assert 5 < r["dfma_tflops"] < r["ffma_tflops"]
+    assert 2000 < r["copy_gbs"] < 8000
+    # the handle stays usable after the probe
+    assert handle.absmax(dev(cuda, np.ones(16, np.float32)), 16) == 1.0
