@@ -40,7 +40,7 @@ sys.path.insert(0, str(ROOT / "emugemm-cdna_b200"))
 SCHEMES = {"bf16x3": 3, "fp16x3": 4, "native": 1}
 
 # DRAM bytes per launch of the tensor-core kernel from one ncu capture (read + write), by (scheme, size).
-TRAFFIC = {("bf16x3", 8192): 2.366702e9 + 0.256244e9}
+TRAFFIC = {("bf16x3", 8192): 3.564580e9 + 0.261143e9, ("fp16x3", 8192): 2.951390e9 + 0.266271e9}
 
 
 def parse():
@@ -74,7 +74,8 @@ def peaks():
 
 def tc_kernel_name(M: int, N: int, K: int, scheme: str) -> str:
     """The tensor-core kernel the library picks for this shape: EMUGEMM_TC_KERNEL, else the tile table's code, else
-    the built-in rule (CTA pairs for bf16x3 with K > 1024); fp16x3 has no fused variants."""
+    the built-in rule (CTA pairs with K > 1024; for fp16x3 only when the 256 x 256 pair tiles fill the SM pairs);
+    fp16x3 has no fused variants."""
     import emugemm
 
     fp16 = scheme == "fp16x3"
@@ -82,7 +83,8 @@ def tc_kernel_name(M: int, N: int, K: int, scheme: str) -> str:
     code = {"single": 1, "pair": 2, "fused": 3, "fusea": 4}.get(env) or \
         emugemm.lib().emugemm_tune_lookup(M, N, K, 2 if fp16 else 1)
     if not code:
-        code = 2 if (not fp16 and K > 1024) else 1
+        pair_tiles = -(-M // 256) * -(-N // 256)
+        code = 2 if K > 1024 and (not fp16 or pair_tiles >= 148 // 2) else 1
     if fp16 and code >= 3:
         code = 2
     return {1: "k_tc_gemm", 2: "k_tc_gemm_pair", 3: "k_tc_fused",

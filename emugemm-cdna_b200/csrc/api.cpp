@@ -161,9 +161,9 @@ static long round_up(long x, long m) { return (x + m - 1) / m * m; }
 // Tensor-core kernel for a shape: 1 = single-CTA, 2 = CTA pair, 3 = CTA pair with the split fused in, 4 = CTA pair
 // with A split into TMEM in the kernel (3 and 4: bf16x3). The environment variable EMUGEMM_TC_KERNEL ("single",
 // "pair", "fused", "fusea") wins, then the tile table's code, then the built-in choice, fitted to the B200 tile
-// table (tiles_b200.csv): bf16x3 on CTA pairs when K > 1024 (pairs won at every K >= 4096 of the table, by up to
-// 17 % at small M, N; single-CTA tiles won at K = 1024, by up to 9 %), fp16x3 on single-CTA 128 x 128 tiles (all
-// 87 fp16 shapes of the table).
+// table (tiles_b200.csv): CTA pairs when K > 1024 (bf16x3: pairs won at every K >= 4096 of the table; at K = 1024
+// single-CTA or fused tiles won by up to 7 %), and for fp16x3 only when the 256 x 256 pair tiles at least fill
+// the SM pairs (with fewer tiles the 128 x 128 single-CTA tiles won, by up to 26 %).
 // EMUGEMM_LOG (set and not "0"): one stderr line per GEMM with the plan (scheme, chunks, predicted error, reason)
 // and one per tensor-core launch with the kernel chosen. The reference's observable decision record is plan.reason;
 // this makes it and the kernel choice visible without changing the API.
@@ -202,7 +202,10 @@ static int tc_kernel_choice(Handle* h, int M, int N, long K, bool fp16) {
     else if (v && std::strcmp(v, "fused") == 0) code = 3;
     else if (v && std::strcmp(v, "fusea") == 0) code = 4;
     if (!code) code = lookup_tile(M, N, K, fp16 ? 2 : 1).tc_variant;
-    if (!code) code = (!fp16 && K > 1024) ? 2 : 1;
+    if (!code) {
+        const long pair_tiles = ((M + 255) / 256) * (long)((N + 255) / 256);
+        code = (K > 1024 && (!fp16 || pair_tiles >= h->num_sms / 2)) ? 2 : 1;
+    }
     if (fp16 && code >= 3) code = 2;
     if (log_enabled()) {
         static const char* names[] = {"?", "single", "pair", "fused", "fusea"};

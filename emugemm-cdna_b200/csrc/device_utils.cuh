@@ -87,9 +87,12 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(addr), "r"(rank));
     return out;
 }
-// Arrive (release at cluster scope) on an mbarrier given by its shared::cluster address, possibly in a peer CTA.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+// Arrive on an mbarrier given by its shared::cluster address with the default semantics (release at CTA scope).
+// For a consumer that has finished its tcgen05.ld reads (tcgen05.wait::ld, then tcgen05.fence::before_thread_sync)
+// and only tells the MMA issuer that the TMEM buffer is free. A cluster-scope release
+// (mbarrier.arrive.release.cluster) stalled the arriving thread for about a thousand cycles.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 __device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
     asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
@@ -215,6 +218,17 @@ __device__ __forceinline__ void mma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(m));
+}
+// D(tmem) = A * B + D * 2^-11 on the pair (kind::f16 scale-input-d): the accumulator held so far is scaled by an exact
+// power of two before this product is added.
+__device__ __forceinline__ void mma_f16_ss_pair_scale11(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                        uint32_t idesc) {
+    uint32_t m = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.eq.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%4, %4, %4, %4, %4, %4, %4, %4}, p, 11;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(m));
 }
 // D(tmem) (+)= A(tmem) * B(smem desc) on the pair: A is read from TMEM (lane = row, each 32-bit column holding two
 // consecutive 16-bit K elements, the lower K in the low half), rows 0..127 from the leader's TMEM and 128..255 from

@@ -357,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(lead_te0 + (uint32_t)(b * sizeof(uint64_t)));
+                if (lane == 0) mbar_arrive_remote(lead_te0 + (uint32_t)(b * sizeof(uint64_t)));
             }
             if (!ok) break;
             const int m = mb2 * 2 * kBM + row_in_tile;

@@ -1,17 +1,25 @@
 // k_tc_gemm2.cu - the 3-product emulated-FP32 GEMM on CTA pairs (tcgen05 cta_group::2).
 //
-// Same product, slices, promotion and epilogue as k_tc_gemm.cu (see there), but two CTAs of a cluster share one
-// 256 x BN output tile: each CTA loads 128 rows of A and BN/2 rows of the transposed B into its own shared
-// memory, the pair's leader issues tcgen05.mma.cta_group::2 (M = 256), which reads the other halves from the
-// peer, and each CTA's TMEM receives the accumulator of its own 128 rows. Per SM this halves the B operand's
-// shared-memory and L2 traffic for the same tensor work.
+// Same slices as k_tc_gemm.cu (see there), but two CTAs of a cluster share one 256 x 256 output tile: each CTA
+// loads 128 rows of A and 128 rows of the transposed B into its own shared memory, the pair's leader issues
+// tcgen05.mma.cta_group::2 (M = 256, N = 256), which reads the other halves from the peer, and each CTA's TMEM
+// receives the accumulator of its own 128 rows. Per SM this halves the B operand's shared-memory and L2 traffic
+// for the same tensor work.
+//
+// Promotion: each accumulator holds one chunk of K and is added into FP32 registers with round-to-nearest.
+//   bf16x3: chunks of 128; per k16 step lo*hi, hi*lo, hi*hi into one accumulator (bit-identical to k_tc_gemm.cu).
+//   fp16x3: chunks of 64 (one stage); the stage's cross products lo*hi and hi*lo (lo carries a factor 2048)
+//   accumulate first, then the first hi*hi MMA scales the accumulator by 2^-11 on the way in (scale-input-d), then
+//   the remaining hi*hi follow. One accumulator of 256 columns per buffer, as for bf16x3.
 //
 // Cross-CTA signalling:
 //   both CTAs' TMA loads of a stage complete on the LEADER's full barrier (TMA .cta_group::2 form, each
 //   load writing only its own CTA), which the leader armed with the bytes of both halves;
 //   the leader's commits after a stage / a chunk arrive on the empty / tmem_full barriers of BOTH CTAs
 //   (tcgen05.commit to the CTA mask 0b11);
-//   every epilogue warp of both CTAs arrives on the leader's tmem_empty once it has drained a chunk.
+//   every epilogue warp of both CTAs arrives on the leader's tmem_empty once it has drained a chunk, with a
+//   CTA-scope arrive (its TMEM reads have completed; a cluster-scope release stalled each warp for ~1000 cycles
+//   per chunk, which at 64-K chunks made the epilogue the bottleneck).
 // Every wait is bounded; a CTA that gives up raises the abort flag of both CTAs, unwinds, and both meet at a
 // final cluster barrier before the pair's TMEM is freed.
 #include "device_utils.cuh"
@@ -35,18 +43,20 @@ constexpr int kBM = 128;             // rows per CTA (the pair covers 256)
 constexpr int kBK = 64;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kChunkKB = 128 / kBK;  // promotion every 128 values of K, as in k_tc_gemm.cu
 constexpr int kGroupM = 8;           // pair tiles: groups of 8 row blocks of 256
 
 template <bool FP16>
 struct Cfg2 {
-    static constexpr int BN = FP16 ? 128 : 256;      // pair tile width
+    static constexpr int BN = 256;                   // pair tile width
     static constexpr int BNH = BN / 2;               // rows of transposed B held by each CTA
     static constexpr int A_BYTES = kBM * kBK * 2;
     static constexpr int B_BYTES = BNH * kBK * 2;
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     static constexpr int STAGES = (196608 / STAGE_BYTES) < 6 ? (196608 / STAGE_BYTES) : 6;
-    static constexpr int ACC_COLS = FP16 ? 2 * BN : BN;
+    static constexpr int ACC_COLS = BN;
+    // k-blocks per accumulator: bf16x3 promotes every 128 values of K; fp16x3 every 64, one stage, because its
+    // hi*hi product is added after the stage's cross products have been scaled by 2^-11 in the accumulator
+    static constexpr int CHUNK_KB = FP16 ? 1 : 128 / kBK;
     static constexpr int HALF = BN / 2;              // columns per epilogue thread
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 512;
     static constexpr uint32_t IDESC = idesc_f16(2 * kBM, BN, !FP16);
@@ -89,6 +99,12 @@ __device__ __forceinline__ void drain_wait2(uint64_t* bar, uint32_t parity) {
     }
 }
 
+// x * 2^e, correctly rounded like ldexpf: a multiply by the exact power of two when 2^e is a normal float.
+__device__ __forceinline__ float scale_pow2(float x, int e) {
+    if (e >= -126 && e <= 127) return x * __int_as_float((e + 127) << 23);
+    return ldexpf(x, e);
+}
+
 // Raise the abort flag of both CTAs of the pair.
 __device__ __forceinline__ void abort_pair(Ctl2* ctl, uint32_t peer) {
     ctl->abort = 1;
@@ -113,7 +129,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool leader = rank == 0;
     const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
     const int num_tiles = p.num_m2 * p.num_n;
-    const int nchunks = (p.nk + kChunkKB - 1) / kChunkKB;
+    const int nchunks = (p.nk + C_::CHUNK_KB - 1) / C_::CHUNK_KB;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C_::STAGES; ++s) {
@@ -188,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             long it = 0, ch = 0;
             bool ok = true;
             for (int t = pair; t < num_tiles && ok; t += num_pairs) {
-                for (int kb0 = 0; kb0 < p.nk && ok; kb0 += kChunkKB, ++ch) {
+                for (int kb0 = 0; kb0 < p.nk && ok; kb0 += C_::CHUNK_KB, ++ch) {
                     const int b = (int)(ch & 1);
                     const uint32_t bph = (uint32_t)((ch >> 1) & 1);
                     if (!mbar_wait_cluster(&ctl->tmem_empty[b], bph ^ 1u, abort, p.err, kErrTimeoutMma)) {
@@ -196,9 +212,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t d_main = tmem_base + (uint32_t)(b * C_::ACC_COLS);
-                    const uint32_t d_cross = FP16 ? d_main + (uint32_t)C_::BN : d_main;
-                    const int kb1 = min(p.nk, kb0 + kChunkKB);
+                    const uint32_t d = tmem_base + (uint32_t)(b * C_::ACC_COLS);
+                    const int kb1 = min(p.nk, kb0 + C_::CHUNK_KB);
                     for (int kb = kb0; kb < kb1; ++kb, ++it) {
                         const int s = (int)(it % C_::STAGES);
                         const uint32_t ph = (uint32_t)((it / C_::STAGES) & 1);
@@ -212,13 +227,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint64_t a_lo = sdesc_kmajor(st + C_::A_BYTES, 128);
                         const uint64_t b_hi = sdesc_kmajor(st + 2 * C_::A_BYTES, 128);
                         const uint64_t b_lo = sdesc_kmajor(st + 2 * C_::A_BYTES + C_::B_BYTES, 128);
+                        if (FP16) {
+                            // D = sum(lo*hi + hi*lo) over the stage, then D = hi*hi + D * 2^-11 (the cross slices
+                            // carry the 2048 of lo), then the remaining hi*hi: one accumulator holds the 64-K chunk
 #pragma unroll
-                        for (int ks = 0; ks < kBK / 16; ++ks) {
-                            const uint64_t adv = (uint64_t)(ks * 32) >> 4;
-                            const uint32_t acc = (kb != kb0 || ks != 0) ? 1u : 0u;
-                            mma_f16_ss_pair(d_cross, a_lo + adv, b_hi + adv, C_::IDESC, acc);
-                            mma_f16_ss_pair(d_cross, a_hi + adv, b_lo + adv, C_::IDESC, 1u);
-                            mma_f16_ss_pair(d_main, a_hi + adv, b_hi + adv, C_::IDESC, FP16 ? acc : 1u);
+                            for (int ks = 0; ks < kBK / 16; ++ks) {
+                                const uint64_t adv = (uint64_t)(ks * 32) >> 4;
+                                mma_f16_ss_pair(d, a_lo + adv, b_hi + adv, C_::IDESC, ks != 0 ? 1u : 0u);
+                                mma_f16_ss_pair(d, a_hi + adv, b_lo + adv, C_::IDESC, 1u);
+                            }
+                            mma_f16_ss_pair_scale11(d, a_hi, b_hi, C_::IDESC);
+#pragma unroll
+                            for (int ks = 1; ks < kBK / 16; ++ks) {
+                                const uint64_t adv = (uint64_t)(ks * 32) >> 4;
+                                mma_f16_ss_pair(d, a_hi + adv, b_hi + adv, C_::IDESC, 1u);
+                            }
+                        } else {
+#pragma unroll
+                            for (int ks = 0; ks < kBK / 16; ++ks) {
+                                const uint64_t adv = (uint64_t)(ks * 32) >> 4;
+                                const uint32_t acc = (kb != kb0 || ks != 0) ? 1u : 0u;
+                                mma_f16_ss_pair(d, a_lo + adv, b_hi + adv, C_::IDESC, acc);
+                                mma_f16_ss_pair(d, a_hi + adv, b_lo + adv, C_::IDESC, 1u);
+                                mma_f16_ss_pair(d, a_hi + adv, b_hi + adv, C_::IDESC, 1u);
+                            }
                         }
                         mma_commit_pair_both(&ctl->empty[s], (uint16_t)0x3);
                     }
@@ -259,40 +291,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int q = 0; q < C_::HALF / 16; ++q) {
                     uint32_t r[16];
                     tmem_ld_32x32b_x16(tb + (uint32_t)(q * 16), r);
-                    if (FP16) {
-                        uint32_t x[16];
-                        tmem_ld_32x32b_x16(tb + (uint32_t)(C_::BN + q * 16), x);
-                        tmem_ld_wait();
+                    tmem_ld_wait();
 #pragma unroll
-                        for (int j = 0; j < 16; ++j)
-                            sum[q * 16 + j] += __uint_as_float(r[j]) + __uint_as_float(x[j]) * (1.0f / 2048.0f);
-                    } else {
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) sum[q * 16 + j] += __uint_as_float(r[j]);
-                    }
+                    for (int j = 0; j < 16; ++j) sum[q * 16 + j] += __uint_as_float(r[j]);
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(lead_te0 + (uint32_t)(b * sizeof(uint64_t)));
+                if (lane == 0) mbar_arrive_remote(lead_te0 + (uint32_t)(b * sizeof(uint64_t)));
             }
             if (!ok) break;
             const int m = mb2 * 2 * kBM + row_in_tile;
             if (m < p.M) {
                 const int n0 = nb * C_::BN + col0;
-                if (FP16) {
-                    const int e_row = p.row_exp[m];
-#pragma unroll
-                    for (int j = 0; j < C_::HALF; ++j) {
-                        const int n = n0 + j;
-                        if (n < p.N) sum[j] = ldexpf(sum[j], e_row + p.col_exp[n]);
-                    }
-                }
+                // fp16x3: undo the power-of-two row and column scaling of the split as each value is stored
+                const int e_row = FP16 ? p.row_exp[m] : 0;
+                const int* ce = p.col_exp + n0;
+                auto val = [&](int j) { return FP16 ? scale_pow2(sum[j], e_row + ce[j]) : sum[j]; };
                 if (p.C64) {
                     double* crow = p.C64 + (size_t)m * p.ldc64;
 #pragma unroll
                     for (int j = 0; j < C_::HALF; ++j)
-                        if (n0 + j < p.N) crow[n0 + j] = (double)sum[j];
+                        if (n0 + j < p.N) crow[n0 + j] = (double)val(j);
                 } else {
                     float* crow = p.C + (size_t)m * p.ldc;
                     const bool vec = (n0 + C_::HALF <= p.N) && ((p.ldc & 3) == 0) &&
@@ -301,11 +320,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         float4* c4 = reinterpret_cast<float4*>(crow + n0);
 #pragma unroll
                         for (int j = 0; j < C_::HALF / 4; ++j)
-                            c4[j] = make_float4(sum[4 * j], sum[4 * j + 1], sum[4 * j + 2], sum[4 * j + 3]);
+                            c4[j] = make_float4(val(4 * j), val(4 * j + 1), val(4 * j + 2), val(4 * j + 3));
                     } else {
 #pragma unroll
                         for (int j = 0; j < C_::HALF; ++j)
-                            if (n0 + j < p.N) crow[n0 + j] = sum[j];
+                            if (n0 + j < p.N) crow[n0 + j] = val(j);
                     }
                 }
             }

@@ -7,8 +7,10 @@ where `tile` is the winner (bf16/fp16: 1 = single-CTA, 2 = CTA pair, 3 = fused s
 fp32: SIMT tile edge 32, 64 or 128),
 `default_ms` the built-in choice's time and `gain` = default_ms / best_ms. Rows already present for a key are
 skipped, so an interrupted run resumes; --shard i/n takes every n-th shape starting at i (one process per GPU).
+--dtypes restricts the grid; --replace first drops the table's rows of those dtypes, so that they are measured
+again after a kernel change while the other rows stay.
 
-    python emugemm-cdna_b200/tune_tiles.py tiles_b200.csv [--shard 0/8] [--quick]
+    python emugemm-cdna_b200/tune_tiles.py tiles_b200.csv [--shard 0/8] [--quick] [--dtypes bf16,fp16 --replace]
 """
 from __future__ import annotations
 
@@ -38,6 +40,21 @@ def existing_keys(path: pathlib.Path) -> set:
                 if len(row) == 10 and row[0] != "arch":
                     keys.add((int(row[2]), int(row[3]), int(row[4]), row[5]))
     return keys
+
+
+def drop_rows(path: pathlib.Path, dtypes: set) -> None:
+    """Rewrite the table without its rows of the given dtypes (the header and other rows stay, in order)."""
+    if not path.exists():
+        return
+    with path.open("r+") as f:
+        fcntl.flock(f, fcntl.LOCK_EX)
+        keep = [ln for ln in f.read().splitlines(keepends=True)
+                if not (len(ln.split(",")) == 10 and ln.split(",")[5] in dtypes)]
+        f.seek(0)
+        f.truncate()
+        f.writelines(keep)
+        f.flush()
+        fcntl.flock(f, fcntl.LOCK_UN)
 
 
 def append_row(path: pathlib.Path, row: str) -> None:
@@ -104,7 +121,10 @@ def main():
     ap.add_argument("--shard", default="0/1")
     ap.add_argument("--quick", action="store_true")
     ap.add_argument("--reps", type=int, default=5)
+    ap.add_argument("--dtypes", default="bf16,fp16,fp32")
+    ap.add_argument("--replace", action="store_true")
     args = ap.parse_args()
+    dtypes = set(args.dtypes.split(","))
     i, n = (int(x) for x in args.shard.split("/"))
     torch.cuda.set_device(0)
     if args.quick:
@@ -113,7 +133,10 @@ def main():
         sizes = (1024, 2048, 4096, 8192, 16384)
         grid = list(itertools.product(sizes, sizes, (1024, 4096, 16384, 65536), ("bf16", "fp16", "fp32")))
         grid = [g for g in grid if g[0] * g[1] * g[2] <= 8192 ** 3 * 2]
+    grid = [g for g in grid if g[3] in dtypes]
     path = pathlib.Path(args.table)
+    if args.replace and i == 0:
+        drop_rows(path, dtypes)
     done = existing_keys(path)
     with emugemm.Handle() as h:
         for j, (M, N, K, dt) in enumerate(grid):

@@ -120,10 +120,10 @@ def test_committed_b200_tile_table():
     try:
         assert lib.emugemm_init_for_arch(table.encode(), b"sm_100a") == 0
         assert lib.emugemm_tune_rows() == 261
-        assert lib.emugemm_tune_lookup(2048, 1024, 16384, 1) == 4        # bf16x3: A split into TMEM
+        assert lib.emugemm_tune_lookup(1024, 1024, 1024, 1) == 4         # bf16x3: A split into TMEM
         assert lib.emugemm_tune_lookup(1024, 1024, 16384, 1) == 2        # bf16x3: CTA pairs
-        assert lib.emugemm_tune_lookup(16384, 16384, 1024, 1) == 1       # bf16x3, short K: single CTA
-        assert lib.emugemm_tune_lookup(8192, 8192, 4096, 2) == 1         # fp16x3: single CTA
+        assert lib.emugemm_tune_lookup(8192, 8192, 4096, 2) == 2         # fp16x3: CTA pairs (scaled accumulator)
+        assert lib.emugemm_tune_lookup(1024, 1024, 4096, 2) == 1         # fp16x3, 16 pair tiles: single CTA
         assert lib.emugemm_tune_lookup(1024, 2048, 4096, 0) == 128       # FP32 tile edge
         assert lib.emugemm_init_for_arch(table.encode(), b"sm_90a") == 0
         assert lib.emugemm_tune_rows() == 0
