@@ -296,6 +296,16 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
     return from_cuda(pair ? launch_tc_gemm_pair(t, h->stream) : launch_tc_gemm(t, h->stream));
 }
 
+// FP32 SIMT tile code for a shape: EMUGEMM_FP32_TILE (16, 32, 64 or 128) wins, then the tile table's code (looked up at
+// the chunk length), else 0 (the built-in choice of launch_fp32_gemm).
+static int fp32_tile_choice(int M, int N, long K, int chunks) {
+    if (const char* v = std::getenv("EMUGEMM_FP32_TILE")) {
+        const int t = std::atoi(v);
+        if (t == 16 || t == 32 || t == 64 || t == 128) return t;
+    }
+    return lookup_tile(M, N, K / (chunks < 1 ? 1 : chunks), 0).fp32_bm;
+}
+
 static emugemm_status_t run_fp32(Handle* h, int M, int N, long K, const float* A, long lda, const float* B, long ldb,
                                  float* C, long ldc, double* C64, long ldc64, int chunks) {
     Fp32GemmArgs f;
@@ -304,7 +314,7 @@ static emugemm_status_t run_fp32(Handle* h, int M, int N, long K, const float* A
     f.M = M; f.N = N; f.K = K;
     f.chunks = chunks < 1 ? 1 : chunks;
     f.num_sms = h->num_sms;
-    f.bm = lookup_tile(M, N, K / f.chunks, 0).fp32_bm;
+    f.bm = fp32_tile_choice(M, N, K, f.chunks);
     f.ws64 = nullptr;
     size_t wsb = fp32_gemm_ws_bytes(f);
     if (wsb) {
@@ -631,7 +641,9 @@ emugemm_status_t emugemm_reduce_f64(emugemm_handle_t handle, int M, int N, int G
 
 int emugemm_fp32_groups(int M, int N, long K, int chunks, int num_sms) {
     emu::Fp32GemmArgs f{};
-    f.M = M; f.N = N; f.K = K; f.chunks = chunks; f.num_sms = num_sms; f.bm = 0;
+    f.M = M; f.N = N; f.K = K; f.chunks = chunks < 1 ? 1 : chunks; f.num_sms = num_sms;
+    f.lda = K; f.ldb = N;   // contiguous operands, as the caller's own rows would be
+    f.bm = emu::fp32_tile_choice(M, N, K, f.chunks);
     return emu::fp32_gemm_groups(f);
 }
 

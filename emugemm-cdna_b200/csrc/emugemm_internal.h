@@ -50,7 +50,7 @@ struct TileChoice {
     int tc_variant;     // tensor-core kernel: 0 = built-in choice, 1 = single-CTA, 2 = CTA pair (cta_group::2),
                         // 3 = CTA pair with the split fused in, 4 = CTA pair with A split into TMEM in the
                         // kernel and B pre-split (3 and 4: bf16x3 only)
-    int fp32_bm;        // FP32 SIMT tile edge: 0 = auto, 32, 64 or 128
+    int fp32_bm;        // FP32 SIMT tile: 0 = auto, 32, 64 or 128 (square), 16 (16 x 32, k_fp32_narrow)
 };
 TileChoice lookup_tile(int M, int N, long K, int dtype /*0 fp32, 1 bf16, 2 fp16*/);
 
@@ -193,7 +193,7 @@ struct Fp32GemmArgs {
     int chunks;
     double* ws64;                // G x M x N FP64 partials when G > 1
     int num_sms;
-    int bm;                      // 0 = auto
+    int bm;                      // 0 = auto, else a tile code (16, 32, 64, 128)
 };
 int fp32_gemm_groups(const Fp32GemmArgs& a);   // G chosen for this shape
 size_t fp32_gemm_ws_bytes(const Fp32GemmArgs& a);

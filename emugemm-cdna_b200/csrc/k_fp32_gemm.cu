@@ -325,6 +325,114 @@ __global__ void __launch_bounds__(kThr) k_fp32_gemm_cp(Params p) {
     }
 }
 
+// 16 x 32 tiles for products whose output has too few elements to give every SM a 32 x 32 tile (C3: M = N = 256,
+// 65536 chains, c = 1). 128 threads, each running a 2 x 2 block of chains, so the CTA grid covers 128 SMs (the 32
+// tile: 64) with one warp per SM sub-partition.
+//
+// What bounds every FP32 SIMT tile here is shared-memory delivery, not the FMA pipe: an SM serves one 128-byte
+// wavefront per clock (one float per lane of a warp) while it can issue four FFMA warp-instructions, and a thread
+// with a TM x TN block of chains needs TM + TN floats per k for TM * TN FMAs. The FMA pipe can therefore be at most
+// TM * TN / (TM + TN) / 4 busy: 0.25 for 2 x 2, 0.5 for 4 x 4, 1 for 8 x 8 (ncu: the 1 x 4 form of this kernel
+// ran with the L1/shared pipe 97 % busy and the FMA pipe at 24 %). Few output elements force small blocks.
+//
+// Per four k a thread reads each of its two rows of A as one float4 along k (rows padded by 4 floats) and, per k,
+// its two columns of B as one float2: 16 wavefronts per 16 FMAs per warp. The stage is 64 deep. Same chains (k
+// ascending per element), same FP64 folds and the same VEC conditions as k_fp32_gemm_cp.
+template <int STAGES>
+__global__ void __launch_bounds__(128) k_fp32_narrow(Params p) {
+    constexpr int BK = 64, BKP = BK + 4, TR = 16, TC = 32;
+    constexpr int A_CH = TR * BK / 4, CH = A_CH + BK * TC / 4, CPT = CH / 128;
+    static_assert(CH % 128 == 0, "copies per thread");
+    extern __shared__ __align__(16) float narrow_smem[];
+    auto As = reinterpret_cast<float (*)[TR][BKP]>(narrow_smem);                       // [stage][m][k], rows padded
+    auto Bs = reinterpret_cast<float (*)[BK][TC]>(narrow_smem + STAGES * TR * BKP);    // [stage][k][n]
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;               // rows 2*ty, 2*ty+1; columns 2*tx, 2*tx+1
+    const int m0 = blockIdx.y * TR, n0 = blockIdx.x * TC;
+    const int g = blockIdx.z;
+    const int c_first = g * p.cpg;
+    const int c_last = min(p.ce, c_first + p.cpg);
+    double* Wg = p.W ? p.W + (size_t)g * p.M * p.N : nullptr;
+
+    for (int ci = c_first; ci < c_last; ++ci) {
+        const long kbeg = (long)ci * p.kc;
+        const long kend = min(p.K, kbeg + p.kc);
+        const long nkb = (kend - kbeg + BK - 1) / BK;
+        auto issue = [&](long kt) {
+            const int st = (int)(kt % STAGES);
+            const long k = kbeg + kt * BK;
+#pragma unroll
+            for (int c = 0; c < CPT; ++c) {
+                const int f = tid + c * 128;
+                if (f < A_CH) {
+                    const int r = f / (BK / 4), q = f % (BK / 4);
+                    const int m = m0 + r;
+                    const long kk = k + q * 4;
+                    const bool v = m < p.M && kk < kend;
+                    cp_async16(&As[st][r][q * 4], v ? (const void*)(p.A + (size_t)m * p.lda + kk) : (const void*)p.A,
+                               v);
+                } else {
+                    const int f2 = f - A_CH;
+                    const int kr = f2 / (TC / 4), q = f2 % (TC / 4);
+                    const long kk = k + kr;
+                    const int n = n0 + q * 4;
+                    const bool v = kk < kend && n < p.N;
+                    cp_async16(&Bs[st][kr][q * 4], v ? (const void*)(p.B + (size_t)kk * p.ldb + n) : (const void*)p.B,
+                               v);
+                }
+            }
+        };
+        float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+        for (int kt = 0; kt < STAGES - 1; ++kt) {
+            if (kt < nkb) issue(kt);
+            cp_async_commit();
+        }
+        for (long kt = 0; kt < nkb; ++kt) {
+            if (kt + STAGES - 1 < nkb) issue(kt + STAGES - 1);
+            cp_async_commit();
+            cp_async_wait<STAGES - 1>();
+            __syncthreads();
+            const int st = (int)(kt % STAGES);
+#pragma unroll
+            for (int k4 = 0; k4 < BK / 4; ++k4) {
+                const float4 a0 = *reinterpret_cast<const float4*>(&As[st][2 * ty][k4 * 4]);
+                const float4 a1 = *reinterpret_cast<const float4*>(&As[st][2 * ty + 1][k4 * 4]);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const float2 b = *reinterpret_cast<const float2*>(&Bs[st][k4 * 4 + kk][tx * 2]);
+                    const float x0 = kk == 0 ? a0.x : kk == 1 ? a0.y : kk == 2 ? a0.z : a0.w;
+                    const float x1 = kk == 0 ? a1.x : kk == 1 ? a1.y : kk == 2 ? a1.z : a1.w;
+                    acc[0][0] = __fmaf_rn(x0, b.x, acc[0][0]);
+                    acc[0][1] = __fmaf_rn(x0, b.y, acc[0][1]);
+                    acc[1][0] = __fmaf_rn(x1, b.x, acc[1][0]);
+                    acc[1][1] = __fmaf_rn(x1, b.y, acc[1][1]);
+                }
+            }
+            __syncthreads();
+        }
+        cp_async_wait<0>();
+        const bool first = (ci == c_first), last = (ci == c_last - 1);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int m = m0 + 2 * ty + i;
+            if (m >= p.M) continue;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int n = n0 + tx * 2 + j;
+                if (n >= p.N) continue;
+                const size_t wi = (size_t)m * p.N + n;
+                const double s = first ? (double)acc[i][j] : Wg[wi] + (double)acc[i][j];
+                if (last && p.G == 1) {
+                    if (p.C64) p.C64[(size_t)m * p.ldc64 + n] = s;
+                    else p.C[(size_t)m * p.ldc + n] = (float)s;
+                } else {
+                    Wg[wi] = s;
+                }
+            }
+        }
+    }
+}
+
 __global__ void k_reduce_f64(const double* __restrict__ P, int G, int M, int N, long ldp_plane, float* C,
                              long ldc, double* C64, long ldc64) {
     const size_t total = (size_t)M * N;
@@ -344,18 +452,32 @@ struct Shape {
     int tiles;
 };
 
-// Chunk groups for `tiles` output tiles: enough CTAs for two per SM, at most one group per chunk.
-static int groups_for(int ce, long tiles, int sms) {
+// Chunk groups for `tiles` output tiles: enough CTAs for `per_sm` per SM (two 8-warp CTAs, or four 4-warp CTAs of
+// the narrow kernel), at most one group per chunk.
+static int groups_for(int ce, long tiles, int sms, int per_sm = 2) {
     if (ce <= 1) return 1;
-    long want = (2L * sms + tiles - 1) / tiles;
+    long want = ((long)per_sm * sms + tiles - 1) / tiles;
     if (want < 1) want = 1;
     return (int)(want < ce ? want : ce);
 }
 
 // Tile edge: 128 when its tiles fill at least half the SMs (in the B200 tile table 128 won 83 of 87 FP32 shapes,
 // by 30-50 % at 1024 x 2048 where its 128 tiles cover 86 % of the SMs); else 64 when its tiles x chunk groups fill
-// the SMs; else 32 (2 x 2 chains per thread), so that a product with few output tiles and few chunks
-// (M = N = 256, c = 1) spreads its FMA chains over more SMs. No chain changes with the tile edge.
+// the SMs; else 32 (2 x 2 chains per thread) when those fill the SMs; else the 16 x 32 tiles of k_fp32_narrow, so
+// that a product with few output tiles and few chunks (M = N = 256, c = 1) spreads its FMA chains over more SMs.
+// No chain changes with the tile.
+// The 16-byte copies of the cp.async kernels need 16-byte aligned rows and K, N and the chunk length multiples of 4.
+static bool vec_ok(const Fp32GemmArgs& a, long kc) {
+    return (a.lda % 4 == 0) && (a.ldb % 4 == 0) && (a.N % 4 == 0) && (a.K % 4 == 0) && (kc % 4 == 0) &&
+           ((reinterpret_cast<uintptr_t>(a.A) & 15) == 0) && ((reinterpret_cast<uintptr_t>(a.B) & 15) == 0);
+}
+
+// Tile codes: 128, 64, 32 (square tiles) and 16 (16 x 32 tiles of k_fp32_narrow).
+static long tiles_of(const Fp32GemmArgs& a, int bm) {
+    const int bn = bm == 16 ? 32 : bm;
+    return (long)((a.M + bm - 1) / bm) * ((a.N + bn - 1) / bn);
+}
+
 Shape shape_of(const Fp32GemmArgs& a) {
     Shape s;
     const int sms = a.num_sms > 0 ? a.num_sms : 148;
@@ -364,13 +486,14 @@ Shape shape_of(const Fp32GemmArgs& a) {
     if (s.kc < 1) s.kc = 1;
     s.ce = (int)((a.K + s.kc - 1) / s.kc);
     if (s.ce < 1) s.ce = 1;
-    auto tiles_of = [&](int bm) { return (long)((a.M + bm - 1) / bm) * ((a.N + bm - 1) / bm); };
     if (a.bm) s.bm = a.bm;
-    else if (2 * tiles_of(128) >= sms) s.bm = 128;
-    else if (tiles_of(64) * groups_for(s.ce, tiles_of(64), sms) >= sms) s.bm = 64;
-    else s.bm = 32;
-    s.tiles = (int)tiles_of(s.bm);
-    const int G = groups_for(s.ce, s.tiles, sms);
+    else if (2 * tiles_of(a, 128) >= sms) s.bm = 128;
+    else if (tiles_of(a, 64) * groups_for(s.ce, tiles_of(a, 64), sms) >= sms) s.bm = 64;
+    else if (tiles_of(a, 32) * groups_for(s.ce, tiles_of(a, 32), sms) >= sms) s.bm = 32;
+    else s.bm = 16;
+    if (s.bm == 16 && !vec_ok(a, s.kc)) s.bm = 32;   // the narrow kernel exists only in the cp.async form
+    s.tiles = (int)tiles_of(a, s.bm);
+    const int G = groups_for(s.ce, s.tiles, sms, s.bm == 16 ? 4 : 2);
     s.cpg = (s.ce + G - 1) / G;
     s.G = (s.ce + s.cpg - 1) / s.cpg;
     return s;
@@ -406,11 +529,10 @@ int launch_fp32_gemm(const Fp32GemmArgs& a, void* stream) {
     p.M = a.M; p.N = a.N; p.K = a.K;
     p.kc = s.kc; p.ce = s.ce; p.cpg = s.cpg; p.G = s.G;
     if ((s.G > 1 || s.ce > 1) && !a.ws64) return (int)cudaErrorInvalidValue;
-    const bool vec = (a.lda % 4 == 0) && (a.ldb % 4 == 0) && (a.N % 4 == 0) && (a.K % 4 == 0) &&
-                     (s.kc % 4 == 0) && ((reinterpret_cast<uintptr_t>(a.A) & 15) == 0) &&
-                     ((reinterpret_cast<uintptr_t>(a.B) & 15) == 0);
+    const bool vec = vec_ok(a, s.kc);
     cudaStream_t st = (cudaStream_t)stream;
-    dim3 grid((unsigned)((a.N + s.bm - 1) / s.bm), (unsigned)((a.M + s.bm - 1) / s.bm), (unsigned)s.G);
+    const int bn = s.bm == 16 ? 32 : s.bm;
+    dim3 grid((unsigned)((a.N + bn - 1) / bn), (unsigned)((a.M + s.bm - 1) / s.bm), (unsigned)s.G);
     if (s.bm == 128) {
         if (vec) launch_cfg<128, 8, true>(p, grid, st);
         else launch_cfg<128, 8, false>(p, grid, st);
@@ -420,6 +542,13 @@ int launch_fp32_gemm(const Fp32GemmArgs& a, void* stream) {
     } else if (s.bm == 32) {
         if (vec) k_fp32_gemm_cp<32, 8><<<grid, kThr, 0, st>>>(p);
         else launch_cfg<32, 2, false>(p, grid, st);
+    } else if (s.bm == 16) {
+        constexpr int kNarrowStages = 4;   // 50 KB: four CTAs per SM
+        const int smem = kNarrowStages * (16 * 68 + 64 * 32) * (int)sizeof(float);
+        cudaError_t e = cudaFuncSetAttribute(k_fp32_narrow<kNarrowStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             smem);
+        if (e != cudaSuccess) return (int)e;
+        k_fp32_narrow<kNarrowStages><<<grid, 128, smem, st>>>(p);
     } else {
         return (int)cudaErrorInvalidValue;
     }

@@ -111,6 +111,31 @@ def test_chunked_fp32_bitexact(cuda, handle, shape, chunks):
     assert np.array_equal(C.cpu().numpy(), want.astype(np.float32))
 
 
+@pytest.mark.parametrize("tile", [16, 32, 64, 128])
+@pytest.mark.parametrize("shape,chunks", [((256, 256, 8192), 1), ((256, 256, 8192), 4), ((100, 36, 1000), 3),
+                                          ((33, 20, 260), 1), ((64, 130, 500), 2)])
+def test_fp32_tiles_bitexact(cuda, handle, monkeypatch, tile, shape, chunks):
+    """Every FP32 SIMT tile (EMUGEMM_FP32_TILE: 16 = the 16 x 32 narrow kernel, 32 / 64 / 128 square) runs the same
+    chains and FP64 folds: bit-exact against the oracle with the group split the library reports. Ragged M, N not
+    a multiple of 32, chunk lengths not a multiple of 64; N = 130 is not a multiple of 4, so the narrow kernel falls
+    back to the 32 tile there."""
+    torch = cuda
+    monkeypatch.setenv("EMUGEMM_FP32_TILE", str(tile))
+    M, N, K = shape
+    A = datagen.uniform((M, K), 5 + K + tile)
+    B = datagen.uniform((K, N), 6 + K + tile)
+    dA, dB = dev(torch, A), dev(torch, B)
+    P64 = torch.empty((M, N), dtype=torch.float64, device="cuda")
+    handle.partial_f64(M, N, K, dA, K, dB, N, P64, emugemm.FP32_CHUNKED, chunks)
+    handle.sync()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    G = emugemm.fp32_groups(M, N, K, chunks, sms)
+    want = oracle.fp32_chunked(A, B, chunks, cpg=oracle.group_size(K, chunks, G), f64=True)
+    assert np.array_equal(P64.cpu().numpy(), want)
+    C, p, _ = run_sgemm(torch, handle, A, B, force=emugemm.NATIVE_FP32)
+    assert np.array_equal(C, oracle.fp32_chunked(A, B, 1))
+
+
 def test_auto_chunked_plan_runs_chunked(cuda, handle):
     """A target below what bf16x3 and fp16x3 can reach (2e-7 at K = 65536) routes to FP32_CHUNKED with c > 1;
     the result is the bit-exact chain."""
