@@ -54,10 +54,11 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
-    ap.add_argument("--workload", default="square", choices=["square", "rows", "ksplit", "chunked", "rho"],
+    ap.add_argument("--workload", default="square", choices=["square", "rows", "ksplit", "chunked", "longk", "rho"],
                     help="square: S^3 per GPU (weak); rows: one S^3 product, rows over GPUs; "
-                         "ksplit: S x S x --k, K over GPUs; chunked: FP32_CHUNKED S x S x --k; rho: rho probe S^3")
-    ap.add_argument("--k", type=int, default=1048576, help="K of the ksplit and chunked workloads")
+                         "ksplit: S x S x --k, K over GPUs; chunked: FP32_CHUNKED S x S x --k; "
+                         "longk: --scheme at S x S x --k; rho: rho probe S^3")
+    ap.add_argument("--k", type=int, default=1048576, help="K of the ksplit, chunked and longk workloads")
     ap.add_argument("--chunks", type=int, default=4, help="K-chunks of the chunked workload")
     ap.add_argument("--probes", type=int, default=64, help="probe vectors of the rho workload")
     return ap.parse_args()
@@ -74,7 +75,7 @@ def peaks():
 
 def tc_kernel_name(M: int, N: int, K: int, scheme: str) -> str:
     """The tensor-core kernel the library picks for this shape: EMUGEMM_TC_KERNEL, else the tile table's code, else
-    the built-in rule (CTA pairs with K > 1024; for fp16x3 only when the 256 x 256 pair tiles fill the SM pairs);
+    the built-in rule of the library (a copy of it);
     fp16x3 has no fused variants."""
     import emugemm
 
@@ -83,8 +84,11 @@ def tc_kernel_name(M: int, N: int, K: int, scheme: str) -> str:
     code = {"single": 1, "pair": 2, "fused": 3, "fusea": 4}.get(env) or \
         emugemm.lib().emugemm_tune_lookup(M, N, K, 2 if fp16 else 1)
     if not code:
-        pair_tiles = -(-M // 256) * -(-N // 256)
-        code = 2 if K > 1024 and (not fp16 or pair_tiles >= 148 // 2) else 1
+        pair_tiles, pairs = -(-M // 256) * -(-N // 256), 148 // 2
+        if not fp16:
+            code = 2 if (K > 1024 or pair_tiles >= pairs) else 1
+        else:
+            code = 2 if ((K > 1024 or pair_tiles >= 512) if pair_tiles >= pairs else K >= 16384) else 1
     if fp16 and code >= 3:
         code = 2
     return {1: "k_tc_gemm", 2: "k_tc_gemm_pair", 3: "k_tc_fused",
@@ -358,6 +362,20 @@ def ours(args) -> None:
         def step():
             h.partial_f64(M, N, K, A, K, B, N, P, 2, args.chunks)
             h.reduce_f64(M, N, 1, P, C)
+    elif wl == "longk":
+        # the long-K comparison (M = N = S, K = args.k, U[-1,1]): the --scheme product forced, one emugemm_sgemm per
+        # step; few output tiles, so the tensor-core kernel splits K over the SM pairs
+        M, N, K = S, S, args.k
+        m_loc, k_loc = M, K
+        A = torch.rand((M, K), device="cuda", generator=gen) * 2 - 1
+        B = torch.rand((K, N), device="cuda", generator=gen) * 2 - 1
+        C = torch.empty((M, N), device="cuda")
+        total_flop = 2.0 * M * N * K * world
+        scaling = "weak"
+        desc = f"{args.scheme} emulated SGEMM {M}x{N}x{K}" + (f", {world} independent replicas" if world > 1 else "")
+
+        def step():
+            h.sgemm(M, N, K, A, B, C, force=scheme, hints=hints())
     elif wl == "rho":
         # rho = ||(|A||B|)||_F / ||AB||_F estimated with args.probes Rademacher vectors (signed and |.| products)
         M, N, K = S, S, S
@@ -430,8 +448,8 @@ def ours(args) -> None:
 
     # dominant kernel: the tensor-core 3-product GEMM (3 * 2 * m * n * k tensor FLOPs per rank and step), the FP32
     # SIMT GEMM (2 * m * n * k) for the chunked workload, the skinny probe products (4 * P * K * (M + N)) for rho
-    if wl == "chunked":
-        kern_key, kern_name, bound = "fp32_gemm", "k_fp32_gemm / k_fp32_gemm_cp (+ k_reduce_f64)", "fp32"
+    if wl == "chunked" or (wl == "longk" and args.scheme == "native"):
+        kern_key, kern_name, bound = "fp32_gemm", "k_fp32_gemm / k_fp32_gemm_cp / k_fp32_narrow (+ k_reduce_f64)", "fp32"
         rank_tensor_flop = 2.0 * m_loc * N * k_loc
     elif wl == "rho":
         kern_key, kern_name, bound = "rho", "rho probe (k_omega, k_skinny_cp x2, k_combine[_sq], k_final)", "fp32"
@@ -539,7 +557,7 @@ def ours(args) -> None:
             "unit": "TFLOPS", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": scaling, "vs_baseline": None, "dtype": "f32",
-            "data": ("synthetic U[-1,1] (torch generator)" if wl == "chunked"
+            "data": ("synthetic U[-1,1] (torch generator)" if wl in ("chunked", "longk")
                      else "synthetic N(0,1)*2^e, e~U{-20..20} (torch generator)"),
             "config": {"workload": desc, "M": M * (world if wl == "square" else 1), "N": N, "K": K,
                        "scheme": ("fp32_chunked" if wl == "chunked" else "rho_probe" if wl == "rho" else args.scheme),

@@ -7,6 +7,7 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdio>
@@ -161,9 +162,11 @@ static long round_up(long x, long m) { return (x + m - 1) / m * m; }
 // Tensor-core kernel for a shape: 1 = single-CTA, 2 = CTA pair, 3 = CTA pair with the split fused in, 4 = CTA pair
 // with A split into TMEM in the kernel (3 and 4: bf16x3). The environment variable EMUGEMM_TC_KERNEL ("single",
 // "pair", "fused", "fusea") wins, then the tile table's code, then the built-in choice, fitted to the B200 tile
-// table (tiles_b200.csv): CTA pairs when K > 1024 (bf16x3: pairs won at every K >= 4096 of the table; at K = 1024
-// single-CTA or fused tiles won by up to 7 %), and for fp16x3 only when the 256 x 256 pair tiles at least fill
-// the SM pairs (with fewer tiles the 128 x 128 single-CTA tiles won, by up to 26 %).
+// table (tiles_b200.csv):
+//   bf16x3: CTA pairs when K > 1024 or their 256 x 256 tiles fill the SM pairs (pairs won every shape with K >= 4096
+//   and the K = 1024 shapes with at least 128 tiles; with fewer, single-CTA or fused tiles won by up to 8 %);
+//   fp16x3: with tiles that fill the SM pairs, pairs when K > 1024 or at least 512 tiles (else the 128 x 128
+//   single-CTA tiles won, by up to 26 %); with fewer tiles, pairs when K >= 16384, long enough for the K splits.
 // EMUGEMM_LOG (set and not "0"): one stderr line per GEMM with the plan (scheme, chunks, predicted error, reason)
 // and one per tensor-core launch with the kernel chosen. The reference's observable decision record is plan.reason;
 // this makes it and the kernel choice visible without changing the API.
@@ -194,6 +197,22 @@ static void log_plan(const char* entry, int M, int N, long K, const emu_plan_t& 
                  p.reason ? p.reason : "");
 }
 
+// K splits of the CTA-pair kernel. When its 256 x 256 tiles cannot occupy the SM pairs (a few output tiles and a long
+// K: M = N = 256, K = 262144 is one tile for 74 pairs), each tile's K range is split into whole ranges of k-blocks
+// of at least 1024 values of K, for at most one unit per SM pair; every split writes an FP64 partial and the
+// partials are summed in order (deterministic). Within a split the promotion and accumulation order is unchanged.
+// EMUGEMM_TC_SPLITK (a count >= 1) overrides the choice.
+static int tc_split_count(long Mp, long Np, long Kp, int num_sms) {
+    const long nk = Kp / 64, tiles = (Mp / 256) * (Np / 256), pairs = num_sms / 2;
+    long want = 1;
+    if (const char* v = std::getenv("EMUGEMM_TC_SPLITK")) want = std::atol(v);
+    else if (tiles > 0 && tiles < pairs) want = std::min(pairs / tiles, nk / 16);
+    if (want < 1) want = 1;
+    if (want > nk) want = nk;
+    const long kps = (nk + want - 1) / want;
+    return (int)((nk + kps - 1) / kps);   // every split non-empty
+}
+
 static int tc_kernel_choice(Handle* h, int M, int N, long K, bool fp16) {
     const char* v = std::getenv("EMUGEMM_TC_KERNEL");
     int code = 0;
@@ -203,8 +222,9 @@ static int tc_kernel_choice(Handle* h, int M, int N, long K, bool fp16) {
     else if (v && std::strcmp(v, "fusea") == 0) code = 4;
     if (!code) code = lookup_tile(M, N, K, fp16 ? 2 : 1).tc_variant;
     if (!code) {
-        const long pair_tiles = ((M + 255) / 256) * (long)((N + 255) / 256);
-        code = (K > 1024 && (!fp16 || pair_tiles >= h->num_sms / 2)) ? 2 : 1;
+        const long pair_tiles = (round_up(M, 256) / 256) * (round_up(N, 256) / 256), pairs = h->num_sms / 2;
+        if (!fp16) code = (K > 1024 || pair_tiles >= pairs) ? 2 : 1;
+        else code = (pair_tiles >= pairs ? (K > 1024 || pair_tiles >= 512) : K >= 16384) ? 2 : 1;
     }
     if (fp16 && code >= 3) code = 2;
     if (log_enabled()) {
@@ -292,8 +312,17 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
     t.row_exp = rexp; t.col_exp = cexp;
     t.err = h->err_dev;
     t.num_sms = h->num_sms;
+    if (pair) {
+        t.splits = tc_split_count(Mp, Np, Kp, h->num_sms);
+        if (t.splits > 1) {
+            t.part64 = (double*)ws_get(h, kWsSplitK, (size_t)t.splits * M * N * sizeof(double));
+            if (!t.part64) return EMUGEMM_STATUS_MEMORY_ERROR;
+        }
+    }
     ProfScope ps(h, kProfTcGemm);
-    return from_cuda(pair ? launch_tc_gemm_pair(t, h->stream) : launch_tc_gemm(t, h->stream));
+    e = pair ? launch_tc_gemm_pair(t, h->stream) : launch_tc_gemm(t, h->stream);
+    if (e || t.splits <= 1) return from_cuda(e);
+    return from_cuda(launch_reduce_f64(t.part64, t.splits, M, N, (long)M * N, C, ldc, C64, ldc64, h->stream));
 }
 
 // FP32 SIMT tile code for a shape: EMUGEMM_FP32_TILE (16, 32, 64 or 128) wins, then the tile table's code (looked up at

@@ -73,6 +73,7 @@ enum WsSlot {
     kWsRhoT1, kWsRhoT2, kWsRhoPart,
     kWsScalar,
     kWsHostA, kWsHostB, kWsHostC,   // device copies of the operands of emugemm_sgemm_host
+    kWsSplitK,                      // FP64 partial planes of the split-K tensor-core GEMM
     kWsCount
 };
 
@@ -165,6 +166,10 @@ struct TcGemmArgs {
     const int* row_exp; const int* col_exp;        // fp16x3 only
     unsigned* err;
     int num_sms;
+    // CTA-pair kernel only: K split into `splits` ranges of whole k-blocks (every range non-empty); each writes an
+    // FP64 partial plane part64[s] (M x N, ld N) instead of C, and the caller sums the planes in order.
+    int splits = 1;
+    double* part64 = nullptr;
 };
 int launch_tc_gemm(const TcGemmArgs& a, void* stream);
 int tc_gemm_bn(int fp16);   // output tile width of the bf16x3 (0) / fp16x3 (1) kernel

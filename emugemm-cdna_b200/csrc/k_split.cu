@@ -91,17 +91,38 @@ __device__ __forceinline__ int exponent_for_max(float mx) {
     return q - 15;
 }
 
-// One warp per row of A.
-__global__ void k_row_exponents(const float* __restrict__ A, int M, long K, long lda, int* __restrict__ e_out) {
+// Row maxima of A over a segment of K per blockIdx.y: one warp per (row, segment), 16-byte loads when the row and
+// the segment start are aligned, combined across segments with integer atomicMax on the (non-negative) float bits.
+// Segments keep the whole GPU busy when A has few rows and long ones (M = 256, K = 262144).
+__global__ void k_row_max(const float* __restrict__ A, int M, long K, long lda, long k_per_seg,
+                          unsigned* __restrict__ rowmax_bits) {
     const int warps = blockDim.x >> 5;
     const int row = blockIdx.x * warps + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= M) return;
+    const long k0 = (long)blockIdx.y * k_per_seg;
+    const long k1 = min(K, k0 + k_per_seg);
     const float* a = A + (size_t)row * lda;
     float m = 0.f;
-    for (long k = lane; k < K; k += 32) m = fmaxf(m, fabsf(a[k]));
+    long k = k0;
+    if ((((uintptr_t)(a + k0)) & 15) == 0) {
+        const float4* a4 = reinterpret_cast<const float4*>(a + k0);
+        const long n4 = (k1 - k0) >> 2;
+        for (long i = lane; i < n4; i += 32) {
+            const float4 v = __ldg(a4 + i);
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+        k = k0 + 4 * n4;
+    }
+    for (long kk = k + lane; kk < k1; kk += 32) m = fmaxf(m, fabsf(a[kk]));
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) e_out[row] = exponent_for_max(m);
+    if (lane == 0) atomicMax(rowmax_bits + row, __float_as_uint(m));
+}
+
+// In place: the max bits of each row become the row's exponent.
+__global__ void k_row_exponents(int* __restrict__ e, int M) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r < M) e[r] = exponent_for_max(__uint_as_float((unsigned)e[r]));
 }
 
 // Column maxima of B (K x N) over a slice of K per blockIdx.y, combined with integer atomicMax.
@@ -263,9 +284,24 @@ int launch_absmax(const float* X, long rows, long cols, long ld, float* out, voi
 
 int launch_row_exponents(const float* A, int M, long K, long lda, int* e_out, void* stream) {
     if (M == 0) return 0;
+    cudaStream_t s = (cudaStream_t)stream;
+    cudaError_t e = cudaMemsetAsync(e_out, 0, sizeof(int) * (size_t)M, s);
+    if (e != cudaSuccess) return (int)e;
     const int warps = 8;
-    k_row_exponents<<<(M + warps - 1) / warps, warps * 32, 0, (cudaStream_t)stream>>>(A, M, K, lda, e_out);
-    count_launch();
+    const long bx = (M + warps - 1) / warps;
+    // about 8 blocks per SM, segments of at least 4096 values of K, starting on multiples of 4
+    long segs = (148 * 8 + bx - 1) / bx;
+    const long max_segs = (K + 4095) / 4096;
+    if (segs > max_segs) segs = max_segs;
+    if (segs < 1) segs = 1;
+    long kps = (K + segs - 1) / segs;
+    kps = (kps + 3) / 4 * 4;
+    segs = (K + kps - 1) / kps;
+    if (segs < 1) segs = 1;
+    k_row_max<<<dim3((unsigned)bx, (unsigned)segs), warps * 32, 0, s>>>(A, M, K, lda, kps,
+                                                                         reinterpret_cast<unsigned*>(e_out));
+    k_row_exponents<<<(M + 255) / 256, 256, 0, s>>>(e_out, M);
+    count_launch(2);
     return (int)cudaGetLastError();
 }
 

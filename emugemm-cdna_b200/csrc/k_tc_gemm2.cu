@@ -75,11 +75,22 @@ struct Ctl2 {
 struct KParams2 {
     int M, N, num_m2, num_n, nk;   // num_m2: row blocks of 256
     int kpb;                       // k-blocks per K panel of the slices
+    int splits, kps;               // K splits and k-blocks per split (splits = 1: whole K per tile)
     float* C; long ldc;
     double* C64; long ldc64;
+    double* part;                  // splits > 1: FP64 partial planes [splits][M][N]
     const int* row_exp; const int* col_exp;
     unsigned* err;
 };
+
+// Work unit u (tile x K split): the tile, the split and its k-block range [kb0, kb1).
+__device__ __forceinline__ void unit_of(const KParams2& p, int num_tiles, int u, int& tile, int& sp, int& kb0,
+                                        int& kb1) {
+    tile = u % num_tiles;
+    sp = u / num_tiles;
+    kb0 = sp * p.kps;
+    kb1 = min(p.nk, kb0 + p.kps);
+}
 
 __device__ __forceinline__ void tile_coords2(int t, int num_m2, int num_n, int& mb2, int& nb) {
     const int per_group = kGroupM * num_n;
@@ -129,7 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool leader = rank == 0;
     const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
     const int num_tiles = p.num_m2 * p.num_n;
-    const int nchunks = (p.nk + C_::CHUNK_KB - 1) / C_::CHUNK_KB;
+    const int num_units = num_tiles * p.splits;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C_::STAGES; ++s) {
@@ -165,12 +176,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             long it = 0;
             bool ok = true;
             const uint32_t lead_full0 = mapa_shared(smem_u32(&ctl->full[0]), 0);
-            for (int t = pair; t < num_tiles && ok; t += num_pairs) {
-                int mb2, nb;
+            for (int u = pair; u < num_units && ok; u += num_pairs) {
+                int t, sp, kbb, kbe, mb2, nb;
+                unit_of(p, num_tiles, u, t, sp, kbb, kbe);
                 tile_coords2(t, p.num_m2, p.num_n, mb2, nb);
                 const int a_row = mb2 * 2 * kBM + (int)rank * kBM;
                 const int b_row = nb * C_::BN + (int)rank * C_::BNH;
-                for (int kb = 0; kb < p.nk; ++kb, ++it) {
+                for (int kb = kbb; kb < kbe; ++kb, ++it) {
                     const int s = (int)(it % C_::STAGES);
                     const uint32_t ph = (uint32_t)((it / C_::STAGES) & 1);
                     // empty[s] of both CTAs is signalled by the leader's commit once the pair MMA read stage s
@@ -203,8 +215,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             // ---------------- leader: pair MMA issuer ----------------
             long it = 0, ch = 0;
             bool ok = true;
-            for (int t = pair; t < num_tiles && ok; t += num_pairs) {
-                for (int kb0 = 0; kb0 < p.nk && ok; kb0 += C_::CHUNK_KB, ++ch) {
+            for (int u = pair; u < num_units && ok; u += num_pairs) {
+                int t, sp, kbb, kbe;
+                unit_of(p, num_tiles, u, t, sp, kbb, kbe);
+                for (int kb0 = kbb; kb0 < kbe && ok; kb0 += C_::CHUNK_KB, ++ch) {
                     const int b = (int)(ch & 1);
                     const uint32_t bph = (uint32_t)((ch >> 1) & 1);
                     if (!mbar_wait_cluster(&ctl->tmem_empty[b], bph ^ 1u, abort, p.err, kErrTimeoutMma)) {
@@ -213,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     tc_fence_after();
                     const uint32_t d = tmem_base + (uint32_t)(b * C_::ACC_COLS);
-                    const int kb1 = min(p.nk, kb0 + C_::CHUNK_KB);
+                    const int kb1 = min(kbe, kb0 + C_::CHUNK_KB);
                     for (int kb = kb0; kb < kb1; ++kb, ++it) {
                         const int s = (int)(it % C_::STAGES);
                         const uint32_t ph = (uint32_t)((it / C_::STAGES) & 1);
@@ -274,9 +288,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lead_te0 = mapa_shared(smem_u32(&ctl->tmem_empty[0]), 0);
         long ch = 0;
         bool ok = true;
-        for (int t = pair; t < num_tiles && ok; t += num_pairs) {
-            int mb2, nb;
+        for (int u = pair; u < num_units && ok; u += num_pairs) {
+            int t, sp, kbb, kbe, mb2, nb;
+            unit_of(p, num_tiles, u, t, sp, kbb, kbe);
             tile_coords2(t, p.num_m2, p.num_n, mb2, nb);
+            const int nchunks = (kbe - kbb + C_::CHUNK_KB - 1) / C_::CHUNK_KB;
             float sum[C_::HALF];
 #pragma unroll
             for (int j = 0; j < C_::HALF; ++j) sum[j] = 0.f;
@@ -307,7 +323,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int e_row = FP16 ? p.row_exp[m] : 0;
                 const int* ce = p.col_exp + n0;
                 auto val = [&](int j) { return FP16 ? scale_pow2(sum[j], e_row + ce[j]) : sum[j]; };
-                if (p.C64) {
+                if (p.splits > 1) {
+                    double* crow = p.part + ((size_t)sp * p.M + m) * p.N;
+#pragma unroll
+                    for (int j = 0; j < C_::HALF; ++j)
+                        if (n0 + j < p.N) crow[n0 + j] = (double)val(j);
+                } else if (p.C64) {
                     double* crow = p.C64 + (size_t)m * p.ldc64;
 #pragma unroll
                     for (int j = 0; j < C_::HALF; ++j)
@@ -374,6 +395,10 @@ int launch_pair_impl(const TcGemmArgs& a, void* stream) {
     p.num_n = a.Np / C_::BN;
     p.nk = (int)(a.Kp / kBK);
     p.kpb = (int)(a.KP / kBK);
+    p.splits = a.splits > 1 ? a.splits : 1;
+    p.kps = (p.nk + p.splits - 1) / p.splits;
+    if (p.splits > 1 && (!a.part64 || (p.nk + p.kps - 1) / p.kps != p.splits)) return (int)cudaErrorInvalidValue;
+    p.part = a.part64;
     p.C = a.C;
     p.ldc = a.ldc;
     p.C64 = a.C64;
@@ -401,7 +426,7 @@ int launch_pair_impl(const TcGemmArgs& a, void* stream) {
         cudaGetLastError();
         clusters = (a.num_sms > 0 ? a.num_sms : 148) / 2;
     }
-    if (clusters > tiles) clusters = tiles;
+    if (clusters > tiles * p.splits) clusters = tiles * p.splits;
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     e = cudaLaunchKernelEx(&cfg, k_tc_gemm_pair<FP16>, tah, tal, tbh, tbl, p);
     count_launch();

@@ -366,8 +366,9 @@ def test_pair_kernel_matches_single_cta_kernel(cuda, handle, monkeypatch, force,
     single-CTA kernel: identical bits. fp16x3: the single-CTA kernel keeps hi*hi and the cross products in two
     accumulators; the pair kernel scales the cross products by 2^-11 inside one accumulator and promotes every 64
     of K. Their sums round differently, so both kernels must sit within the accumulation bound of the exact slice
-    products."""
+    products. K is not split (the split-K form sums FP64 partials and is tested on its own)."""
     torch = cuda
+    monkeypatch.setenv("EMUGEMM_TC_SPLITK", "1")
     M, N, K = shape
     A = datagen.normal((M, K), 60 + M)
     B = datagen.normal((K, N), 61 + N)
@@ -387,6 +388,41 @@ def test_pair_kernel_matches_single_cta_kernel(cuda, handle, monkeypatch, force,
             assert d <= _accum_bound(K), (v, d)
 
 
+@pytest.mark.parametrize("force", [emugemm.BF16X3, emugemm.FP16X3])
+@pytest.mark.parametrize("shape,splits", [((256, 256, 20000), None), ((256, 256, 20000), 7), ((300, 260, 9000), None),
+                                          ((200, 520, 4100), 3), ((64, 96, 40000), None)])
+def test_pair_kernel_split_k(cuda, handle, monkeypatch, force, shape, splits):
+    """Few 256 x 256 pair tiles and a long K: each tile's K range is split over SM pairs (None: the built-in count;
+    else EMUGEMM_TC_SPLITK), every split writes an FP64 partial and the partials are summed in order. The result
+    sits within the accumulation bound of the exact slice products, within 1e-6 of the unsplit kernel's (relative
+    to ||AB||), and is deterministic; the FP64 partial entry point gives the same sum before its final rounding."""
+    torch = cuda
+    M, N, K = shape
+    A = datagen.normal((M, K), 90 + M)
+    B = datagen.normal((K, N), 91 + N)
+    monkeypatch.setenv("EMUGEMM_TC_KERNEL", "pair")
+    monkeypatch.setenv("EMUGEMM_TC_SPLITK", "1")
+    C1, _, _ = run_sgemm(torch, handle, A, B, force=force, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+    if splits is None:
+        monkeypatch.delenv("EMUGEMM_TC_SPLITK")
+    else:
+        monkeypatch.setenv("EMUGEMM_TC_SPLITK", str(splits))
+    Cs, _, _ = run_sgemm(torch, handle, A, B, force=force, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+    Cs2, _, _ = run_sgemm(torch, handle, A, B, force=force, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+    dA, dB = dev(torch, A), dev(torch, B)
+    P = torch.full((M, N), float("nan"), dtype=torch.float64, device="cuda")
+    handle.partial_f64(M, N, K, dA, K, dB, N, P, force, 1)
+    handle.sync()
+    R = oracle.gemm_f64(A, B)
+    nR = np.linalg.norm(R)
+    Rh = oracle.slice_product(A, B, kind=0 if force == emugemm.BF16X3 else 1)
+    assert np.isfinite(Cs).all()
+    assert np.array_equal(Cs, Cs2)
+    assert np.array_equal(P.cpu().numpy().astype(np.float32), Cs)
+    assert np.linalg.norm(Cs.astype(np.float64) - Rh) / nR <= _accum_bound(K)
+    assert np.linalg.norm(Cs.astype(np.float64) - C1) / nR <= 1e-6
+
+
 @pytest.mark.parametrize("variant", ["fused", "fusea"])
 @pytest.mark.parametrize("shape", [(256, 256, 128), (260, 516, 1004), (1024, 768, 2048), (2048, 2048, 512),
                                    (384, 264, 96), (1, 1, 1), (33, 65, 129), (260, 500, 20000)])
@@ -395,8 +431,9 @@ def test_fused_split_kernel_matches_presplit(cuda, handle, monkeypatch, variant,
     """bf16x3 with the split fused into the CTA-pair GEMM uses the same slices, k-steps and promotion points as
     the pre-split kernels: identical bits. `fused`: FP32 tiles of A and B by TMA, hi/lo made in shared memory;
     `fusea`: A's hi/lo made in the kernel and written into TMEM, B pre-split. Leading dimensions TMA cannot address
-    (not a multiple of 4 floats) fall back to the pre-split path."""
+    (not a multiple of 4 floats) fall back to the pre-split path. The pair kernel runs without K splits."""
     torch = cuda
+    monkeypatch.setenv("EMUGEMM_TC_SPLITK", "1")
     M, N, K = shape
     if gen == "normal":
         A = datagen.normal((M, K), 70 + M)
@@ -424,6 +461,7 @@ def test_fused_split_kernel_matches_presplit(cuda, handle, monkeypatch, variant,
 def test_fused_split_kernel_partial_f64(cuda, handle, monkeypatch, variant):
     """The FP64 partial output of the fused kernels (K-split building block) equals the pre-split kernel's."""
     torch = cuda
+    monkeypatch.setenv("EMUGEMM_TC_SPLITK", "1")
     M, N, K = 300, 260, 1536
     A = dev(torch, datagen.normal((M, K), 80))
     B = dev(torch, datagen.normal((K, N), 81))
