@@ -437,8 +437,18 @@ __global__ void k_reduce_f64(const double* __restrict__ P, int G, int M, int N, 
                              long ldc, double* C64, long ldc64) {
     const size_t total = (size_t)M * N;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        // planes in order g = 0 .. G-1; eight loads are issued before their adds, so the loads overlap while the
+        // additions keep their order
         double s = P[i];
-        for (int g = 1; g < G; ++g) s += P[(size_t)g * ldp_plane + i];
+        int g = 1;
+        for (; g + 8 <= G; g += 8) {
+            double v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = __ldg(P + (size_t)(g + u) * ldp_plane + i);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) s += v[u];
+        }
+        for (; g < G; ++g) s += P[(size_t)g * ldp_plane + i];
         const size_t m = i / N, n = i - m * N;
         if (C64) C64[m * ldc64 + n] = s;
         else C[m * ldc + n] = (float)s;
