@@ -87,6 +87,9 @@ def tc_kernel_name(M: int, N: int, K: int, scheme: str) -> str:
         pair_tiles, pairs = -(-M // 256) * -(-N // 256), 148 // 2
         if not fp16:
             code = 2 if (K > 1024 or pair_tiles >= pairs) else 1
+            nck = -(-K // 128)
+            if code == 2 and pair_tiles < 16 and min(pairs // pair_tiles, nck // 8) > 1:
+                code = 3
         else:
             code = 2 if ((K > 1024 or pair_tiles >= 512) if pair_tiles >= pairs else K >= 16384) else 1
     if fp16 and code >= 3:

@@ -164,7 +164,8 @@ static long round_up(long x, long m) { return (x + m - 1) / m * m; }
 // "pair", "fused", "fusea") wins, then the tile table's code, then the built-in choice, fitted to the B200 tile
 // table (tiles_b200.csv):
 //   bf16x3: CTA pairs when K > 1024 or their 256 x 256 tiles fill the SM pairs (pairs won every shape with K >= 4096
-//   and the K = 1024 shapes with at least 128 tiles; with fewer, single-CTA or fused tiles won by up to 8 %);
+//   and the K = 1024 shapes with at least 128 tiles; with fewer, single-CTA or fused tiles won by up to 8 %); the
+//   fused CTA-pair kernel instead when there are fewer than 16 tiles and K is split over the SM pairs;
 //   fp16x3: with tiles that fill the SM pairs, pairs when K > 1024 or at least 512 tiles (else the 128 x 128
 //   single-CTA tiles won, by up to 26 %); with fewer tiles, pairs when K >= 16384, long enough for the K splits.
 // EMUGEMM_LOG (set and not "0"): one stderr line per GEMM with the plan (scheme, chunks, predicted error, reason)
@@ -197,23 +198,25 @@ static void log_plan(const char* entry, int M, int N, long K, const emu_plan_t& 
                  p.reason ? p.reason : "");
 }
 
-// K splits of the CTA-pair kernel. When its 256 x 256 tiles cannot occupy the SM pairs (a few output tiles and a long
-// K: M = N = 256, K = 262144 is one tile for 74 pairs), each tile's K range is split into whole ranges of k-blocks
-// of at least 1024 values of K, for at most one unit per SM pair; every split writes an FP64 partial and the
-// partials are summed in order (deterministic). Within a split the promotion and accumulation order is unchanged.
-// EMUGEMM_TC_SPLITK (a count >= 1) overrides the choice.
-static int tc_split_count(long Mp, long Np, long Kp, int num_sms) {
-    const long nk = Kp / 64, tiles = (Mp / 256) * (Np / 256), pairs = num_sms / 2;
+// K splits of the CTA-pair kernels. When their 256 x 256 tiles cannot occupy the SM pairs (a few output tiles and a
+// long K: M = N = 256, K = 262144 is one tile for 74 pairs), each tile's K range is split into ranges of whole 128-K
+// chunks of the true K, at least 1024 values of K each, for at most one unit per SM pair; every split writes an FP64
+// partial and the partials are summed in order (deterministic). Every split starts a promotion chunk, so the pre-split
+// and the fused kernel split at the same values of K and stay bit-identical. EMUGEMM_TC_SPLITK (a count >= 1)
+// overrides the choice.
+static int tc_split_count(long Mp, long Np, long K, int num_sms) {
+    const long nck = (K + 127) / 128, tiles = (Mp / 256) * (Np / 256), pairs = num_sms / 2;   // 128-K chunks
     long want = 1;
     if (const char* v = std::getenv("EMUGEMM_TC_SPLITK")) want = std::atol(v);
-    else if (tiles > 0 && tiles < pairs) want = std::min(pairs / tiles, nk / 16);
+    else if (tiles > 0 && tiles < pairs) want = std::min(pairs / tiles, nck / 8);
     if (want < 1) want = 1;
-    if (want > nk) want = nk;
-    const long kps = (nk + want - 1) / want;
-    return (int)((nk + kps - 1) / kps);   // every split non-empty
+    if (want > nck) want = nck;
+    const long kpc = (nck + want - 1) / want;
+    return (int)((nck + kpc - 1) / kpc);   // every split non-empty
 }
 
 static int tc_kernel_choice(Handle* h, int M, int N, long K, bool fp16) {
+    if (h->pin_tc_code) return h->pin_tc_code;
     const char* v = std::getenv("EMUGEMM_TC_KERNEL");
     int code = 0;
     if (v && std::strcmp(v, "single") == 0) code = 1;
@@ -223,7 +226,14 @@ static int tc_kernel_choice(Handle* h, int M, int N, long K, bool fp16) {
     if (!code) code = lookup_tile(M, N, K, fp16 ? 2 : 1).tc_variant;
     if (!code) {
         const long pair_tiles = (round_up(M, 256) / 256) * (round_up(N, 256) / 256), pairs = h->num_sms / 2;
-        if (!fp16) code = (K > 1024 || pair_tiles >= pairs) ? 2 : 1;
+        if (!fp16) {
+            code = (K > 1024 || pair_tiles >= pairs) ? 2 : 1;
+            // few tiles and K split over the SM pairs: the GEMM reads each operand element once, so the split pass
+            // (8 bytes moved per element) costs more than the GEMM; the fused kernel splits in shared memory
+            // (256^2 x 262144: 106 -> 217 TFLOPS; at 16 tiles both kernels tie)
+            if (code == 2 && pair_tiles < 16 && tc_split_count(round_up(M, 256), round_up(N, 256), K, h->num_sms) > 1)
+                code = 3;
+        }
         else code = (pair_tiles >= pairs ? (K > 1024 || pair_tiles >= 512) : K >= 16384) ? 2 : 1;
     }
     if (fp16 && code >= 3) code = 2;
@@ -243,8 +253,18 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
     const int choice = tc_kernel_choice(h, M, N, K, fp16);
     if (choice == 3) {
         ProfScope ps(h, kProfTcGemm);
-        const int e = launch_tc_fused(A, lda, B, ldb, M, N, K, C, ldc, C64, ldc64, h->err_dev, h->num_sms, h->stream);
-        if (e != (int)cudaErrorNotSupported) return from_cuda(e);
+        const int splits = h->pin_splits ? h->pin_splits : tc_split_count(round_up(M, 256), round_up(N, 256), K, h->num_sms);
+        double* part = nullptr;
+        if (splits > 1) {
+            part = (double*)ws_get(h, kWsSplitK, (size_t)splits * M * N * sizeof(double));
+            if (!part) return EMUGEMM_STATUS_MEMORY_ERROR;
+        }
+        const int e = launch_tc_fused(A, lda, B, ldb, M, N, K, C, ldc, C64, ldc64, h->err_dev, h->num_sms, h->stream,
+                                      splits, part);
+        if (e != (int)cudaErrorNotSupported) {
+            if (e || splits <= 1) return from_cuda(e);
+            return from_cuda(launch_reduce_f64(part, splits, M, N, (long)M * N, C, ldc, C64, ldc64, h->stream));
+        }
         // operands TMA cannot address (odd leading dimension or alignment): pre-split below
     }
     if (choice == 4 && (lda & 3) == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0) {
@@ -313,7 +333,8 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
     t.err = h->err_dev;
     t.num_sms = h->num_sms;
     if (pair) {
-        t.splits = tc_split_count(Mp, Np, Kp, h->num_sms);
+        t.splits = h->pin_splits ? h->pin_splits : tc_split_count(Mp, Np, K, h->num_sms);
+        t.K = K;
         if (t.splits > 1) {
             t.part64 = (double*)ws_get(h, kWsSplitK, (size_t)t.splits * M * N * sizeof(double));
             if (!t.part64) return EMUGEMM_STATUS_MEMORY_ERROR;
@@ -589,6 +610,18 @@ emugemm_status_t emugemm_sgemm_host(emugemm_handle_t handle, int M, int N, long 
     if (w < 256) w = 256;
     while ((N + w - 1) / w > emu::kMaxHostPanels) w += 256;
     const int np = (int)((N + w - 1) / w);
+    // the panels use the kernel and K split count of the whole product, so C has the bits of the single call
+    const bool tc = plan.chosen == EMU_SCHEME_BF16X3 || plan.chosen == EMU_SCHEME_BF16X6 ||
+                    plan.chosen == EMU_SCHEME_FP16X3;
+    if (tc) {
+        const bool fp16 = plan.chosen == EMU_SCHEME_FP16X3;
+        h->pin_tc_code = emu::tc_kernel_choice(h, M, N, K, fp16);
+        h->pin_splits = emu::tc_split_count(emu::round_up(M, 256), emu::round_up(N, 256), K, h->num_sms);
+    }
+    struct Unpin {
+        Handle* h;
+        ~Unpin() { h->pin_tc_code = 0; h->pin_splits = 0; }
+    } unpin{h};
     e = cudaMemcpyAsync(dA, A, a_bytes, cudaMemcpyHostToDevice, cin);
     for (int j = 0; j < np && !e; ++j) {
         const long n0 = (long)j * w, wn = (n0 + w <= N) ? w : N - n0;

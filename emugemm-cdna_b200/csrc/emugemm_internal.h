@@ -103,6 +103,9 @@ struct Handle {
         const float* A = nullptr; int M = 0; long K = 0, lda = 0; int kind = -1; long Mp = 0, Kp = 0;
         const void* ws0 = nullptr; const void* ws1 = nullptr; const void* rexp = nullptr;
     } a_key;
+    // emugemm_sgemm_host: while its column panels run, the tensor-core kernel and K split count chosen for the whole
+    // product (0: choose per call), so that the panels round like the single call would.
+    int pin_tc_code = 0, pin_splits = 0;
     // emugemm_sgemm_host: copy streams (H2D, D2H) and events, created on first use.
     void* copy_in = nullptr;
     void* copy_out = nullptr;
@@ -170,6 +173,7 @@ struct TcGemmArgs {
     // FP64 partial plane part64[s] (M x N, ld N) instead of C, and the caller sums the planes in order.
     int splits = 1;
     double* part64 = nullptr;
+    long K = 0;          // the true K (split boundaries are 128-K chunks of it); 0: Kp
 };
 int launch_tc_gemm(const TcGemmArgs& a, void* stream);
 int tc_gemm_bn(int fp16);   // output tile width of the bf16x3 (0) / fp16x3 (1) kernel
@@ -177,9 +181,11 @@ int tc_gemm_bn(int fp16);   // output tile width of the bf16x3 (0) / fp16x3 (1) 
 int launch_tc_gemm_pair(const TcGemmArgs& a, void* stream);
 int tc_pair_bn(int fp16);
 // k_tc_fused.cu: bf16x3 with the split fused into the CTA-pair GEMM (FP32 tiles by TMA, no slices in HBM).
+// splits / part64: K splits on 128-K chunk boundaries with FP64 partial planes, as for launch_tc_gemm_pair.
 // Returns cudaErrorNotSupported unless lda, ldb are multiples of 4 and A, B are 16-byte aligned.
 int launch_tc_fused(const float* A, long lda, const float* B, long ldb, int M, int N, long K, float* C, long ldc,
-                    double* C64, long ldc64, unsigned* err, int num_sms, void* stream);
+                    double* C64, long ldc64, unsigned* err, int num_sms, void* stream, int splits = 1,
+                    double* part64 = nullptr);
 // k_tc_fused_a.cu: bf16x3 on CTA pairs with A split in the kernel into TMEM and B's slices pre-split (b_hi, b_lo:
 // Np x Kp in K panels of KP, Np a multiple of tc_fused_a_bn()). cudaErrorNotSupported unless lda % 4 == 0 and A is
 // 16-byte aligned.

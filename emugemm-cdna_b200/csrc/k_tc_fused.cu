@@ -84,10 +84,21 @@ struct CtlF {
 
 struct KParamsF {
     int M, N, num_m2, num_n, nk;
+    int splits, kps;   // K splits and k-blocks (of 32) per split; split boundaries fall on 128-K chunks
     float* C; long ldc;
     double* C64; long ldc64;
+    double* part;      // splits > 1: FP64 partial planes [splits][M][N]
     unsigned* err;
 };
+
+// Work unit u (tile x K split): the tile, the split and its k-block range [kb0, kb1).
+__device__ __forceinline__ void unit_of_f(const KParamsF& p, int num_tiles, int u, int& tile, int& sp, int& kb0,
+                                          int& kb1) {
+    tile = u % num_tiles;
+    sp = u / num_tiles;
+    kb0 = sp * p.kps;
+    kb1 = min(p.nk, kb0 + p.kps);
+}
 
 __device__ __forceinline__ void tile_coords_f(int t, int num_m2, int num_n, int& mb2, int& nb) {
     const int per_group = kGroupM * num_n;
@@ -156,7 +167,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool leader = rank == 0;
     const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
     const int num_tiles = p.num_m2 * p.num_n;
-    const int nchunks = (p.nk + kChunkKB - 1) / kChunkKB;
+    const int num_units = num_tiles * p.splits;
     const bool is_epi = warp >= kEpiFirst && warp < kEpiFirst + kEpiWarps;
 
     if (threadIdx.x == 0) {
@@ -196,12 +207,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // ---------------- TMA producer: FP32 tiles of this CTA's A rows and B columns ----------------
                 long it = 0;
                 bool ok = true;
-                for (int t = pair; t < num_tiles && ok; t += num_pairs) {
-                    int mb2, nb;
+                for (int u = pair; u < num_units && ok; u += num_pairs) {
+                    int t, sp, kbb, kbe, mb2, nb;
+                    unit_of_f(p, num_tiles, u, t, sp, kbb, kbe);
                     tile_coords_f(t, p.num_m2, p.num_n, mb2, nb);
                     const int a_row = mb2 * 2 * kBM + (int)rank * kBM;
                     const int b_col = nb * kBN + (int)rank * kBNH;
-                    for (int kb = 0; kb < p.nk; ++kb, ++it) {
+                    for (int kb = kbb; kb < kbe; ++kb, ++it) {
                         const int s = (int)(it % kF32Stages);
                         const uint32_t ph = (uint32_t)((it / kF32Stages) & 1);
                         if (!mbar_wait(&ctl->f32_empty[s], ph ^ 1u, abort, p.err, kErrTimeoutProducer)) { ok = false; break; }
@@ -223,8 +235,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // ---------------- leader: pair MMA issuer ----------------
                 long it = 0, ch = 0;
                 bool ok = true;
-                for (int t = pair; t < num_tiles && ok; t += num_pairs) {
-                    for (int kb0 = 0; kb0 < p.nk && ok; kb0 += kChunkKB, ++ch) {
+                for (int u = pair; u < num_units && ok; u += num_pairs) {
+                    int t, sp, kbb, kbe;
+                    unit_of_f(p, num_tiles, u, t, sp, kbb, kbe);
+                    for (int kb0 = kbb; kb0 < kbe && ok; kb0 += kChunkKB, ++ch) {
                         const int b = (int)(ch & 1);
                         const uint32_t bph = (uint32_t)((ch >> 1) & 1);
                         if (!mbar_wait_cluster(&ctl->tmem_empty[b], bph ^ 1u, abort, p.err, kErrTimeoutMma)) {
@@ -233,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         tc_fence_after();
                         const uint32_t d = tmem_base + (uint32_t)(b * kAccCols);
-                        const int kb1 = min(p.nk, kb0 + kChunkKB);
+                        const int kb1 = min(kbe, kb0 + kChunkKB);
                         for (int kb = kb0; kb < kb1; ++kb, ++it) {
                             const int s = (int)(it % kBfStages);
                             const uint32_t ph = (uint32_t)((it / kBfStages) & 1);
@@ -278,8 +292,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr int kBatch = 3;                                        // items loaded before any is stored
             long it = 0;
             bool ok = true;
-            for (int t = pair; t < num_tiles && ok; t += num_pairs) {
-                for (int kb = 0; kb < p.nk; ++kb, ++it) {
+            for (int u = pair; u < num_units && ok; u += num_pairs) {
+                int t, sp, kbb, kbe;
+                unit_of_f(p, num_tiles, u, t, sp, kbb, kbe);
+                for (int kb = kbb; kb < kbe; ++kb, ++it) {
                     const int s = (int)(it % kF32Stages);
                     const uint32_t ph = (uint32_t)((it / kF32Stages) & 1);
                     const int q = (int)(it % kBfStages);
@@ -355,9 +371,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lead_te0 = mapa_shared(smem_u32(&ctl->tmem_empty[0]), 0);
         long ch = 0;
         bool ok = true;
-        for (int t = pair; t < num_tiles && ok; t += num_pairs) {
-            int mb2, nb;
+        for (int u = pair; u < num_units && ok; u += num_pairs) {
+            int t, sp, kbb, kbe, mb2, nb;
+            unit_of_f(p, num_tiles, u, t, sp, kbb, kbe);
             tile_coords_f(t, p.num_m2, p.num_n, mb2, nb);
+            const int nchunks = (kbe - kbb + kChunkKB - 1) / kChunkKB;
             float sum[kHalf];
 #pragma unroll
             for (int j = 0; j < kHalf; ++j) sum[j] = 0.f;
@@ -384,7 +402,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int m = mb2 * 2 * kBM + row_in_tile;
             if (m < p.M) {
                 const int n0 = nb * kBN + col0;
-                if (p.C64) {
+                if (p.splits > 1) {
+                    double* crow = p.part + ((size_t)sp * p.M + m) * p.N;
+#pragma unroll
+                    for (int j = 0; j < kHalf; ++j)
+                        if (n0 + j < p.N) crow[n0 + j] = (double)sum[j];
+                } else if (p.C64) {
                     double* crow = p.C64 + (size_t)m * p.ldc64;
 #pragma unroll
                     for (int j = 0; j < kHalf; ++j)
@@ -422,7 +445,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // A: M x K row-major FP32 (lda), B: K x N row-major FP32 (ldb); needs lda % 4 == ldb % 4 == 0 and 16-byte
 // aligned A, B (TMA). Returns cudaErrorNotSupported when those do not hold, so the caller can pre-split instead.
 int launch_tc_fused(const float* A, long lda, const float* B, long ldb, int M, int N, long K, float* C, long ldc,
-                    double* C64, long ldc64, unsigned* err, int num_sms, void* stream) {
+                    double* C64, long ldc64, unsigned* err, int num_sms, void* stream, int splits,
+                    double* part64) {
     if ((lda & 3) || (ldb & 3) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
         return (int)cudaErrorNotSupported;
     PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
@@ -456,6 +480,15 @@ int launch_tc_fused(const float* A, long lda, const float* B, long ldb, int M, i
     p.num_m2 = (M + 2 * kBM - 1) / (2 * kBM);
     p.num_n = (N + kBN - 1) / kBN;
     p.nk = (int)((K + kBK - 1) / kBK);
+    p.splits = splits > 1 ? splits : 1;
+    p.kps = p.nk;
+    if (p.splits > 1) {
+        const int nck = (int)((K + 127) / 128);   // 128-K chunks of the true K, as in launch_tc_gemm_pair
+        const int kpc = (nck + p.splits - 1) / p.splits;
+        p.kps = kpc * kChunkKB;
+        if (!part64 || (nck + kpc - 1) / kpc != p.splits) return (int)cudaErrorInvalidValue;
+    }
+    p.part = part64;
     p.C = C;
     p.ldc = ldc;
     p.C64 = C64;
@@ -481,7 +514,7 @@ int launch_tc_fused(const float* A, long lda, const float* B, long ldb, int M, i
         cudaGetLastError();
         clusters = (num_sms > 0 ? num_sms : 148) / 2;
     }
-    if (clusters > tiles) clusters = tiles;
+    if (clusters > tiles * p.splits) clusters = tiles * p.splits;
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     e = cudaLaunchKernelEx(&cfg, k_tc_fused, ta, tb, p);
     count_launch();

@@ -396,8 +396,17 @@ int launch_pair_impl(const TcGemmArgs& a, void* stream) {
     p.nk = (int)(a.Kp / kBK);
     p.kpb = (int)(a.KP / kBK);
     p.splits = a.splits > 1 ? a.splits : 1;
-    p.kps = (p.nk + p.splits - 1) / p.splits;
-    if (p.splits > 1 && (!a.part64 || (p.nk + p.kps - 1) / p.kps != p.splits)) return (int)cudaErrorInvalidValue;
+    p.kps = p.nk;
+    if (p.splits > 1) {
+        // split boundaries on 128-K chunks of the true K (two k-blocks), so that every split starts a promotion
+        // chunk and the fused kernel, whose k-blocks are 32 deep, splits at the same values of K; k-blocks past
+        // the last split are zero padding of the K panels
+        const long K = a.K > 0 ? a.K : a.Kp;
+        const int nck = (int)((K + 127) / 128);
+        const int kpc = (nck + p.splits - 1) / p.splits;
+        p.kps = 2 * kpc;
+        if (!a.part64 || (nck + kpc - 1) / kpc != p.splits) return (int)cudaErrorInvalidValue;
+    }
     p.part = a.part64;
     p.C = a.C;
     p.ldc = a.ldc;

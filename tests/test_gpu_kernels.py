@@ -457,6 +457,29 @@ def test_fused_split_kernel_matches_presplit(cuda, handle, monkeypatch, variant,
         assert splits["fusea"] == 1                           # B's split (or both, on the fallback)
 
 
+@pytest.mark.parametrize("splits", [None, 5])
+@pytest.mark.parametrize("shape", [(256, 256, 40000), (260, 500, 20000), (300, 264, 9000)])
+def test_fused_split_k_matches_pair(cuda, handle, monkeypatch, splits, shape):
+    """Split-K in the fused kernel (FP32 tiles split in the kernel) and in the pre-split pair kernel: both split K on
+    the same 128-K chunk boundaries and promote at the same points, so C is bit-identical; it also sits within the
+    accumulation bound of the exact slice products (None: the built-in split count, else EMUGEMM_TC_SPLITK)."""
+    torch = cuda
+    if splits is not None:
+        monkeypatch.setenv("EMUGEMM_TC_SPLITK", str(splits))
+    M, N, K = shape
+    A = datagen.normal((M, K), 95 + M)
+    B = datagen.normal((K, N), 96 + N)
+    out = {}
+    for v in ("pair", "fused"):
+        monkeypatch.setenv("EMUGEMM_TC_KERNEL", v)
+        out[v], _, _ = run_sgemm(torch, handle, A, B, force=emugemm.BF16X3, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+    assert np.isfinite(out["fused"]).all()
+    assert np.array_equal(out["fused"], out["pair"])
+    R = oracle.gemm_f64(A, B)
+    d = np.linalg.norm(out["fused"].astype(np.float64) - oracle.slice_product(A, B, kind=0)) / np.linalg.norm(R)
+    assert d <= _accum_bound(K)
+
+
 @pytest.mark.parametrize("variant", ["fused", "fusea"])
 def test_fused_split_kernel_partial_f64(cuda, handle, monkeypatch, variant):
     """The FP64 partial output of the fused kernels (K-split building block) equals the pre-split kernel's."""
@@ -495,6 +518,24 @@ def test_sgemm_host_matches_device(cuda, handle, force, shape):
         handle.sync()
         assert p.chosen == force
         assert np.array_equal(hC.numpy(), want), (shape, use)
+
+
+@pytest.mark.parametrize("force", [emugemm.BF16X3, emugemm.FP16X3])
+def test_sgemm_host_long_k_matches_device(cuda, handle, force):
+    """Few output tiles and a long K: the single call splits K over the SM pairs (bf16x3 in the fused kernel). The
+    host-buffer entry point runs column panels with fewer tiles each, but with the kernel and split count of the
+    whole product, so its C has the same bits."""
+    torch = cuda
+    M, N, K = 256, 1024, 24000
+    A = datagen.normal((M, K), 93)
+    B = datagen.normal((K, N), 94)
+    want, _, _ = run_sgemm(torch, handle, A, B, force=force, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+    hA = torch.from_numpy(A).pin_memory()
+    hB = torch.from_numpy(B).pin_memory()
+    hC = torch.full((M, N), float("nan")).pin_memory()
+    handle.sgemm_host(M, N, K, hA, hB, hC, force=force, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+    handle.sync()
+    assert np.array_equal(hC.numpy(), want)
 
 
 def test_log_lines(cuda):
