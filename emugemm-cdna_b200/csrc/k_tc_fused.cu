@@ -20,6 +20,9 @@
 // warp), the peer's each send a 16-byte cp.async.bulk that completes those bytes on the leader's barrier (a
 // thread-issued remote arrive with release at cluster scope stalls its warp for ~1200 cycles). The leader's commits
 // free the bf16 stages and publish TMEM chunks in both CTAs. All waits are bounded.
+// K splits (few output tiles, long K): a work unit is a tile and a range of whole 128-K chunks, as in
+// k_tc_gemm2.cu, with the same boundaries; each split writes an FP64 partial plane that the caller sums in order, so
+// the two kernels stay bit-identical. Reading each FP32 operand element once, this kernel then needs no split pass.
 #include "device_utils.cuh"
 #include "emugemm_internal.h"
 

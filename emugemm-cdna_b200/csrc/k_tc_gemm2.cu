@@ -12,6 +12,10 @@
 //   accumulate first, then the first hi*hi MMA scales the accumulator by 2^-11 on the way in (scale-input-d), then
 //   the remaining hi*hi follow. One accumulator of 256 columns per buffer, as for bf16x3.
 //
+// K splits (few output tiles, long K; TcGemmArgs::splits > 1): a work unit is a tile and a range of whole 128-K
+// chunks of the true K; units are dealt to the SM pairs like tiles, and each writes an FP64 partial plane that the
+// caller sums in order.
+//
 // Cross-CTA signalling:
 //   both CTAs' TMA loads of a stage complete on the LEADER's full barrier (TMA .cta_group::2 form, each
 //   load writing only its own CTA), which the leader armed with the bytes of both halves;
