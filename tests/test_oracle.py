@@ -145,3 +145,21 @@ def test_family2_rho_is_tunable():
         A, B = datagen.family2(M, M, K, rho_t)
         rt = oracle.rho_true(A, B)
         assert rho_t / 3 < rt < rho_t * 3
+
+
+def test_rescale_forms_equal_ldexpf():
+    """The fp16x3 store tail undoes the 2^e row/column scaling in two forms: x * 2^e with 2^e a normal float (when
+    -126 <= e <= 127), and float(double(x) * 2^e) otherwise. Both round once, so each equals ldexpf(x, e) bit for
+    bit, subnormal, zero and overflowing results included (numpy's float32 ldexp as the reference)."""
+    rng = np.random.default_rng(7)
+    x = (rng.standard_normal(200000) * np.exp2(rng.integers(-40, 41, 200000))).astype(np.float32)
+    x[:4] = [0.0, -0.0, np.float32(2.0 ** -149), np.float32(3.4e38)]
+    e = rng.integers(-330, 231, x.size).astype(np.int32)
+    normal = (e >= -126) & (e <= 127)
+    with np.errstate(over="ignore"):   # overflowing results are part of the check
+        want = np.ldexp(x, e).astype(np.float32)
+        fast = (x[normal] * np.exp2(e[normal]).astype(np.float32)).astype(np.float32)
+        exact = (x.astype(np.float64) * np.exp2(e.astype(np.float64))).astype(np.float32)
+    assert np.array_equal(fast.view(np.uint32), want[normal].view(np.uint32))
+    assert np.array_equal(exact.view(np.uint32), want.view(np.uint32))
+    assert (~normal).sum() > 1000 and (np.abs(want) < 2.0 ** -126).sum() > 100 and np.isinf(want).sum() > 100
