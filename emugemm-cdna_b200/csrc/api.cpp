@@ -160,9 +160,9 @@ static void prof_clear(Handle* h) {
 static long round_up(long x, long m) { return (x + m - 1) / m * m; }
 
 // Tensor-core kernel for a shape: 1 = single-CTA, 2 = CTA pair, 3 = CTA pair with the split fused in, 4 = CTA pair
-// with A split into TMEM in the kernel (3 and 4: bf16x3). The environment variable EMUGEMM_TC_KERNEL ("single",
-// "pair", "fused", "fusea") wins, then the tile table's code, then the built-in choice, fitted to the B200 tile
-// table (tiles_b200.csv):
+// with A split into TMEM in the kernel (3 and 4: bf16x3). The handle's EMUGEMM_ATTR_TC_KERNEL (default: the
+// environment variable EMUGEMM_TC_KERNEL, "single", "pair", "fused" or "fusea", read when the handle was created)
+// wins, then the tile table's code, then the built-in choice, fitted to the B200 tile table (tiles_b200.csv):
 //   bf16x3: CTA pairs when K > 1024 or their 256 x 256 tiles fill the SM pairs (pairs won every shape with K >= 4096
 //   and the K = 1024 shapes with at least 128 tiles; with fewer, single-CTA or fused tiles won by up to 8 %); the
 //   fused CTA-pair kernel instead when there are fewer than 16 tiles and K is split over the SM pairs;
@@ -202,12 +202,12 @@ static void log_plan(const char* entry, int M, int N, long K, const emu_plan_t& 
 // long K: M = N = 256, K = 262144 is one tile for 74 pairs), each tile's K range is split into ranges of whole 128-K
 // chunks of the true K, at least 1024 values of K each, for at most one unit per SM pair; every split writes an FP64
 // partial and the partials are summed in order (deterministic). Every split starts a promotion chunk, so the pre-split
-// and the fused kernel split at the same values of K and stay bit-identical. EMUGEMM_TC_SPLITK (a count >= 1)
-// overrides the choice.
-static int tc_split_count(long Mp, long Np, long K, int num_sms) {
+// and the fused kernel split at the same values of K and stay bit-identical. The handle's EMUGEMM_ATTR_TC_SPLITK
+// (`forced`, a count >= 1; 0 = choose) overrides the choice.
+static int tc_split_count(long Mp, long Np, long K, int num_sms, int forced) {
     const long nck = (K + 127) / 128, tiles = (Mp / 256) * (Np / 256), pairs = num_sms / 2;   // 128-K chunks
     long want = 1;
-    if (const char* v = std::getenv("EMUGEMM_TC_SPLITK")) want = std::atol(v);
+    if (forced > 0) want = forced;
     else if (tiles > 0 && tiles < pairs) want = std::min(pairs / tiles, nck / 8);
     if (want < 1) want = 1;
     if (want > nck) want = nck;
@@ -217,12 +217,7 @@ static int tc_split_count(long Mp, long Np, long K, int num_sms) {
 
 static int tc_kernel_choice(Handle* h, int M, int N, long K, bool fp16) {
     if (h->pin_tc_code) return h->pin_tc_code;
-    const char* v = std::getenv("EMUGEMM_TC_KERNEL");
-    int code = 0;
-    if (v && std::strcmp(v, "single") == 0) code = 1;
-    else if (v && std::strcmp(v, "pair") == 0) code = 2;
-    else if (v && std::strcmp(v, "fused") == 0) code = 3;
-    else if (v && std::strcmp(v, "fusea") == 0) code = 4;
+    int code = h->tc_kernel;
     if (!code) code = lookup_tile(M, N, K, fp16 ? 2 : 1).tc_variant;
     if (!code) {
         const long pair_tiles = (round_up(M, 256) / 256) * (round_up(N, 256) / 256), pairs = h->num_sms / 2;
@@ -231,7 +226,8 @@ static int tc_kernel_choice(Handle* h, int M, int N, long K, bool fp16) {
             // few tiles and K split over the SM pairs: the GEMM reads each operand element once, so the split pass
             // (8 bytes moved per element) costs more than the GEMM; the fused kernel splits in shared memory
             // (256^2 x 262144: 106 -> 217 TFLOPS; at 16 tiles both kernels tie)
-            if (code == 2 && pair_tiles < 16 && tc_split_count(round_up(M, 256), round_up(N, 256), K, h->num_sms) > 1)
+            if (code == 2 && pair_tiles < 16 &&
+                tc_split_count(round_up(M, 256), round_up(N, 256), K, h->num_sms, h->tc_splitk) > 1)
                 code = 3;
         }
         else code = (pair_tiles >= pairs ? (K > 1024 || pair_tiles >= 512) : K >= 16384) ? 2 : 1;
@@ -253,7 +249,8 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
     const int choice = tc_kernel_choice(h, M, N, K, fp16);
     if (choice == 3) {
         ProfScope ps(h, kProfTcGemm);
-        const int splits = h->pin_splits ? h->pin_splits : tc_split_count(round_up(M, 256), round_up(N, 256), K, h->num_sms);
+        const int splits = h->pin_splits ? h->pin_splits
+                                         : tc_split_count(round_up(M, 256), round_up(N, 256), K, h->num_sms, h->tc_splitk);
         double* part = nullptr;
         if (splits > 1) {
             part = (double*)ws_get(h, kWsSplitK, (size_t)splits * M * N * sizeof(double));
@@ -333,7 +330,7 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
     t.err = h->err_dev;
     t.num_sms = h->num_sms;
     if (pair) {
-        t.splits = h->pin_splits ? h->pin_splits : tc_split_count(Mp, Np, K, h->num_sms);
+        t.splits = h->pin_splits ? h->pin_splits : tc_split_count(Mp, Np, K, h->num_sms, h->tc_splitk);
         t.K = K;
         if (t.splits > 1) {
             t.part64 = (double*)ws_get(h, kWsSplitK, (size_t)t.splits * M * N * sizeof(double));
@@ -346,14 +343,32 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
     return from_cuda(launch_reduce_f64(t.part64, t.splits, M, N, (long)M * N, C, ldc, C64, ldc64, h->stream));
 }
 
-// FP32 SIMT tile code for a shape: EMUGEMM_FP32_TILE (16, 32, 64 or 128) wins, then the tile table's code (looked up at
-// the chunk length), else 0 (the built-in choice of launch_fp32_gemm).
-static int fp32_tile_choice(int M, int N, long K, int chunks) {
-    if (const char* v = std::getenv("EMUGEMM_FP32_TILE")) {
-        const int t = std::atoi(v);
-        if (t == 16 || t == 32 || t == 64 || t == 128) return t;
-    }
+// FP32 SIMT tile code for a shape: `forced` (the handle's EMUGEMM_ATTR_FP32_TILE: 16, 32, 64 or 128; 0 = choose) wins,
+// then the tile table's code (looked up at the chunk length), else 0 (the built-in choice of launch_fp32_gemm).
+static int fp32_tile_choice(int M, int N, long K, int chunks, int forced) {
+    if (forced == 16 || forced == 32 || forced == 64 || forced == 128) return forced;
     return lookup_tile(M, N, K / (chunks < 1 ? 1 : chunks), 0).fp32_bm;
+}
+
+// Defaults of the per-handle kernel choices, from the environment (read when a handle is created).
+static int env_tc_kernel() {
+    const char* v = std::getenv("EMUGEMM_TC_KERNEL");
+    if (!v) return 0;
+    if (std::strcmp(v, "single") == 0) return 1;
+    if (std::strcmp(v, "pair") == 0) return 2;
+    if (std::strcmp(v, "fused") == 0) return 3;
+    if (std::strcmp(v, "fusea") == 0) return 4;
+    return 0;
+}
+static int env_tc_splitk() {
+    const char* v = std::getenv("EMUGEMM_TC_SPLITK");
+    const long n = v ? std::atol(v) : 0;
+    return n >= 1 && n <= (1L << 20) ? (int)n : 0;
+}
+static int env_fp32_tile() {
+    const char* v = std::getenv("EMUGEMM_FP32_TILE");
+    const int t = v ? std::atoi(v) : 0;
+    return (t == 16 || t == 32 || t == 64 || t == 128) ? t : 0;
 }
 
 static emugemm_status_t run_fp32(Handle* h, int M, int N, long K, const float* A, long lda, const float* B, long ldb,
@@ -364,7 +379,7 @@ static emugemm_status_t run_fp32(Handle* h, int M, int N, long K, const float* A
     f.M = M; f.N = N; f.K = K;
     f.chunks = chunks < 1 ? 1 : chunks;
     f.num_sms = h->num_sms;
-    f.bm = fp32_tile_choice(M, N, K, f.chunks);
+    f.bm = fp32_tile_choice(M, N, K, f.chunks, h->fp32_tile);
     f.ws64 = nullptr;
     size_t wsb = fp32_gemm_ws_bytes(f);
     if (wsb) {
@@ -422,6 +437,9 @@ emugemm_status_t emugemm_create_handle(emugemm_handle_t* out) {
     if (!emu::is_sm100(dev)) return EMUGEMM_STATUS_ARCH_MISMATCH;
     Handle* h = new Handle();
     h->device = dev;
+    h->tc_kernel = emu::env_tc_kernel();
+    h->tc_splitk = emu::env_tc_splitk();
+    h->fp32_tile = emu::env_fp32_tile();
     cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, dev);
     if (cudaHostAlloc((void**)&h->err_host, sizeof(unsigned), cudaHostAllocMapped) != cudaSuccess ||
         cudaHostGetDevicePointer((void**)&h->err_dev, h->err_host, 0) != cudaSuccess) {
@@ -465,6 +483,39 @@ emugemm_status_t emugemm_set_workspace_limit(emugemm_handle_t handle, size_t byt
     if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
     h->ws_limit = bytes;
     return EMUGEMM_STATUS_SUCCESS;
+}
+
+emugemm_status_t emugemm_set_attr(emugemm_handle_t handle, int attr, long value) {
+    Handle* h = reinterpret_cast<Handle*>(handle);
+    if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
+    switch (attr) {
+        case EMUGEMM_ATTR_TC_KERNEL:
+            if (value < 0 || value > 4) return EMUGEMM_STATUS_INVALID_VALUE;
+            h->tc_kernel = (int)value;
+            return EMUGEMM_STATUS_SUCCESS;
+        case EMUGEMM_ATTR_TC_SPLITK:
+            if (value < 0 || value > (1L << 20)) return EMUGEMM_STATUS_INVALID_VALUE;
+            h->tc_splitk = (int)value;
+            return EMUGEMM_STATUS_SUCCESS;
+        case EMUGEMM_ATTR_FP32_TILE:
+            if (value != 0 && value != 16 && value != 32 && value != 64 && value != 128)
+                return EMUGEMM_STATUS_INVALID_VALUE;
+            h->fp32_tile = (int)value;
+            return EMUGEMM_STATUS_SUCCESS;
+    }
+    return EMUGEMM_STATUS_INVALID_VALUE;
+}
+
+emugemm_status_t emugemm_get_attr(emugemm_handle_t handle, int attr, long* value) {
+    Handle* h = reinterpret_cast<Handle*>(handle);
+    if (!h) return EMUGEMM_STATUS_INVALID_HANDLE;
+    if (!value) return EMUGEMM_STATUS_INVALID_POINTER;
+    switch (attr) {
+        case EMUGEMM_ATTR_TC_KERNEL: *value = h->tc_kernel; return EMUGEMM_STATUS_SUCCESS;
+        case EMUGEMM_ATTR_TC_SPLITK: *value = h->tc_splitk; return EMUGEMM_STATUS_SUCCESS;
+        case EMUGEMM_ATTR_FP32_TILE: *value = h->fp32_tile; return EMUGEMM_STATUS_SUCCESS;
+    }
+    return EMUGEMM_STATUS_INVALID_VALUE;
 }
 
 emugemm_status_t emugemm_sync(emugemm_handle_t handle) {
@@ -616,7 +667,7 @@ emugemm_status_t emugemm_sgemm_host(emugemm_handle_t handle, int M, int N, long 
     if (tc) {
         const bool fp16 = plan.chosen == EMU_SCHEME_FP16X3;
         h->pin_tc_code = emu::tc_kernel_choice(h, M, N, K, fp16);
-        h->pin_splits = emu::tc_split_count(emu::round_up(M, 256), emu::round_up(N, 256), K, h->num_sms);
+        h->pin_splits = emu::tc_split_count(emu::round_up(M, 256), emu::round_up(N, 256), K, h->num_sms, h->tc_splitk);
     }
     struct Unpin {
         Handle* h;
@@ -701,12 +752,16 @@ emugemm_status_t emugemm_reduce_f64(emugemm_handle_t handle, int M, int N, int G
     return emu::from_cuda(emu::launch_reduce_f64(P, G, M, N, (long)M * N, C, N, nullptr, 0, h->stream));
 }
 
-int emugemm_fp32_groups(int M, int N, long K, int chunks, int num_sms) {
+int emugemm_fp32_groups_tile(int M, int N, long K, int chunks, int num_sms, int tile) {
     emu::Fp32GemmArgs f{};
     f.M = M; f.N = N; f.K = K; f.chunks = chunks < 1 ? 1 : chunks; f.num_sms = num_sms;
     f.lda = K; f.ldb = N;   // contiguous operands, as the caller's own rows would be
-    f.bm = emu::fp32_tile_choice(M, N, K, f.chunks);
+    f.bm = emu::fp32_tile_choice(M, N, K, f.chunks, tile);
     return emu::fp32_gemm_groups(f);
+}
+
+int emugemm_fp32_groups(int M, int N, long K, int chunks, int num_sms) {
+    return emugemm_fp32_groups_tile(M, N, K, chunks, num_sms, emu::env_fp32_tile());
 }
 
 unsigned long long emugemm_kernel_launch_count(void) { return emu::g_launches.load(); }

@@ -56,9 +56,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 }
 
 // Bounded wait for the phase with the given parity. Returns false when the wait gave up, either because
-// the time limit passed (then *err gets err_bit) or because another role already raised *abort.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          unsigned* err, unsigned err_bit) {
+// `limit_ns` passed (then *err gets err_bit) or because another role already raised *abort.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort, unsigned* err,
+                                              unsigned err_bit, unsigned long long limit_ns) {
     const uint32_t a = smem_u32(bar);
     if (mbar_try_wait(a, parity)) return true;
     unsigned long long t0 = globaltimer();
@@ -66,13 +66,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
         if (mbar_try_wait(a, parity)) return true;
         if ((it & 63u) == 0) {
             if (*abort) return false;
-            if (globaltimer() - t0 > kWaitLimitNs) {
+            if (globaltimer() - t0 > limit_ns) {
                 *abort = 1;
                 if (err) atomicOr(err, err_bit);
                 return false;
             }
         }
     }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          unsigned* err, unsigned err_bit) {
+    return mbar_wait_for(bar, parity, abort, err, err_bit, kWaitLimitNs);
 }
 
 // ---- clusters (CTA pairs) ------------------------------------------------------------------------------

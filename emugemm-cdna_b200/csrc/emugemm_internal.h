@@ -103,6 +103,9 @@ struct Handle {
         const float* A = nullptr; int M = 0; long K = 0, lda = 0; int kind = -1; long Mp = 0, Kp = 0;
         const void* ws0 = nullptr; const void* ws1 = nullptr; const void* rexp = nullptr;
     } a_key;
+    // Kernel choices (emugemm_set_attr; defaults from the environment when the handle is created): tensor-core kernel
+    // code (0 auto), K splits of the CTA-pair kernels (0 auto), FP32 SIMT tile code (0 auto).
+    int tc_kernel = 0, tc_splitk = 0, fp32_tile = 0;
     // emugemm_sgemm_host: while its column panels run, the tensor-core kernel and K split count chosen for the whole
     // product (0: choose per call), so that the panels round like the single call would.
     int pin_tc_code = 0, pin_splits = 0;

@@ -32,6 +32,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <mutex>
 
 namespace emu {
@@ -75,6 +76,7 @@ struct Ctl {
     uint64_t tmem_full[2];
     uint64_t tmem_empty[2];
     uint64_t drain;
+    uint64_t never;            // nothing arrives on it: the target of the test stall below
     uint32_t tmem_base;
     int abort;
 };
@@ -86,7 +88,11 @@ struct KParams {
     double* C64; long ldc64;
     const int* row_exp; const int* col_exp;
     unsigned* err;
+    int stall_chunk;   // test hook: the MMA issuer waits on `never` before this chunk (-1: never)
 };
+
+// Limit of the test stall's wait: short, so a test of failure reporting takes about a millisecond.
+constexpr unsigned long long kStallLimitNs = 1000000ull;
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
     const int per_group = kGroupM * num_n;
@@ -132,6 +138,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&ctl->tmem_empty[b], 32 * kEpiWarps);
         }
         mbar_init(&ctl->drain, 1);
+        mbar_init(&ctl->never, 1);
         ctl->abort = 0;
         fence_mbar_init();
     }
@@ -187,6 +194,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int kb0 = 0; kb0 < p.nk && ok; kb0 += kChunkKB, ++ch) {
                     const int b = (int)(ch & 1);
                     const uint32_t bph = (uint32_t)((ch >> 1) & 1);
+                    // test hook: a wait that must run out, with MMAs of earlier chunks and loads of later stages in
+                    // flight; the kernel then unwinds exactly as after any timed-out wait
+                    if (ch == (long)p.stall_chunk &&
+                        !mbar_wait_for(&ctl->never, 0, abort, p.err, kErrTimeoutMma, kStallLimitNs)) {
+                        ok = false;
+                        break;
+                    }
                     if (!mbar_wait(&ctl->tmem_empty[b], bph ^ 1u, abort, p.err, kErrTimeoutMma)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t d_main = tmem_base + (uint32_t)(b * C_::ACC_COLS);
@@ -319,6 +333,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---- host side: tensor maps ------------------------------------------------------------------------------
+// Launches still to stall (emugemm_test_stall_next_launches).
+std::atomic<int> g_stall_launches{0};
+
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
 
@@ -374,6 +391,9 @@ int launch_impl(const TcGemmArgs& a, void* stream) {
     p.row_exp = a.row_exp;
     p.col_exp = a.col_exp;
     p.err = a.err;
+    p.stall_chunk = -1;
+    for (int n = g_stall_launches.load(); n > 0;)
+        if (g_stall_launches.compare_exchange_weak(n, n - 1)) { p.stall_chunk = 1; break; }
     const int tiles = p.num_m * p.num_n;
     int grid = a.num_sms > 0 ? a.num_sms : 148;
     if (grid > tiles) grid = tiles;
@@ -397,3 +417,5 @@ int launch_tc_gemm(const TcGemmArgs& a, void* stream) {
 }
 
 }  // namespace emu
+
+extern "C" void emugemm_test_stall_next_launches(int n) { emu::g_stall_launches.store(n < 0 ? 0 : n); }

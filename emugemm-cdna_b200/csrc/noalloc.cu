@@ -18,8 +18,12 @@
 //     streams, or different host threads without ordering) race on it and produce wrong results; callers
 //     must order them, for example by issuing them all on one stream.
 //   - The array keeps the previous call's contents. Each call rewrites every slice element the GEMM reads
-//     (zero padding included) and clears its device status word before launching, so no stale value
-//     reaches the result.
+//     (zero padding included), so no stale slice value reaches the result.
+//   - A bounded device-side wait that gives up (the kernel then unwinds and leaves C incomplete) sets a bit
+//     in a status word at the end of the array. The call itself returns before its kernels run, so it
+//     cannot report that; emugemm_noalloc_sync(stream) synchronises the stream, reads the word, clears it
+//     and returns EMUGEMM_STATUS_TIMEOUT if any call since the previous query timed out. The word stays
+//     set until it is read, so one query after several calls reports a timeout in any of them.
 //   - The first call on a device resolves the array's device address with cudaGetSymbolAddress (once per
 //     device, with that device current). That first call should come before any stream capture.
 //   - The call is asynchronous on `stream` and allocates nothing: no cudaMalloc, cudaFree, host-pinned
@@ -114,8 +118,8 @@ extern "C" emugemm_status_t emugemm_sgemm_bf16x3_noalloc(int M, int N, long K, c
     uint16_t* a_lo = a_hi + (size_t)Mp * Kp;
     uint16_t* b_hi = a_lo + (size_t)Mp * Kp;
     uint16_t* b_lo = b_hi + (size_t)Np * Kp;
+    // sticky until emugemm_noalloc_sync reads it (zero when the module is loaded)
     unsigned* status = reinterpret_cast<unsigned*>(base + kNoAllocScratchBytes);
-    if (cudaMemsetAsync(status, 0, sizeof(unsigned), st) != cudaSuccess) return EMUGEMM_STATUS_INTERNAL_ERROR;
     int e = launch_split_rows(A, M, K, K, (int)Mp, Kp, KP, 0, nullptr, a_hi, a_lo, stream);
     if (!e) e = launch_split_cols(B, K, N, N, (int)Np, Kp, KP, 0, nullptr, b_hi, b_lo, stream);
     if (e) return EMUGEMM_STATUS_INTERNAL_ERROR;
@@ -130,4 +134,27 @@ extern "C" emugemm_status_t emugemm_sgemm_bf16x3_noalloc(int M, int N, long K, c
     e = launch_tc_gemm(t, stream);
     if (e == (int)cudaErrorInvalidValue) return EMUGEMM_STATUS_INVALID_VALUE;
     return e ? EMUGEMM_STATUS_INTERNAL_ERROR : EMUGEMM_STATUS_SUCCESS;
+}
+
+extern "C" emugemm_status_t emugemm_noalloc_sync(void* stream) {
+    using namespace emu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return EMUGEMM_STATUS_INTERNAL_ERROR;
+    const cudaError_t se = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    unsigned char* base = nullptr;
+    int sms = 0;
+    if (scratch_for_device(dev, &base, &sms) != cudaSuccess) return EMUGEMM_STATUS_INTERNAL_ERROR;
+    unsigned* status = reinterpret_cast<unsigned*>(base + kNoAllocScratchBytes);
+    unsigned word = 0;
+    // synchronous copies of one word between the static array and a host variable: nothing is allocated
+    if (cudaMemcpy(&word, status, sizeof word, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return EMUGEMM_STATUS_INTERNAL_ERROR;
+    if (word) {
+        const unsigned zero = 0;
+        if (cudaMemcpy(status, &zero, sizeof zero, cudaMemcpyHostToDevice) != cudaSuccess)
+            return EMUGEMM_STATUS_INTERNAL_ERROR;
+        std::fprintf(stderr, "emugemm_sgemm_bf16x3_noalloc: a device-side wait timed out (flags 0x%x)\n", word);
+        return EMUGEMM_STATUS_TIMEOUT;
+    }
+    return se == cudaSuccess ? EMUGEMM_STATUS_SUCCESS : EMUGEMM_STATUS_INTERNAL_ERROR;
 }

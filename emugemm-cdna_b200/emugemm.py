@@ -20,6 +20,10 @@ HEADER = HERE.parent / "include" / "emugemm.h"
 AUTO, NATIVE_FP32, FP32_CHUNKED, BF16X3, FP16X3, BF16X6 = range(6)
 SCHEME_NAMES = ["AUTO", "NATIVE_FP32", "FP32_CHUNKED", "BF16X3", "FP16X3", "BF16X6"]
 
+# emugemm_attr_t: per-handle kernel choices
+ATTR_TC_KERNEL, ATTR_TC_SPLITK, ATTR_FP32_TILE = 0, 1, 2
+TC_KERNEL_CODES = {"auto": 0, "single": 1, "pair": 2, "fused": 3, "fusea": 4}
+
 STATUS = {
     0: "SUCCESS", 1: "INVALID_HANDLE", 2: "NOT_IMPLEMENTED", 3: "INVALID_POINTER", 4: "INVALID_SIZE",
     5: "MEMORY_ERROR", 6: "INTERNAL_ERROR", 11: "INVALID_VALUE", 100: "ARCH_MISMATCH", 101: "TIMEOUT",
@@ -101,6 +105,12 @@ _SIGS = {
     "emugemm_split_bf16": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     "emugemm_split_f16": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     "emugemm_fp32_groups": (c_int, [c_int, c_int, c_long, c_int, c_int]),
+    "emugemm_fp32_groups_tile": (c_int, [c_int, c_int, c_long, c_int, c_int, c_int]),
+    "emugemm_set_attr": (c_int, [c_void_p, c_int, c_long]),
+    "emugemm_get_attr": (c_int, [c_void_p, c_int, P(c_long)]),
+    "emugemm_test_stall_next_launches": (None, [c_int]),
+    "emugemm_sgemm_bf16x3_noalloc": (c_int, [c_int, c_int, c_long, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "emugemm_noalloc_sync": (c_int, [c_void_p]),
     "emugemm_kernel_launch_count": (ctypes.c_ulonglong, []),
     "emugemm_profile_begin": (c_int, [c_void_p]),
     "emugemm_profile_end": (c_int, [c_void_p, P(c_double), P(c_int), c_int]),
@@ -171,6 +181,8 @@ class Handle:
         self.h = h
         if stream is not None:
             self.set_stream(stream)
+        # kernel choices as created (from the environment), restored by reset_kernels()
+        self._kernel_defaults = tuple(self.get_attr(a) for a in (ATTR_TC_KERNEL, ATTR_TC_SPLITK, ATTR_FP32_TILE))
 
     def set_stream(self, stream) -> None:
         s = stream if isinstance(stream, int) else int(getattr(stream, "cuda_stream", 0))
@@ -198,6 +210,33 @@ class Handle:
 
     def sync(self) -> None:
         check("emugemm_sync", lib().emugemm_sync(self.h))
+
+    def sync_status(self) -> int:
+        """emugemm_sync's status code (0 = SUCCESS, 101 = TIMEOUT, ...), without raising."""
+        return int(lib().emugemm_sync(self.h))
+
+    def set_attr(self, attr: int, value: int) -> None:
+        check("emugemm_set_attr", lib().emugemm_set_attr(self.h, attr, value))
+
+    def get_attr(self, attr: int) -> int:
+        v = c_long()
+        check("emugemm_get_attr", lib().emugemm_get_attr(self.h, attr, ctypes.byref(v)))
+        return v.value
+
+    def reset_kernels(self) -> None:
+        """Restore the kernel choices the handle was created with."""
+        for a, v in zip((ATTR_TC_KERNEL, ATTR_TC_SPLITK, ATTR_FP32_TILE), self._kernel_defaults):
+            self.set_attr(a, v)
+
+    def set_kernels(self, tc_kernel: str | int | None = None, splitk: int | None = None,
+                    fp32_tile: int | None = None) -> None:
+        """Per-handle kernel choices (emugemm_set_attr); a name of TC_KERNEL_CODES or a code; 0 = automatic."""
+        if tc_kernel is not None:
+            self.set_attr(ATTR_TC_KERNEL, TC_KERNEL_CODES[tc_kernel] if isinstance(tc_kernel, str) else tc_kernel)
+        if splitk is not None:
+            self.set_attr(ATTR_TC_SPLITK, splitk)
+        if fp32_tile is not None:
+            self.set_attr(ATTR_FP32_TILE, fp32_tile)
 
     def sgemm(self, M: int, N: int, K: int, A, B, C, max_rel_err: float = 1e-5, force: int = AUTO,
               hints: EmuHints | None = None, use_hints: bool = True) -> tuple[EmuPlan, EmuHints | None]:
@@ -283,5 +322,15 @@ def launch_count() -> int:
     return int(lib().emugemm_kernel_launch_count())
 
 
-def fp32_groups(M: int, N: int, K: int, chunks: int, num_sms: int) -> int:
-    return int(lib().emugemm_fp32_groups(M, N, K, chunks, num_sms))
+def fp32_groups(M: int, N: int, K: int, chunks: int, num_sms: int, tile: int | None = None) -> int:
+    """FP64 partial groups of the FP32_CHUNKED kernel; tile = the handle's EMUGEMM_ATTR_FP32_TILE (None: the
+    environment default)."""
+    if tile is None:
+        return int(lib().emugemm_fp32_groups(M, N, K, chunks, num_sms))
+    return int(lib().emugemm_fp32_groups_tile(M, N, K, chunks, num_sms, tile))
+
+
+def test_stall_next_launches(n: int) -> None:
+    """Testing hook: the next n single-CTA tensor-core launches give up a 1 ms wait on a barrier nothing arrives
+    on (emugemm_test_stall_next_launches)."""
+    lib().emugemm_test_stall_next_launches(n)

@@ -102,9 +102,9 @@ def tune_shape(h, M, N, K, dtype, reps):
         kernels = (((1, "single"), (2, "pair"), (3, "fused"), (4, "fusea")) if dtype == "bf16"
                    else ((1, "single"), (2, "pair")))
         for tile, name in kernels:
-            os.environ["EMUGEMM_TC_KERNEL"] = name
+            h.set_kernels(tc_kernel=name)
             res[tile] = timed()
-        os.environ.pop("EMUGEMM_TC_KERNEL", None)
+        h.set_kernels(tc_kernel=0)
     default_ms = timed()   # the built-in choice: no table row, no override
     best = min(res, key=res.get)
     return best, res[best], default_ms

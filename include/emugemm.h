@@ -212,7 +212,8 @@ int emugemm_tune_rows(void);
 int emugemm_tune_lookup(int M, int N, long K, int dtype);
 
 /* Number of FP64 partial groups the FP32_CHUNKED kernel uses for this shape on a GPU with num_sms SMs
-   (fixes its summation order: chunk sums within a group in order, then the groups in order). */
+   (fixes its summation order: chunk sums within a group in order, then the groups in order), for a handle
+   created with the current environment (EMUGEMM_FP32_TILE read at this call). */
 int emugemm_fp32_groups(int M, int N, long K, int chunks, int num_sms);
 
 /* Per-handle kernel timing with CUDA events recorded on the handle's stream around each kernel class:
@@ -236,6 +237,39 @@ emugemm_status_t emugemm_profile_end(emugemm_handle_t handle, double* ms_by_kind
    asynchronous on `stream` (a cudaStream_t; NULL = legacy default stream), current device must be sm_100. */
 emugemm_status_t emugemm_sgemm_bf16x3_noalloc(int M, int N, long K, const float* A, const float* B, float* C,
                                               void* stream);
+/* Completion status of emugemm_sgemm_bf16x3_noalloc on the current device (no emugemm-cdna counterpart; the
+   handle path reports the same event through emugemm_sync). Synchronises `stream`, then reads and clears the
+   status word kept at the end of the static array: EMUGEMM_STATUS_TIMEOUT if a bounded device-side wait of any
+   call since the previous query gave up (that call's C is incomplete), else SUCCESS. Allocates nothing. */
+emugemm_status_t emugemm_noalloc_sync(void* stream);
+
+/* Per-handle kernel choices (no emugemm-cdna counterpart; there rocBLAS picks the kernel). Every handle starts
+   from the process environment, read when the handle is created: EMUGEMM_TC_KERNEL ("single", "pair", "fused",
+   "fusea"), EMUGEMM_TC_SPLITK (a count >= 1) and EMUGEMM_FP32_TILE (16, 32, 64, 128); unset means 0, the tile
+   table's choice and then the built-in one. A handle's setting changes only that handle's later calls. The K split
+   count changes the order of the FP64 partial sums, so two handles with different settings may differ in the last
+   bits of C; each setting on its own is deterministic. */
+typedef enum {
+    EMUGEMM_ATTR_TC_KERNEL = 0,   /* 0 auto, 1 single CTA, 2 CTA pair, 3 pair with the split fused in,
+                                     4 pair with A split into TMEM (3, 4: bf16x3 only; fp16x3 runs 2) */
+    EMUGEMM_ATTR_TC_SPLITK = 1,   /* 0 auto, n >= 1: K splits of the CTA-pair kernels */
+    EMUGEMM_ATTR_FP32_TILE = 2    /* 0 auto, 16 (16 x 32), 32, 64, 128: tile of the FP32 SIMT kernel */
+} emugemm_attr_t;
+/* INVALID_VALUE for an unknown attribute or a value outside the ranges above. */
+emugemm_status_t emugemm_set_attr(emugemm_handle_t handle, int attr, long value);
+emugemm_status_t emugemm_get_attr(emugemm_handle_t handle, int attr, long* value);
+
+/* emugemm_fp32_groups for an explicit FP32 tile code (0 = the tile table, then the built-in choice), as a handle
+   with EMUGEMM_ATTR_FP32_TILE = tile uses it. */
+int emugemm_fp32_groups_tile(int M, int N, long K, int chunks, int num_sms, int tile);
+
+/* Testing hook for failure reporting (no emugemm-cdna counterpart). The next n launches of the single-CTA
+   tensor-core kernel, from any entry point, make their MMA issuer wait before its second 128-K chunk on a
+   barrier that nothing arrives on, with a 1 ms limit; the wait gives up and the kernel unwinds as after any
+   timed-out wait (loads and MMAs in flight drained, TMEM freed, the timeout bit set in the error word), leaving
+   that launch's C incomplete. emugemm_sync (or emugemm_noalloc_sync) then returns EMUGEMM_STATUS_TIMEOUT. No
+   fault, trap or hang is involved; n = 0 cancels. */
+void emugemm_test_stall_next_launches(int n);
 
 /* Number of kernels this library launched since the process started (all handles). */
 unsigned long long emugemm_kernel_launch_count(void);

@@ -1,12 +1,15 @@
 """Shared pytest setup: the `gpu` marker, import paths for the binding and the oracle, and helpers."""
 from __future__ import annotations
 
+import os
 import pathlib
 import sys
 
 import pytest
 
 ROOT = pathlib.Path(__file__).resolve().parents[1]
+# the emugemm-cdna source tree: present where the oracle is built, absent on a GPU box (tests that read it skip)
+REF_ROOT = pathlib.Path(os.environ.get("EMUGEMM_REF_ROOT", "/root/reference"))
 for p in (ROOT / "emugemm-cdna_b200", ROOT / "oracle", ROOT / "tests"):
     if str(p) not in sys.path:
         sys.path.insert(0, str(p))
@@ -36,3 +39,11 @@ def handle(cuda):
     h = emugemm.Handle()
     yield h
     h.close()
+
+
+@pytest.fixture(autouse=True)
+def _restore_kernel_choices(request):
+    """A test that changes the session handle's kernel choices (emugemm_set_attr) leaves them as it found them."""
+    yield
+    if "handle" in request.fixturenames:
+        request.getfixturevalue("handle").reset_kernels()

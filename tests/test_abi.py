@@ -101,7 +101,9 @@ def test_reference_table_is_rejected_on_b200():
     """The reference's own gfx90a table (820 rows) must be refused wholesale for sm_100a."""
     import pathlib
 
-    ref_csv = pathlib.Path("/root/reference/data/tune_table.csv")
+    from conftest import REF_ROOT
+
+    ref_csv = REF_ROOT / "data" / "tune_table.csv"
     if not ref_csv.exists():
         pytest.skip("reference tree not present")
     lib = emugemm.lib()

@@ -114,13 +114,13 @@ def test_chunked_fp32_bitexact(cuda, handle, shape, chunks):
 @pytest.mark.parametrize("tile", [16, 32, 64, 128])
 @pytest.mark.parametrize("shape,chunks", [((256, 256, 8192), 1), ((256, 256, 8192), 4), ((100, 36, 1000), 3),
                                           ((33, 20, 260), 1), ((64, 130, 500), 2)])
-def test_fp32_tiles_bitexact(cuda, handle, monkeypatch, tile, shape, chunks):
-    """Every FP32 SIMT tile (EMUGEMM_FP32_TILE: 16 = the 16 x 32 narrow kernel, 32 / 64 / 128 square) runs the same
+def test_fp32_tiles_bitexact(cuda, handle, tile, shape, chunks):
+    """Every FP32 SIMT tile (EMUGEMM_ATTR_FP32_TILE: 16 = the 16 x 32 narrow kernel, 32 / 64 / 128 square) runs the same
     chains and FP64 folds: bit-exact against the oracle with the group split the library reports. Ragged M, N not
     a multiple of 32, chunk lengths not a multiple of 64; N = 130 is not a multiple of 4, so the narrow kernel falls
     back to the 32 tile there."""
     torch = cuda
-    monkeypatch.setenv("EMUGEMM_FP32_TILE", str(tile))
+    handle.set_kernels(fp32_tile=tile)
     M, N, K = shape
     A = datagen.uniform((M, K), 5 + K + tile)
     B = datagen.uniform((K, N), 6 + K + tile)
@@ -129,7 +129,7 @@ def test_fp32_tiles_bitexact(cuda, handle, monkeypatch, tile, shape, chunks):
     handle.partial_f64(M, N, K, dA, K, dB, N, P64, emugemm.FP32_CHUNKED, chunks)
     handle.sync()
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    G = emugemm.fp32_groups(M, N, K, chunks, sms)
+    G = emugemm.fp32_groups(M, N, K, chunks, sms, tile=tile)
     want = oracle.fp32_chunked(A, B, chunks, cpg=oracle.group_size(K, chunks, G), f64=True)
     assert np.array_equal(P64.cpu().numpy(), want)
     C, p, _ = run_sgemm(torch, handle, A, B, force=emugemm.NATIVE_FP32)
@@ -186,13 +186,13 @@ def test_bf16x3_matches_slice_products(cuda, handle, shape):
 @pytest.mark.parametrize("variant", ["single", "pair"])
 @pytest.mark.parametrize("shape", [(128, 128, 64), (200, 300, 500), (512, 256, 2048), (1, 1, 1), (64, 128, 24000),
                                    (600, 520, 4100)])
-def test_fp16x3_scaled_matches_slice_products(cuda, handle, monkeypatch, variant, shape):
+def test_fp16x3_scaled_matches_slice_products(cuda, handle, variant, shape):
     """fp16x3 on N(0,1)*2^e data (the full exponent range, so every row and column is rescaled): both tensor-core
     kernels against the exact slice products. The pair kernel scales each stage's cross products by 2^-11 inside
     the accumulator (tcgen05 scale-input-d) before adding hi*hi; the single-CTA kernel keeps two accumulators."""
     torch = cuda
     M, N, K = shape
-    monkeypatch.setenv("EMUGEMM_TC_KERNEL", variant)
+    handle.set_kernels(tc_kernel=variant)
     A = datagen.wide_range((M, K), 77)
     B = datagen.wide_range((K, N), 78)
     C, p, _ = run_sgemm(torch, handle, A, B, force=emugemm.FP16X3)
@@ -361,20 +361,20 @@ def test_a_is_reused_reuses_the_split(cuda, handle):
 @pytest.mark.parametrize("force", [emugemm.BF16X3, emugemm.FP16X3])
 @pytest.mark.parametrize("shape", [(256, 256, 128), (300, 520, 1000), (1024, 768, 2048), (1, 1, 1), (2048, 2048, 512),
                                    (256, 256, 20000)])
-def test_pair_kernel_matches_single_cta_kernel(cuda, handle, monkeypatch, force, shape):
+def test_pair_kernel_matches_single_cta_kernel(cuda, handle, force, shape):
     """bf16x3: the CTA-pair kernel (cta_group::2) computes every output from the same slices and k-steps as the
     single-CTA kernel: identical bits. fp16x3: the single-CTA kernel keeps hi*hi and the cross products in two
     accumulators; the pair kernel scales the cross products by 2^-11 inside one accumulator and promotes every 64
     of K. Their sums round differently, so both kernels must sit within the accumulation bound of the exact slice
     products. K is not split (the split-K form sums FP64 partials and is tested on its own)."""
     torch = cuda
-    monkeypatch.setenv("EMUGEMM_TC_SPLITK", "1")
+    handle.set_kernels(splitk=1)
     M, N, K = shape
     A = datagen.normal((M, K), 60 + M)
     B = datagen.normal((K, N), 61 + N)
     out = {}
     for variant in ("single", "pair"):
-        monkeypatch.setenv("EMUGEMM_TC_KERNEL", variant)
+        handle.set_kernels(tc_kernel=variant)
         C, p, _ = run_sgemm(torch, handle, A, B, force=force, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
         out[variant] = C
     assert np.isfinite(out["pair"]).all()
@@ -391,22 +391,22 @@ def test_pair_kernel_matches_single_cta_kernel(cuda, handle, monkeypatch, force,
 @pytest.mark.parametrize("force", [emugemm.BF16X3, emugemm.FP16X3])
 @pytest.mark.parametrize("shape,splits", [((256, 256, 20000), None), ((256, 256, 20000), 7), ((300, 260, 9000), None),
                                           ((200, 520, 4100), 3), ((64, 96, 40000), None)])
-def test_pair_kernel_split_k(cuda, handle, monkeypatch, force, shape, splits):
+def test_pair_kernel_split_k(cuda, handle, force, shape, splits):
     """Few 256 x 256 pair tiles and a long K: each tile's K range is split over SM pairs (None: the built-in count;
-    else EMUGEMM_TC_SPLITK), every split writes an FP64 partial and the partials are summed in order. The result
+    else EMUGEMM_ATTR_TC_SPLITK), every split writes an FP64 partial and the partials are summed in order. The result
     sits within the accumulation bound of the exact slice products, within 1e-6 of the unsplit kernel's (relative
     to ||AB||), and is deterministic; the FP64 partial entry point gives the same sum before its final rounding."""
     torch = cuda
     M, N, K = shape
     A = datagen.normal((M, K), 90 + M)
     B = datagen.normal((K, N), 91 + N)
-    monkeypatch.setenv("EMUGEMM_TC_KERNEL", "pair")
-    monkeypatch.setenv("EMUGEMM_TC_SPLITK", "1")
+    handle.set_kernels(tc_kernel="pair")
+    handle.set_kernels(splitk=1)
     C1, _, _ = run_sgemm(torch, handle, A, B, force=force, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
     if splits is None:
-        monkeypatch.delenv("EMUGEMM_TC_SPLITK")
+        handle.set_kernels(splitk=0)
     else:
-        monkeypatch.setenv("EMUGEMM_TC_SPLITK", str(splits))
+        handle.set_kernels(splitk=splits)
     Cs, _, _ = run_sgemm(torch, handle, A, B, force=force, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
     Cs2, _, _ = run_sgemm(torch, handle, A, B, force=force, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
     dA, dB = dev(torch, A), dev(torch, B)
@@ -427,13 +427,13 @@ def test_pair_kernel_split_k(cuda, handle, monkeypatch, force, shape, splits):
 @pytest.mark.parametrize("shape", [(256, 256, 128), (260, 516, 1004), (1024, 768, 2048), (2048, 2048, 512),
                                    (384, 264, 96), (1, 1, 1), (33, 65, 129), (260, 500, 20000)])
 @pytest.mark.parametrize("gen", ["normal", "wide_range"])
-def test_fused_split_kernel_matches_presplit(cuda, handle, monkeypatch, variant, shape, gen):
+def test_fused_split_kernel_matches_presplit(cuda, handle, variant, shape, gen):
     """bf16x3 with the split fused into the CTA-pair GEMM uses the same slices, k-steps and promotion points as
     the pre-split kernels: identical bits. `fused`: FP32 tiles of A and B by TMA, hi/lo made in shared memory;
     `fusea`: A's hi/lo made in the kernel and written into TMEM, B pre-split. Leading dimensions TMA cannot address
     (not a multiple of 4 floats) fall back to the pre-split path. The pair kernel runs without K splits."""
     torch = cuda
-    monkeypatch.setenv("EMUGEMM_TC_SPLITK", "1")
+    handle.set_kernels(splitk=1)
     M, N, K = shape
     if gen == "normal":
         A = datagen.normal((M, K), 70 + M)
@@ -443,7 +443,7 @@ def test_fused_split_kernel_matches_presplit(cuda, handle, monkeypatch, variant,
         B = datagen.wide_range((K, N), 73 + N, emax=20)
     out, splits = {}, {}
     for v in ("pair", variant):
-        monkeypatch.setenv("EMUGEMM_TC_KERNEL", v)
+        handle.set_kernels(tc_kernel=v)
         handle.profile_begin()
         C, p, _ = run_sgemm(torch, handle, A, B, force=emugemm.BF16X3, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
         splits[v] = handle.profile_end()["split"][1]
@@ -459,19 +459,19 @@ def test_fused_split_kernel_matches_presplit(cuda, handle, monkeypatch, variant,
 
 @pytest.mark.parametrize("splits", [None, 5])
 @pytest.mark.parametrize("shape", [(256, 256, 40000), (260, 500, 20000), (300, 264, 9000)])
-def test_fused_split_k_matches_pair(cuda, handle, monkeypatch, splits, shape):
+def test_fused_split_k_matches_pair(cuda, handle, splits, shape):
     """Split-K in the fused kernel (FP32 tiles split in the kernel) and in the pre-split pair kernel: both split K on
     the same 128-K chunk boundaries and promote at the same points, so C is bit-identical; it also sits within the
-    accumulation bound of the exact slice products (None: the built-in split count, else EMUGEMM_TC_SPLITK)."""
+    accumulation bound of the exact slice products (None: the built-in split count, else EMUGEMM_ATTR_TC_SPLITK)."""
     torch = cuda
     if splits is not None:
-        monkeypatch.setenv("EMUGEMM_TC_SPLITK", str(splits))
+        handle.set_kernels(splitk=splits)
     M, N, K = shape
     A = datagen.normal((M, K), 95 + M)
     B = datagen.normal((K, N), 96 + N)
     out = {}
     for v in ("pair", "fused"):
-        monkeypatch.setenv("EMUGEMM_TC_KERNEL", v)
+        handle.set_kernels(tc_kernel=v)
         out[v], _, _ = run_sgemm(torch, handle, A, B, force=emugemm.BF16X3, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
     assert np.isfinite(out["fused"]).all()
     assert np.array_equal(out["fused"], out["pair"])
@@ -481,16 +481,16 @@ def test_fused_split_k_matches_pair(cuda, handle, monkeypatch, splits, shape):
 
 
 @pytest.mark.parametrize("variant", ["fused", "fusea"])
-def test_fused_split_kernel_partial_f64(cuda, handle, monkeypatch, variant):
+def test_fused_split_kernel_partial_f64(cuda, handle, variant):
     """The FP64 partial output of the fused kernels (K-split building block) equals the pre-split kernel's."""
     torch = cuda
-    monkeypatch.setenv("EMUGEMM_TC_SPLITK", "1")
+    handle.set_kernels(splitk=1)
     M, N, K = 300, 260, 1536
     A = dev(torch, datagen.normal((M, K), 80))
     B = dev(torch, datagen.normal((K, N), 81))
     out = {}
     for variant_ in ("pair", variant):
-        monkeypatch.setenv("EMUGEMM_TC_KERNEL", variant_)
+        handle.set_kernels(tc_kernel=variant_)
         P = torch.full((M, N), float("nan"), dtype=torch.float64, device="cuda")
         handle.partial_f64(M, N, K, A, K, B, N, P, emugemm.BF16X3, 1)
         handle.sync()
@@ -566,7 +566,7 @@ def test_log_lines(cuda):
     assert any("tensor-core kernel=single (bf16x3) M=256 N=384 K=512" in l for l in lines), lines
 
 
-def test_committed_tile_table_dispatch(cuda, handle, monkeypatch):
+def test_committed_tile_table_dispatch(cuda, handle):
     """With the measured B200 table loaded, a shape whose row names the fused-A kernel runs it (the log says so)
     and gives the pair kernel's bits; without the table the built-in choice runs."""
     import csv
@@ -581,9 +581,9 @@ def test_committed_tile_table_dispatch(cuda, handle, monkeypatch):
     assert lib.emugemm_tune_lookup(M, N, K, 1) == 0          # no table yet
     A = datagen.normal((M, K), 97)
     B = datagen.normal((K, N), 98)
-    monkeypatch.setenv("EMUGEMM_TC_KERNEL", "pair")
+    handle.set_kernels(tc_kernel="pair")
     ref, _, _ = run_sgemm(torch, handle, A, B, force=emugemm.BF16X3, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
-    monkeypatch.delenv("EMUGEMM_TC_KERNEL")
+    handle.set_kernels(tc_kernel=0)
     try:
         assert lib.emugemm_init(str(table).encode()) == 0
         assert lib.emugemm_tune_lookup(M, N, K, 1) == 4

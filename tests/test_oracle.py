@@ -163,3 +163,30 @@ def test_rescale_forms_equal_ldexpf():
     assert np.array_equal(fast.view(np.uint32), want[normal].view(np.uint32))
     assert np.array_equal(exact.view(np.uint32), want.view(np.uint32))
     assert (~normal).sum() > 1000 and (np.abs(want) < 2.0 ** -126).sum() > 100 and np.isinf(want).sum() > 100
+
+
+# The cancellation spans of the two C4 families at their benchmark size, 2048 x 2048 x 8192, in FP64 on the host
+# (about 2 s per oscillatory case, 6 s per family-2 case): rho = || |A||B| ||_F / ||AB||_F.
+C4_OSC_RHO = {1.3: (1.1, 1.35), 11.0: (25.0, 36.0), 1150.0: (2700.0, 3400.0)}       # measured 1.22, 30.2, 3022
+C4_FAM2_RHO = {1e2: (90.0, 140.0), 1e4: (9.0e3, 1.1e4), 1.1e6: (1.0e6, 1.2e6)}     # measured 114, 1.0003e4, 1.1003e6
+
+
+def _rho_f64(A, B):
+    A64, B64 = A.astype(np.float64), B.astype(np.float64)
+    return np.linalg.norm(np.abs(A64) @ np.abs(B64)) / np.linalg.norm(A64 @ B64)
+
+
+def test_oscillatory_rho_spans_1_to_3000_at_c4_size():
+    """The oscillatory family covers the cancellation span the benchmark configuration names (about 1.2 to 3000)
+    at its own size, not only at the 512^2 size its docstring quotes."""
+    rhos = {f0: _rho_f64(*datagen.oscillatory(2048, 2048, 8192, f0)) for f0 in C4_OSC_RHO}
+    for f0, (lo, hi) in C4_OSC_RHO.items():
+        assert lo < rhos[f0] < hi, (f0, rhos[f0])
+    assert rhos[1.3] < rhos[11.0] < rhos[1150.0]
+
+
+@pytest.mark.parametrize("rho", sorted(C4_FAM2_RHO))
+def test_family2_rho_at_c4_size(rho):
+    lo, hi = C4_FAM2_RHO[rho]
+    r = _rho_f64(*datagen.family2(2048, 2048, 8192, rho))
+    assert lo < r < hi, r
