@@ -114,5 +114,5 @@ def test_reference_adversarial_contract(cuda):
     r = _run([_binary("emu_adversarial"), 2048, 16384, TABLE], timeout=900)
     assert r.returncode == 0
     assert re.search(r"contract violations: 0\b", r.stdout)
-    cases = [l for l in r.stdout.splitlines() if re.search(r"\b(met|declined \(ok\)|BROKEN)\b", l)]
+    cases = [l for l in r.stdout.splitlines() if re.search(r"\s(met|declined \(ok\)|\*\* BROKEN \*\*)$", l)]
     assert len(cases) == 10
