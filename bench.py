@@ -12,12 +12,15 @@ ours:      value = emulated TFLOPS (2*M*N*K per step) with A, B resident in HBM,
 reference: the emugemm-cdna path has no CPU implementation of its GEMM (its slices go to rocBLAS on an AMD
            GPU), so this arm times the CPU restatement of that path (oracle: split + the three slice
            products, FP64 accumulation) on a bounded row sample with all host threads, rank 0 only.
-With N > 1 (torchrun) each rank computes its own 8192-row block of a (8192*N) x 8192 x 8192 product and B
-is broadcast from rank 0 with NCCL inside every step (weak scaling).
+With N > 1 (torchrun) each rank computes its own 8192-row block of a (8192*N) x 8192 x 8192 product through
+emugemm_sgemm_rows: B is broadcast from rank 0 over the library's NCCL communicator inside every step, in column
+panels whose GEMMs start as they arrive (weak scaling). After the timed region the run checks sampled rows of every
+rank's C against FP64 (`check`) and times the long-K sharded configuration, 4096 x 4096 x 1048576 with K split over
+the ranks through emugemm_sgemm_ksplit, with its own check (`ksplit`).
 Other workloads (--workload): `rows` = one S^3 product with the rows of A split over the ranks and B broadcast
-from rank 0 in column panels (strong scaling; S = 32768 is the sharded multi-GPU configuration); `ksplit` =
-S x S x --k with K split over the ranks, FP64 partial products summed by NCCL and rounded once (S = 4096,
-K = 1048576 is the long-K multi-GPU configuration); `chunked` = FP32_CHUNKED at S x S x --k with --chunks
+from rank 0 in column panels (emugemm_sgemm_rows; strong scaling; S = 32768 is the sharded multi-GPU configuration,
+iid N(0,1)); `ksplit` = S x S x --k with K split over the ranks, FP64 partial products summed by NCCL and rounded
+once (emugemm_sgemm_ksplit; S = 4096, K = 1048576 is the long-K multi-GPU configuration, iid N(0,1)); `chunked` = FP32_CHUNKED at S x S x --k with --chunks
 K-chunks (FP32 FMA chains, chunk sums in FP64; S = 256, K = 262144 is the long-K accumulation configuration),
 U[-1,1] inputs, one partial + rounding per step; `rho` = the cancellation-ratio probe (--probes Hutchinson
 vectors) on an S x S x S product, one emugemm_estimate_rho per step. `chunked` and `rho` run as independent
@@ -61,6 +64,9 @@ def parse():
     ap.add_argument("--k", type=int, default=1048576, help="K of the ksplit, chunked and longk workloads")
     ap.add_argument("--chunks", type=int, default=4, help="K-chunks of the chunked workload")
     ap.add_argument("--probes", type=int, default=64, help="probe vectors of the rho workload")
+    ap.add_argument("--nccl-ctas", type=int, default=0, help="cap on NCCL CTAs per collective (0: NCCL's choice)")
+    ap.add_argument("--no-ksplit", action="store_true", help="skip the K-split sub-record of the square workload")
+    ap.add_argument("--no-check", action="store_true", help="skip the correctness check after the timed region")
     return ap.parse_args()
 
 
@@ -212,6 +218,7 @@ def cpu_fp64_baseline(size: int, budget_s: float = 12.0) -> dict:
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle
 
+    oracle.set_num_threads(cpu_threads())
     rng = np.random.default_rng(1)
     K = N = size
     B = rng.standard_normal((K, N)).astype(np.float32)
@@ -229,6 +236,94 @@ def cpu_fp64_baseline(size: int, budget_s: float = 12.0) -> dict:
             "sample": f"{rows} rows of the {size}^3 FP64 product (A[:{rows}] @ B), {dt:.2f} s"}
 
 
+def _plan_err(M: int, N: int, K: int, scheme: int, chunks: int = 1) -> float:
+    """The predicted normwise error of a forced scheme with absmax 1 and the iid model (the hints of the timed calls)."""
+    import emugemm
+
+    if chunks > 1:
+        return float(emugemm.lib().emugemm_model_err(scheme, K, chunks))
+    return float(emugemm.plan(M, N, K, 1e-5, force=scheme, a_absmax=1.0, b_absmax=1.0, rho=0.0).predicted_err)
+
+
+def check_rows(torch, dist, A, B, C, M_glob: int, N: int, K: int, scheme: int, nrows: int = 64) -> dict:
+    """Row-sharded product: nrows evenly spaced rows of this rank's C block against A[rows] @ B in FP64 (B complete
+    on every rank); the largest error over the ranks."""
+    m = A.shape[0]
+    idx = torch.linspace(0, max(m - 1, 0), min(nrows, m), device="cuda").long()
+    R = A[idx].double() @ B.double()
+    err = ((C[idx].double() - R).norm() / R.norm()).item() if m > 0 else 0.0
+    if dist is not None:
+        t = torch.tensor([err], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        err = float(t.item())
+    pred = _plan_err(M_glob, N, K, scheme)
+    return {"max_rel_err": err, "predicted_err": pred, "ok": bool(err <= pred),
+            "how": f"{min(nrows, m)} sampled rows of every rank's C block vs FP64 A[rows] @ B, max over ranks"}
+
+
+def check_ksplit(torch, dist, h, A_loc, B_loc, C, M: int, N: int, K: int, world: int, rank: int, scheme: int,
+                 nrows: int = 32) -> dict:
+    """K-split product: nrows sampled rows of C (on rank 0) against the FP64 sum over ranks of A_loc[rows] @ B_loc."""
+    idx = torch.linspace(0, M - 1, nrows, device="cuda").long()
+    R = torch.zeros((nrows, N), dtype=torch.float64, device="cuda")
+    kl = A_loc.shape[1]
+    for k0 in range(0, kl, 65536):          # in K pieces, so no FP64 copy of all of B_loc is held
+        k1 = min(kl, k0 + 65536)
+        R += A_loc[idx, k0:k1].double() @ B_loc[k0:k1].double()
+    if dist is not None:
+        dist.all_reduce(R)
+    err = ((C[idx].double() - R).norm() / R.norm()).item() if rank == 0 else 0.0
+    if dist is not None:
+        t = torch.tensor([err], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        err = float(t.item())
+    pred = _plan_err(M, N, K, scheme, chunks=world)
+    return {"max_rel_err": err, "predicted_err": pred, "ok": bool(err <= pred),
+            "how": f"{nrows} sampled rows of C vs the FP64 product of those rows, model error with {world} FP64 chunks"}
+
+
+def ksplit_record(torch, dist, h, args, world: int, rank: int, scheme: int, gen) -> dict:
+    """The long-K sharded configuration in the same run: M = N = 4096, K = args.k (1048576) split over the ranks,
+    iid N(0,1), emugemm_sgemm_ksplit (FP64 partials summed by NCCL, one rounding on rank 0), CUDA events on every
+    rank, the max over ranks; then its correctness check."""
+    M = N = 4096
+    K = args.k
+    k0, k1 = h.comm_krange(K)
+    kl = k1 - k0
+    A = torch.randn((M, kl), device="cuda", generator=gen)
+    B = torch.randn((kl, N), device="cuda", generator=gen)
+    C = torch.empty((M, N), device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step():
+        h.sgemm_ksplit(M, N, K, A, kl, B, N, C, N, root=0, scheme=scheme)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    steps = 5
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    chk = check_ksplit(torch, dist, h, A, B, C, M, N, K, world, rank, scheme)
+    del A, B, C
+    torch.cuda.empty_cache()
+    return {"workload": f"{M}x{N}x{K} bf16x3, K split over {world} GPU(s), FP64 partials summed by NCCL (strong)",
+            "value": 2.0 * M * N * K / (ms * 1e-3) / 1e12, "unit": "TFLOPS", "ms_per_step": ms, "steps": steps,
+            "warmup": 2, "data": "synthetic iid N(0,1)", "check": chk}
+
+
 def reference_arm(args) -> None:
     import numpy as np
 
@@ -238,6 +333,8 @@ def reference_arm(args) -> None:
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle
 
+    # a launcher such as torchrun sets OMP_NUM_THREADS=1 for every rank: use the cores this process may run on
+    oracle.set_num_threads(cpu_threads())
     size = args.size
     rng = np.random.default_rng(2)
     K = N = size
@@ -310,6 +407,11 @@ def ours(args) -> None:
     h = emugemm.Handle(stream=stream.cuda_stream)
     hints = lambda: emugemm.EmuHints(1.0, 1.0, 0, 0.0, 0)  # noqa: E731  (forced scheme: no scans, no rho)
     wl = args.workload
+    # the library's NCCL communicator (its row-sharded and K-split entry points); one rank without torchrun
+    if dist is not None:
+        multigpu.init_comm(h, max_ctas=args.nccl_ctas)
+    elif wl == "ksplit" or (wl == "square" and not args.no_ksplit):
+        h.comm_init(1, 0, emugemm.comm_unique_id(), args.nccl_ctas)
 
     if wl == "square":
         # M = N = K = S per GPU; with N GPUs each rank owns S rows of an (S*N) x S x S product (weak scaling)
@@ -324,8 +426,10 @@ def ours(args) -> None:
                                                                   if world > 1 else "")
         if dist is not None:
             def step():
-                # this rank's row block; B arrives from rank 0 in two column panels, each GEMM starting on arrival
-                multigpu.row_sharded(A, B, C, src=0, panel=(N + 1) // 2, handle=h, scheme=scheme)
+                # this rank's row block (emugemm_sgemm_rows): B arrives from rank 0 in column panels, each panel's GEMM
+                # starting on arrival
+                h.sgemm_rows(M * world, N, K, A, K, B if rank == 0 else None, N, C, N, root=0, force=scheme,
+                             hints=hints())
         else:
             def step():
                 h.sgemm(M, N, K, A, B, C, force=scheme, hints=hints())
@@ -334,19 +438,16 @@ def ours(args) -> None:
         M, N, K = S, S, S
         r0, r1 = multigpu.row_range(M, rank, world)
         m_loc, k_loc = r1 - r0, K
-        A = wide((m_loc, K))
-        B = wide((K, N)) if rank == 0 else torch.empty((K, N), device="cuda")
+        A = torch.randn((m_loc, K), device="cuda", generator=gen)          # the sharded configuration: iid N(0,1)
+        B = torch.randn((K, N), device="cuda", generator=gen) if rank == 0 else torch.empty((K, N), device="cuda")
         C = torch.empty((m_loc, N), device="cuda")
         total_flop = 2.0 * M * N * K
         scaling = "strong"
         desc = f"{args.scheme} emulated SGEMM {S}^3, row blocks of A over {world} GPU(s), B broadcast in panels"
-        # four column panels (multiples of 256): each panel's GEMM still runs whole waves of CTA-pair tiles, and
-        # the broadcast of panel j+1 overlaps the GEMM of panel j
-        rows_panel = ((N + 3) // 4 + 255) // 256 * 256
 
         def step():
             if dist is not None:
-                multigpu.row_sharded(A, B, C, src=0, panel=rows_panel, handle=h, scheme=scheme)
+                h.sgemm_rows(M, N, K, A, K, B if rank == 0 else None, N, C, N, root=0, force=scheme, hints=hints())
             else:
                 h.sgemm(m_loc, N, K, A, B, C, force=scheme, hints=hints())
     elif wl == "chunked":
@@ -398,21 +499,16 @@ def ours(args) -> None:
         M, N, K = S, S, args.k
         k0, k1 = multigpu.k_range(K, rank, world)
         m_loc, k_loc = M, k1 - k0
-        A = wide((M, k_loc))
-        B = wide((k_loc, N))
+        A = torch.randn((M, k_loc), device="cuda", generator=gen)          # the sharded configuration: iid N(0,1)
+        B = torch.randn((k_loc, N), device="cuda", generator=gen)
         C = torch.empty((M, N), device="cuda")
         total_flop = 2.0 * M * N * K
         scaling = "strong"
         desc = f"{args.scheme} emulated SGEMM {M}x{N}x{K}, K split over {world} GPU(s), FP64 partials reduced"
 
-        P = torch.empty((M, N), dtype=torch.float64, device="cuda")
-
         def step():
-            if dist is not None:
-                multigpu.k_split(A, B, C, M=M, N=N, handle=h, scheme=scheme, P=P)
-            else:
-                h.partial_f64(M, N, k_loc, A, k_loc, B, N, P, scheme, 1)
-                h.reduce_f64(M, N, 1, P, C)
+            # emugemm_sgemm_ksplit: FP64 partials summed by NCCL, C rounded once on rank 0
+            h.sgemm_ksplit(M, N, K, A, k_loc, B, N, C, N, root=0, scheme=scheme)
 
     for _ in range(args.warmup):
         step()
@@ -447,6 +543,20 @@ def ours(args) -> None:
         ms_total = float(t.max().item())
         dist.barrier()
     ms_step = ms_total / args.steps
+
+    # Correctness of this run's C, outside the timed region: sampled rows of every rank's C against FP64 products of
+    # the same rows, the largest normwise error over the ranks against the plan's predicted error.
+    check = None
+    if not args.no_check and wl in ("square", "rows", "ksplit"):
+        if wl == "ksplit":
+            check = check_ksplit(torch, dist, h, A, B, C, M, N, K, world, rank, scheme)
+        else:
+            if dist is not None:
+                dist.broadcast(B, src=0)
+            check = check_rows(torch, dist, A, B, C, M * (world if wl == "square" else 1), N, K, scheme)
+    ksplit_rec = None
+    if wl == "square" and not args.no_ksplit:
+        ksplit_rec = ksplit_record(torch, dist, h, args, world, rank, scheme, gen)
     value = total_flop / (ms_step * 1e-3) / 1e12
 
     # dominant kernel: the tensor-core 3-product GEMM (3 * 2 * m * n * k tensor FLOPs per rank and step), the FP32
@@ -493,20 +603,38 @@ def ours(args) -> None:
                                "gbs": 4.0 * (M * K + K * N) / (rho_ms * 1e-3) / 1e9,
                                "hbm_frac": 4.0 * (M * K + K * N) / (rho_ms * 1e-3) / 1e9 / hbm}}
 
-    # end to end: host inputs (pinned) through emugemm_sgemm_host, whose H2D of A and B and D2H of C are inside
-    # every step (B and C in column panels overlapped with the panel GEMMs)
-    # With N GPUs every rank runs emugemm_sgemm_host on its own pinned rows of A and its own pinned copy of B (the
-    # host-buffer product of its row block, no collective); the job's time is the slowest rank's.
+    # end to end: host inputs (pinned) and the host result, the copies inside every timed step.
+    # One GPU: emugemm_sgemm_host (B and C in column panels, overlapped with the panel GEMMs).
+    # N GPUs: every rank's rows of A cross PCIe to its own GPU; B crosses PCIe once, as K-row slices spread over the
+    # ranks, and reaches every GPU through an NCCL all-gather over NVLink (under the copy of A); each rank then runs
+    # emugemm_sgemm on its rows and its C rows go back over PCIe. The job's time is the slowest rank's.
     e2e = None
-    if not args.no_e2e and wl == "square":
-        if dist is not None:
-            dist.broadcast(B, src=0)
+    if not args.no_e2e and wl == "square" and (dist is None or K % world == 0):
         hA = A.cpu().pin_memory()
-        hB = B.cpu().pin_memory()
         hC = torch.empty((M, N), dtype=torch.float32).pin_memory()
+        if dist is None:
+            hB = B.cpu().pin_memory()
+            h2d = hA.numel() * 4 + hB.numel() * 4
 
-        def e2e_step():
-            h.sgemm_host(M, N, K, hA, hB, hC, force=scheme, hints=hints())
+            def e2e_step():
+                h.sgemm_host(M, N, K, hA, hB, hC, force=scheme, hints=hints())
+            path = "emugemm_sgemm_host: pinned host A and B in, C out, inside every step"
+        else:
+            ks = K // world
+            hBs = B[rank * ks:(rank + 1) * ks].cpu().pin_memory()      # B is complete on every rank after the check
+            dA, dBs = torch.empty_like(A), torch.empty((ks, N), device="cuda")
+            dB, dC = torch.empty((K, N), device="cuda"), torch.empty((M, N), device="cuda")
+            h2d = (hA.numel() + hBs.numel()) * 4 * world
+
+            def e2e_step():
+                dBs.copy_(hBs, non_blocking=True)
+                w = dist.all_gather_into_tensor(dB, dBs, async_op=True)
+                dA.copy_(hA, non_blocking=True)
+                w.wait()
+                h.sgemm(M, N, K, dA, dB, dC, force=scheme, hints=hints())
+                hC.copy_(dC, non_blocking=True)
+            path = ("per rank: pinned host rows of A in, B in once as K-row slices over the ranks + NCCL all-gather, "
+                    "emugemm_sgemm on the rows, C rows out; inside every step")
 
         for _ in range(2):
             e2e_step()
@@ -527,9 +655,8 @@ def ours(args) -> None:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e_ms = float(t.item())
         e2e = {"value": 2.0 * M * N * K * world / (e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
-               "h2d_bytes_per_step": int(hA.numel() * 4 + hB.numel() * 4) * world,
-               "d2h_bytes_per_step": int(hC.numel() * 4) * world, "ms_per_step": e_ms,
-               "path": "emugemm_sgemm_host per rank: pinned host A rows and B in, C rows out, inside every step"}
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(hC.numel() * 4) * world, "ms_per_step": e_ms,
+               "path": path}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and wl == "square":
@@ -584,6 +711,10 @@ def ours(args) -> None:
             "clocks": clocks,
             "gpu_launches": launches,
         }
+        if check is not None:
+            line["check"] = check
+        if ksplit_rec is not None:
+            line["ksplit"] = ksplit_rec
         if rank_ms is not None:
             line["ms_per_step_by_rank"] = rank_ms
         line.update(extra)

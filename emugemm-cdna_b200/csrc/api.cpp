@@ -27,7 +27,7 @@ int launch_rho(const float* A, long lda, const float* B, long ldb, int M, int N,
 static std::atomic<unsigned long long> g_launches{0};
 void count_launch(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
-static emugemm_status_t from_cuda(int e) {
+emugemm_status_t from_cuda(int e) {
     if (e == 0) return EMUGEMM_STATUS_SUCCESS;
     if (e == (int)cudaErrorMemoryAllocation) return EMUGEMM_STATUS_MEMORY_ERROR;
     if (e == (int)cudaErrorInvalidValue) return EMUGEMM_STATUS_INVALID_VALUE;
@@ -55,19 +55,14 @@ void* ws_get(Handle* h, int slot, size_t bytes) {
     return h->ws[slot];
 }
 
-// Runs `fn` with the handle's device current and restores the caller's device afterwards.
-struct DeviceGuard {
-    int prev = -1;
-    bool ok = true;
-    explicit DeviceGuard(int dev) {
-        if (cudaGetDevice(&prev) != cudaSuccess) { ok = false; return; }
-        if (prev != dev && cudaSetDevice(dev) != cudaSuccess) ok = false;
-    }
-    ~DeviceGuard() {
-        int cur = -1;
-        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
-    }
-};
+DeviceGuard::DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) { ok = false; return; }
+    if (prev != dev && cudaSetDevice(dev) != cudaSuccess) ok = false;
+}
+DeviceGuard::~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+}
 
 static emugemm_status_t take_device_error(Handle* h) {
     unsigned e = *reinterpret_cast<volatile unsigned*>(h->err_host);
@@ -79,7 +74,7 @@ static emugemm_status_t take_device_error(Handle* h) {
     return EMUGEMM_STATUS_SUCCESS;
 }
 
-static emugemm_status_t sync_check(Handle* h) {
+emugemm_status_t sync_check(Handle* h) {
     cudaError_t e = cudaStreamSynchronize((cudaStream_t)h->stream);
     emugemm_status_t d = take_device_error(h);
     if (d != EMUGEMM_STATUS_SUCCESS) return d;
@@ -87,7 +82,7 @@ static emugemm_status_t sync_check(Handle* h) {
 }
 
 // max|x| of a rows x cols matrix, read back to the host (synchronises the stream).
-static emugemm_status_t absmax(Handle* h, const float* X, long rows, long cols, long ld, float* out) {
+emugemm_status_t absmax(Handle* h, const float* X, long rows, long cols, long ld, float* out) {
     float* d = (float*)ws_get(h, kWsScalar, 64);
     if (!d) return EMUGEMM_STATUS_MEMORY_ERROR;
     int e;
@@ -105,21 +100,29 @@ static emugemm_status_t absmax(Handle* h, const float* X, long rows, long cols, 
     return EMUGEMM_STATUS_SUCCESS;
 }
 
+// The two Hutchinson sums of the rho estimate (src/emugemm.cpp:185-213), read back to the host: v[0] = sum over
+// probes of ||(|A|(|B| w))||^2, v[1] = sum of ||A(B w)||^2. Returns false on failure.
+bool rho_sums(Handle* h, int M, int N, long K, const float* A, long lda, const float* B, long ldb, int P,
+              double v[2]) {
+    if (M <= 0 || N <= 0 || K <= 0) return false;
+    void* ws = ws_get(h, kWsRhoT1, rho_ws_bytes(M, N, K, P, h->num_sms));
+    double* out2 = (double*)ws_get(h, kWsRhoPart, 2 * sizeof(double));
+    if (!ws || !out2) return false;
+    {
+        ProfScope ps(h, kProfRho);
+        if (launch_rho(A, lda, B, ldb, M, N, K, P, ws, h->num_sms, out2, h->stream)) return false;
+    }
+    if (cudaMemcpyAsync(v, out2, 2 * sizeof(double), cudaMemcpyDeviceToHost, (cudaStream_t)h->stream) != cudaSuccess)
+        return false;
+    return sync_check(h) == EMUGEMM_STATUS_SUCCESS;
+}
+
 // src/emugemm.cpp:185-213. Returns < 0 on failure.
 static double estimate_rho(Handle* h, int M, int N, long K, const float* A, long lda, const float* B, long ldb,
                            int P) {
     if (P <= 0) P = 64;
-    if (M <= 0 || N <= 0 || K <= 0) return -1.0;
-    void* ws = ws_get(h, kWsRhoT1, rho_ws_bytes(M, N, K, P, h->num_sms));
-    double* out2 = (double*)ws_get(h, kWsRhoPart, 2 * sizeof(double));
-    if (!ws || !out2) return -1.0;
-    {
-        ProfScope ps(h, kProfRho);
-        if (launch_rho(A, lda, B, ldb, M, N, K, P, ws, h->num_sms, out2, h->stream)) return -1.0;
-    }
     double v[2] = {0, 0};
-    if (cudaMemcpyAsync(v, out2, sizeof v, cudaMemcpyDeviceToHost, (cudaStream_t)h->stream) != cudaSuccess) return -1.0;
-    if (sync_check(h) != EMUGEMM_STATUS_SUCCESS) return -1.0;
+    if (!rho_sums(h, M, N, K, A, lda, B, ldb, P, v)) return -1.0;
     const double num = std::sqrt(v[0] / (double)P), den = std::sqrt(v[1] / (double)P);
     if (num < 0 || !(den > 0)) return -1.0;
     return num / den;
@@ -157,7 +160,7 @@ static void prof_clear(Handle* h) {
     h->prof_n = 0;
 }
 
-static long round_up(long x, long m) { return (x + m - 1) / m * m; }
+long round_up(long x, long m) { return (x + m - 1) / m * m; }
 
 // Tensor-core kernel for a shape: 1 = single-CTA, 2 = CTA pair, 3 = CTA pair with the split fused in, 4 = CTA pair
 // with A split into TMEM in the kernel (3 and 4: bf16x3). The handle's EMUGEMM_ATTR_TC_KERNEL (default: the
@@ -204,7 +207,7 @@ static void log_plan(const char* entry, int M, int N, long K, const emu_plan_t& 
 // partial and the partials are summed in order (deterministic). Every split starts a promotion chunk, so the pre-split
 // and the fused kernel split at the same values of K and stay bit-identical. The handle's EMUGEMM_ATTR_TC_SPLITK
 // (`forced`, a count >= 1; 0 = choose) overrides the choice.
-static int tc_split_count(long Mp, long Np, long K, int num_sms, int forced) {
+int tc_split_count(long Mp, long Np, long K, int num_sms, int forced) {
     const long nck = (K + 127) / 128, tiles = (Mp / 256) * (Np / 256), pairs = num_sms / 2;   // 128-K chunks
     long want = 1;
     if (forced > 0) want = forced;
@@ -215,7 +218,7 @@ static int tc_split_count(long Mp, long Np, long K, int num_sms, int forced) {
     return (int)((nck + kpc - 1) / kpc);   // every split non-empty
 }
 
-static int tc_kernel_choice(Handle* h, int M, int N, long K, bool fp16) {
+int tc_kernel_choice(Handle* h, int M, int N, long K, bool fp16) {
     if (h->pin_tc_code) return h->pin_tc_code;
     int code = h->tc_kernel;
     if (!code) code = lookup_tile(M, N, K, fp16 ? 2 : 1).tc_variant;
@@ -243,10 +246,13 @@ static int tc_kernel_choice(Handle* h, int M, int N, long K, bool fp16) {
 
 // bf16x3 / fp16x3 through the tensor-core kernel over pre-split slices. With a_reused (hints->a_is_reused) and
 // the same A (pointer, shape, leading dimension, scheme) as the split already held in the workspace, A is not
-// split again: the caller has declared A unchanged since that call.
+// split again: the caller has declared A unchanged since that call. With a_only, only A's slices (and its fp16
+// row exponents) are made, for a caller that runs the GEMMs later with a_reused (B, C, N unused).
 static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, long lda, const float* B, long ldb,
-                               float* C, long ldc, double* C64, long ldc64, bool fp16, bool a_reused) {
+                               float* C, long ldc, double* C64, long ldc64, bool fp16, bool a_reused,
+                               bool a_only = false) {
     const int choice = tc_kernel_choice(h, M, N, K, fp16);
+    if (a_only && (choice == 3 || choice == 4)) return EMUGEMM_STATUS_SUCCESS;   // these split A in the kernel
     if (choice == 3) {
         ProfScope ps(h, kProfTcGemm);
         const int splits = h->pin_splits ? h->pin_splits
@@ -308,7 +314,8 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
     if (fp16) {
         ProfScope ps(h, kProfScan);
         if (!reuse) e = launch_row_exponents(A, M, K, lda, rexp, h->stream);
-        if (!e) e = launch_col_exponents(B, K, N, ldb, cexp, reinterpret_cast<unsigned*>(cexp + N), h->stream);
+        if (!e && !a_only)
+            e = launch_col_exponents(B, K, N, ldb, cexp, reinterpret_cast<unsigned*>(cexp + N), h->stream);
         if (e) return from_cuda(e);
     }
     {
@@ -317,10 +324,17 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
             h->a_key = Handle::ASplitKey();   // invalid until the split below has been enqueued
             e = launch_split_rows(A, M, K, lda, (int)Mp, Kp, KP, kind, rexp, a0, a1, h->stream);
         }
-        if (!e) e = launch_split_cols(B, K, N, ldb, (int)Np, Kp, KP, kind, cexp, b0, b1, h->stream);
+        if (!e && !a_only) e = launch_split_cols(B, K, N, ldb, (int)Np, Kp, KP, kind, cexp, b0, b1, h->stream);
     }
     if (e) return from_cuda(e);
     h->a_key = key;
+    if (a_only) {
+        // size the FP64 planes of the K splits now, so that no later panel grows the workspace (a reallocation
+        // synchronises the stream)
+        const int sp = !pair ? 1 : h->pin_splits ? h->pin_splits : tc_split_count(Mp, Np, K, h->num_sms, h->tc_splitk);
+        if (sp > 1 && !ws_get(h, kWsSplitK, (size_t)sp * M * N * sizeof(double))) return EMUGEMM_STATUS_MEMORY_ERROR;
+        return EMUGEMM_STATUS_SUCCESS;
+    }
     TcGemmArgs t;
     t.a_hi = a0; t.a_lo = a1; t.b_hi = b0; t.b_lo = b1;
     t.M = M; t.N = N; t.Mp = (int)Mp; t.Np = (int)Np; t.Kp = Kp; t.KP = KP;
@@ -400,9 +414,8 @@ static emugemm_status_t zero_out(Handle* h, int M, int N, float* C, long ldc, do
     return from_cuda((int)e);
 }
 
-static emugemm_status_t dispatch(Handle* h, emu_scheme_t s, int chunks, int M, int N, long K, const float* A,
-                                 long lda, const float* B, long ldb, float* C, long ldc, double* C64, long ldc64,
-                                 bool a_reused = false) {
+emugemm_status_t dispatch(Handle* h, emu_scheme_t s, int chunks, int M, int N, long K, const float* A, long lda,
+                          const float* B, long ldb, float* C, long ldc, double* C64, long ldc64, bool a_reused) {
     if (M == 0 || N == 0) return EMUGEMM_STATUS_SUCCESS;
     if (K == 0) return zero_out(h, M, N, C, ldc, C64, ldc64);
     switch (s) {
@@ -413,6 +426,18 @@ static emugemm_status_t dispatch(Handle* h, emu_scheme_t s, int chunks, int M, i
         case EMU_SCHEME_BF16X6: return run_tc(h, M, N, K, A, lda, B, ldb, C, ldc, C64, ldc64, false, a_reused);
         case EMU_SCHEME_FP16X3: return run_tc(h, M, N, K, A, lda, B, ldb, C, ldc, C64, ldc64, true, a_reused);
         default: return EMUGEMM_STATUS_NOT_IMPLEMENTED;
+    }
+}
+
+emugemm_status_t prepare_a(Handle* h, emu_scheme_t s, int M, int N, long K, const float* A, long lda) {
+    if (M == 0 || N == 0 || K == 0) return EMUGEMM_STATUS_SUCCESS;
+    switch (s) {
+        case EMU_SCHEME_BF16X3:
+        case EMU_SCHEME_BF16X6:
+            return run_tc(h, M, N, K, A, lda, nullptr, N, nullptr, N, nullptr, 0, false, false, true);
+        case EMU_SCHEME_FP16X3:
+            return run_tc(h, M, N, K, A, lda, nullptr, N, nullptr, N, nullptr, 0, true, false, true);
+        default: return EMUGEMM_STATUS_SUCCESS;   // the FP32 kernels read A as it is
     }
 }
 
@@ -462,6 +487,7 @@ emugemm_status_t emugemm_destroy_handle(emugemm_handle_t handle) {
         if (ev) cudaEventDestroy((cudaEvent_t)ev);
     if (h->copy_in) cudaStreamDestroy((cudaStream_t)h->copy_in);
     if (h->copy_out) cudaStreamDestroy((cudaStream_t)h->copy_out);
+    emu::multigpu_release(h);
     for (int i = 0; i < emu::kWsCount; ++i)
         if (h->ws[i]) cudaFree(h->ws[i]);
     emu::prof_clear(h);
@@ -502,6 +528,10 @@ emugemm_status_t emugemm_set_attr(emugemm_handle_t handle, int attr, long value)
                 return EMUGEMM_STATUS_INVALID_VALUE;
             h->fp32_tile = (int)value;
             return EMUGEMM_STATUS_SUCCESS;
+        case EMUGEMM_ATTR_ROWS_PANELS:
+            if (value < 0 || value > 16) return EMUGEMM_STATUS_INVALID_VALUE;
+            h->rows_panels = (int)value;
+            return EMUGEMM_STATUS_SUCCESS;
     }
     return EMUGEMM_STATUS_INVALID_VALUE;
 }
@@ -514,6 +544,7 @@ emugemm_status_t emugemm_get_attr(emugemm_handle_t handle, int attr, long* value
         case EMUGEMM_ATTR_TC_KERNEL: *value = h->tc_kernel; return EMUGEMM_STATUS_SUCCESS;
         case EMUGEMM_ATTR_TC_SPLITK: *value = h->tc_splitk; return EMUGEMM_STATUS_SUCCESS;
         case EMUGEMM_ATTR_FP32_TILE: *value = h->fp32_tile; return EMUGEMM_STATUS_SUCCESS;
+        case EMUGEMM_ATTR_ROWS_PANELS: *value = h->rows_panels; return EMUGEMM_STATUS_SUCCESS;
     }
     return EMUGEMM_STATUS_INVALID_VALUE;
 }

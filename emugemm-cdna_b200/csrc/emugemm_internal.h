@@ -74,6 +74,8 @@ enum WsSlot {
     kWsScalar,
     kWsHostA, kWsHostB, kWsHostC,   // device copies of the operands of emugemm_sgemm_host
     kWsSplitK,                      // FP64 partial planes of the split-K tensor-core GEMM
+    kWsCommB,                       // emugemm_sgemm_rows: B's column panels as broadcast, panel after panel
+    kWsCommP,                       // emugemm_sgemm_ksplit: the FP64 partial product and its sum over ranks
     kWsCount
 };
 
@@ -113,6 +115,9 @@ struct Handle {
     void* copy_in = nullptr;
     void* copy_out = nullptr;
     void* host_ev[2 * kMaxHostPanels + 2] = {};
+    // multi-GPU state (multigpu.cpp): NCCL communicator, its stream and events; null until emugemm_comm_init
+    void* mg = nullptr;
+    int rows_panels = 0;            // EMUGEMM_ATTR_ROWS_PANELS: 0 = modelled schedule, n = n equal panels
 };
 
 // Profiler scope: records an event before and after the launches inside it when the handle profiles.
@@ -124,6 +129,31 @@ struct ProfScope {
 
 void* ws_get(Handle* h, int slot, size_t bytes);
 void count_launch(unsigned n = 1);
+
+// ---------------------------------------------------------------------------------------------------
+// api.cpp internals shared with multigpu.cpp
+struct DeviceGuard {   // the handle's device current for the scope, the caller's restored afterwards
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev);
+    ~DeviceGuard();
+};
+emugemm_status_t from_cuda(int e);
+emugemm_status_t sync_check(Handle* h);
+emugemm_status_t absmax(Handle* h, const float* X, long rows, long cols, long ld, float* out);
+bool rho_sums(Handle* h, int M, int N, long K, const float* A, long lda, const float* B, long ldb, int P,
+              double v[2]);
+long round_up(long x, long m);
+int tc_split_count(long Mp, long Np, long K, int num_sms, int forced);
+int tc_kernel_choice(Handle* h, int M, int N, long K, bool fp16);
+// One product (or panel) with scheme s into C (FP32) or C64 (FP64); a_reused: A's slices held by the handle are valid.
+emugemm_status_t dispatch(Handle* h, emu_scheme_t s, int chunks, int M, int N, long K, const float* A, long lda,
+                          const float* B, long ldb, float* C, long ldc, double* C64, long ldc64, bool a_reused = false);
+// Make A's slices (and fp16x3 row exponents) for later dispatch calls with a_reused, sizing the B slots for panels of
+// width N; nothing for the FP32 schemes and for the kernels that split A themselves.
+emugemm_status_t prepare_a(Handle* h, emu_scheme_t s, int M, int N, long K, const float* A, long lda);
+// multigpu.cpp: releases the handle's communicator, streams and events
+void multigpu_release(Handle* h);
 
 // ---------------------------------------------------------------------------------------------------
 // Kernel launchers (return a cudaError_t as int; 0 = success).

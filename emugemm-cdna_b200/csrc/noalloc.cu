@@ -78,8 +78,6 @@ cudaError_t scratch_for_device(int dev, unsigned char** out, int* sms) {
     return cudaSuccess;
 }
 
-long round_up(long x, long m) { return (x + m - 1) / m * m; }
-
 }  // namespace
 }  // namespace emu
 

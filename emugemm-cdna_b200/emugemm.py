@@ -21,7 +21,7 @@ AUTO, NATIVE_FP32, FP32_CHUNKED, BF16X3, FP16X3, BF16X6 = range(6)
 SCHEME_NAMES = ["AUTO", "NATIVE_FP32", "FP32_CHUNKED", "BF16X3", "FP16X3", "BF16X6"]
 
 # emugemm_attr_t: per-handle kernel choices
-ATTR_TC_KERNEL, ATTR_TC_SPLITK, ATTR_FP32_TILE = 0, 1, 2
+ATTR_TC_KERNEL, ATTR_TC_SPLITK, ATTR_FP32_TILE, ATTR_ROWS_PANELS = 0, 1, 2, 3
 TC_KERNEL_CODES = {"auto": 0, "single": 1, "pair": 2, "fused": 3, "fusea": 4}
 
 STATUS = {
@@ -111,6 +111,16 @@ _SIGS = {
     "emugemm_test_stall_next_launches": (None, [c_int]),
     "emugemm_sgemm_bf16x3_noalloc": (c_int, [c_int, c_int, c_long, c_void_p, c_void_p, c_void_p, c_void_p]),
     "emugemm_noalloc_sync": (c_int, [c_void_p]),
+    "emugemm_comm_unique_id": (c_int, [c_void_p]),
+    "emugemm_comm_init": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int]),
+    "emugemm_comm_destroy": (c_int, [c_void_p]),
+    "emugemm_comm_rows": (c_int, [c_void_p, c_int, P(c_int), P(c_int)]),
+    "emugemm_comm_krange": (c_int, [c_void_p, c_long, P(c_long), P(c_long)]),
+    "emugemm_sgemm_rows": (c_int, [c_void_p, c_int, c_int, c_long, c_void_p, c_long, c_void_p, c_long, c_void_p,
+                                   c_long, c_int, P(EmuRequest), P(EmuHints), P(EmuPlan)]),
+    "emugemm_sgemm_ksplit": (c_int, [c_void_p, c_int, c_int, c_long, c_void_p, c_long, c_void_p, c_long, c_void_p,
+                                     c_long, c_int, c_int, c_int]),
+    "emugemm_rows_panels": (c_int, [c_int, c_int, c_int, c_long, c_int, c_int, c_void_p, c_void_p, c_int]),
     "emugemm_kernel_launch_count": (ctypes.c_ulonglong, []),
     "emugemm_profile_begin": (c_int, [c_void_p]),
     "emugemm_profile_end": (c_int, [c_void_p, P(c_double), P(c_int), c_int]),
@@ -285,6 +295,44 @@ class Handle:
     def estimate_rho(self, M, N, K, A, B, probes=64) -> float:
         return lib().emugemm_estimate_rho(self.h, M, N, K, _ptr(A), _ptr(B), probes)
 
+    # ---- several GPUs (one process and one handle per GPU; every call is collective) ----
+    def comm_init(self, nranks: int, rank: int, uid: bytes, max_ctas: int = 0) -> None:
+        """Join the library's NCCL communicator; uid = comm_unique_id() of one rank, shared by the caller."""
+        buf = ctypes.create_string_buffer(bytes(uid), 128)
+        check("emugemm_comm_init", lib().emugemm_comm_init(self.h, nranks, rank, buf, max_ctas))
+
+    def comm_destroy(self) -> None:
+        check("emugemm_comm_destroy", lib().emugemm_comm_destroy(self.h))
+
+    def comm_rows(self, M: int) -> tuple[int, int]:
+        """This rank's rows [r0, r1) of an M-row emugemm_sgemm_rows product."""
+        r0, n = c_int(), c_int()
+        check("emugemm_comm_rows", lib().emugemm_comm_rows(self.h, M, ctypes.byref(r0), ctypes.byref(n)))
+        return r0.value, r0.value + n.value
+
+    def comm_krange(self, K: int) -> tuple[int, int]:
+        """This rank's K range [k0, k1) of an emugemm_sgemm_ksplit product."""
+        k0, n = c_long(), c_long()
+        check("emugemm_comm_krange", lib().emugemm_comm_krange(self.h, K, ctypes.byref(k0), ctypes.byref(n)))
+        return k0.value, k0.value + n.value
+
+    def sgemm_rows(self, M, N, K, A_local, lda, B, ldb, C_local, ldc, root=0, max_rel_err=1e-5, force=AUTO,
+                   hints=None):
+        """emugemm_sgemm_rows: rows of A and C on the ranks, B (on `root`; None elsewhere) broadcast in panels."""
+        req = EmuRequest(max_rel_err, force)
+        if hints is None:
+            hints = EmuHints(-1.0, -1.0, 0, 0.0, 0)
+        p = EmuPlan()
+        check("emugemm_sgemm_rows", lib().emugemm_sgemm_rows(self.h, M, N, K, _ptr(A_local), lda, _ptr(B), ldb,
+                                                             _ptr(C_local), ldc, root, ctypes.byref(req),
+                                                             ctypes.byref(hints), ctypes.byref(p)))
+        return p, hints
+
+    def sgemm_ksplit(self, M, N, K, A_local, lda, B_local, ldb, C, ldc, root=0, scheme=BF16X3, chunks=1) -> None:
+        """emugemm_sgemm_ksplit: K split over the ranks, FP64 partials summed by NCCL, C on root (all ranks: -1)."""
+        check("emugemm_sgemm_ksplit", lib().emugemm_sgemm_ksplit(self.h, M, N, K, _ptr(A_local), lda, _ptr(B_local),
+                                                                 ldb, _ptr(C), ldc, root, scheme, chunks))
+
     PEAK_NAMES = ("tc_bf16_tflops", "tc_fp16_tflops", "tc_tf32_tflops", "ffma_tflops", "dfma_tflops", "copy_gbs")
 
     def peak_probe(self, reps: int = 7) -> dict:
@@ -328,6 +376,20 @@ def fp32_groups(M: int, N: int, K: int, chunks: int, num_sms: int, tile: int | N
     if tile is None:
         return int(lib().emugemm_fp32_groups(M, N, K, chunks, num_sms))
     return int(lib().emugemm_fp32_groups_tile(M, N, K, chunks, num_sms, tile))
+
+
+def comm_unique_id() -> bytes:
+    """128 bytes identifying a new communicator (make on one rank, pass to every rank's Handle.comm_init)."""
+    buf = ctypes.create_string_buffer(128)
+    check("emugemm_comm_unique_id", lib().emugemm_comm_unique_id(buf))
+    return buf.raw
+
+
+def rows_panels(M: int, nranks: int, N: int, K: int, num_sms: int = 148, forced: int = 0) -> list[tuple[int, int]]:
+    """The column panels [n0, n1) emugemm_sgemm_rows broadcasts B in (emugemm_rows_panels)."""
+    n0, n1 = (c_int * 16)(), (c_int * 16)()
+    n = lib().emugemm_rows_panels(M, nranks, N, K, num_sms, forced, n0, n1, 16)
+    return [(n0[i], n1[i]) for i in range(n)]
 
 
 def test_stall_next_launches(n: int) -> None:

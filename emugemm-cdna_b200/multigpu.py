@@ -1,5 +1,10 @@
-"""Multi-GPU drivers of the emulated SGEMM: one process per GPU, torch.distributed (NCCL) for the plumbing,
-libemugemm for every GEMM.
+"""Multi-GPU drivers of the emulated SGEMM: one process per GPU.
+
+The product path is the library's own C ABI (emugemm_sgemm_rows / emugemm_sgemm_ksplit over its NCCL communicator);
+init_comm() joins a handle to it, sharing the communicator id over an existing torch.distributed group.
+
+The functions below restate the same partitioning on torch.distributed with an injectable GEMM, so that the
+partitioning, panel order and FP64 reduction run on CPU (gloo) in tests:
 
 row_sharded   C = A*B with the rows of A (and C) split across ranks and B held by one rank. B travels in
               column panels: rank `src` packs B[:, n0:n1] into a contiguous panel and NCCL broadcasts it; each
@@ -19,6 +24,17 @@ from typing import Callable
 
 import torch
 import torch.distributed as dist
+
+
+def init_comm(handle, group=None, max_ctas: int = 0) -> None:
+    """Join `handle` to the library's NCCL communicator over the ranks of `group` (rank 0 makes the id, a
+    torch.distributed broadcast shares it)."""
+    import emugemm
+
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    obj = [emugemm.comm_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0, group=group)
+    handle.comm_init(world, rank, obj[0], max_ctas)
 
 
 def row_range(M: int, rank: int, world: int) -> tuple[int, int]:

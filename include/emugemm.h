@@ -253,7 +253,9 @@ typedef enum {
     EMUGEMM_ATTR_TC_KERNEL = 0,   /* 0 auto, 1 single CTA, 2 CTA pair, 3 pair with the split fused in,
                                      4 pair with A split into TMEM (3, 4: bf16x3 only; fp16x3 runs 2) */
     EMUGEMM_ATTR_TC_SPLITK = 1,   /* 0 auto, n >= 1: K splits of the CTA-pair kernels */
-    EMUGEMM_ATTR_FP32_TILE = 2    /* 0 auto, 16 (16 x 32), 32, 64, 128: tile of the FP32 SIMT kernel */
+    EMUGEMM_ATTR_FP32_TILE = 2,   /* 0 auto, 16 (16 x 32), 32, 64, 128: tile of the FP32 SIMT kernel */
+    EMUGEMM_ATTR_ROWS_PANELS = 3  /* emugemm_sgemm_rows: 0 = the modelled panel schedule, 1..16 = that many equal
+                                     column panels of B (the same value on every rank) */
 } emugemm_attr_t;
 /* INVALID_VALUE for an unknown attribute or a value outside the ranges above. */
 emugemm_status_t emugemm_set_attr(emugemm_handle_t handle, int attr, long value);
@@ -270,6 +272,47 @@ int emugemm_fp32_groups_tile(int M, int N, long K, int chunks, int num_sms, int 
    that launch's C incomplete. emugemm_sync (or emugemm_noalloc_sync) then returns EMUGEMM_STATUS_TIMEOUT. No
    fault, trap or hang is involved; n = 0 cancels. */
 void emugemm_test_stall_next_launches(int n);
+
+/* ---- several GPUs of one node: one process (and one handle) per GPU, NCCL between them ---------------------------
+   No emugemm-cdna counterpart (the reference runs on one GPU); these are the two partitioned forms of its benchmark
+   set. The library makes its own NCCL communicator and opens libnccl.so.2 at run time (the copy already loaded in
+   the process, if any). Every rank calls the same entry points in the same order with the same M, N, K, root,
+   request, hints and attributes; the calls are collective. */
+
+/* 128 bytes (an ncclUniqueId) to be made on one rank and passed to every rank's emugemm_comm_init. */
+emugemm_status_t emugemm_comm_unique_id(void* id_out);
+/* Joins the handle to a communicator of `nranks` ranks (blocks until all ranks have joined). max_ctas > 0 caps the
+   CTAs NCCL uses per collective (they share the SMs with the GEMMs); 0 = NCCL's choice. */
+emugemm_status_t emugemm_comm_init(emugemm_handle_t handle, int nranks, int rank, const void* id, int max_ctas);
+emugemm_status_t emugemm_comm_destroy(emugemm_handle_t handle);
+/* The rows of an M-row product that this rank holds in emugemm_sgemm_rows: [row0, row0 + rows), contiguous blocks in
+   rank order, the first M % nranks ranks one row longer. */
+emugemm_status_t emugemm_comm_rows(emugemm_handle_t handle, int M, int* row0, int* rows);
+/* The K range [k0, k0 + klen) this rank holds in emugemm_sgemm_ksplit: blocks of 64 values of K dealt like rows. */
+emugemm_status_t emugemm_comm_krange(emugemm_handle_t handle, long K, long* k0, long* klen);
+
+/* C = A * B (M x N x K) with the rows of A and C split over the ranks (emugemm_comm_rows) and B on `root`.
+   A_local, C_local: this rank's rows (device, lda >= K, ldc >= N). B: K x N on the root (device, ldb >= N); on the
+   other ranks a buffer that receives the root's B, or NULL. B travels in column panels over NCCL on a stream of the
+   handle, each panel's GEMM starting as soon as it has arrived; A's slices are made once, while the first panel is
+   on its way. Hints are those of emugemm_sgemm, agreed on by the ranks: a_absmax < 0 is the maximum over all row
+   blocks, b_absmax < 0 the root's scan, rho < 0 the Hutchinson estimate of the whole product (all of B first, then
+   each rank's sums over its rows added up). The plan is emugemm_plan of the whole product, the same on every rank,
+   and each rank's C rows equal emugemm_sgemm's for those rows bit for bit (BF16X3, FP16X3, NATIVE_FP32). Returns
+   INVALID_VALUE without a communicator. Asynchronous on the handle's stream, like emugemm_sgemm. */
+emugemm_status_t emugemm_sgemm_rows(emugemm_handle_t handle, int M, int N, long K, const float* A_local, long lda,
+                                    float* B, long ldb, float* C_local, long ldc, int root,
+                                    const emu_request_t* req, emu_hints_t* hints, emu_plan_t* out_plan);
+/* C = A * B with K split over the ranks (emugemm_comm_krange): A_local = A[:, k0:k0+klen] (M x klen, lda >= klen),
+   B_local = B[k0:k0+klen, :] (klen x N). Each rank computes its partial product with `scheme` (and `chunks` for
+   FP32_CHUNKED) in FP64, NCCL sums the partials in FP64, and one rounding gives C (M x N, ldc) on `root`, or on every
+   rank when root = -1. Asynchronous on the handle's stream. */
+emugemm_status_t emugemm_sgemm_ksplit(emugemm_handle_t handle, int M, int N, long K, const float* A_local, long lda,
+                                      const float* B_local, long ldb, float* C, long ldc, int root, int scheme,
+                                      int chunks);
+/* The column panels [n0[i], n1[i]) emugemm_sgemm_rows uses for this product (up to `max` of them); returns their
+   count. forced = EMUGEMM_ATTR_ROWS_PANELS. No GPU work. */
+int emugemm_rows_panels(int M, int nranks, int N, long K, int num_sms, int forced, int* n0, int* n1, int max);
 
 /* Number of kernels this library launched since the process started (all handles). */
 unsigned long long emugemm_kernel_launch_count(void);

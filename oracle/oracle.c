@@ -314,3 +314,13 @@ int orc_num_threads(void) {
     return 1;
 #endif
 }
+
+/* Threads of the calling thread's later parallel regions (a launcher such as torchrun sets OMP_NUM_THREADS=1 for
+   every rank; the CPU baseline then asks for the cores it is allowed to run on). */
+void orc_set_num_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}

@@ -180,6 +180,14 @@ def num_threads() -> int:
     return int(olib().orc_num_threads())
 
 
+def set_num_threads(n: int) -> None:
+    """OpenMP threads of the oracle's later parallel loops, for the calling thread."""
+    f = olib().orc_set_num_threads
+    f.argtypes = [_c.c_int]
+    f.restype = None
+    f(int(n))
+
+
 # ---- the reference planner (compiled from its own source) ---------------------------------------------
 class RefRequest(ctypes.Structure):
     _fields_ = [("max_rel_err", ctypes.c_double), ("force_scheme", ctypes.c_int)]

@@ -1,7 +1,13 @@
-"""The multi-GPU drivers on real GPUs with NCCL: two ranks (one process per GPU), row blocks of A with B
-broadcast from rank 0 in column panels, and the K-split with FP64 partials summed by NCCL. Checked against
-a single-GPU emugemm_sgemm of the same product (row blocks: identical bits; K-split: within the bf16x3
-model error against FP64). Skipped unless two sm_100 GPUs are visible. NVLS stays off (NCCL_NVLS_ENABLE=0)."""
+"""The multi-GPU entry points of the C ABI on real GPUs with NCCL (the library's own communicator).
+
+- One rank (runs on any single B200): emugemm_sgemm_rows with the modelled and with forced panel schedules, and
+  emugemm_sgemm_ksplit, on a one-rank communicator; rows: identical bits to emugemm_sgemm; K-split: the FP64 partial
+  rounded once, identical to emugemm_sgemm_partial_f64 + emugemm_reduce_f64.
+- Two ranks (one process per GPU; skipped unless two sm_100 GPUs are visible): each rank's C rows equal a
+  single-GPU emugemm_sgemm of the whole product bit for bit, for bf16x3 and fp16x3 and for ragged shapes whose row
+  blocks differ by one row; a measured rho (hint -1) agrees with the single-GPU estimate; the K-split sits within
+  the bf16x3 model error against FP64. NVLS stays off (NCCL_NVLS_ENABLE=0).
+"""
 from __future__ import annotations
 
 import os
@@ -10,6 +16,8 @@ import socket
 import pytest
 import torch
 import torch.multiprocessing as mp
+
+import emugemm
 
 pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -21,6 +29,48 @@ def _port():
     p = s.getsockname()[1]
     s.close()
     return p
+
+
+def test_one_rank_comm(cuda):
+    torch = cuda
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    g = torch.Generator(device="cuda").manual_seed(7)
+    M, N, K = 600, 1300, 2100
+    A = torch.randn(M, K, device="cuda", generator=g)
+    B = torch.randn(K, N, device="cuda", generator=g)
+    hints = lambda: emugemm.EmuHints(1.0, 1.0, 0, 0.0, 0)  # noqa: E731
+    with emugemm.Handle() as h:
+        h.comm_init(1, 0, emugemm.comm_unique_id())
+        assert h.comm_rows(M) == (0, M) and h.comm_krange(K) == (0, K)
+        for force in (emugemm.BF16X3, emugemm.FP16X3, emugemm.NATIVE_FP32):
+            ref = torch.full((M, N), float("nan"), device="cuda")
+            h.sgemm(M, N, K, A, B, ref, force=force, hints=hints())
+            for panels in (0, 3, 16):
+                h.set_attr(emugemm.ATTR_ROWS_PANELS, panels)
+                C = torch.full((M, N), float("nan"), device="cuda")
+                p, _ = h.sgemm_rows(M, N, K, A, K, B, N, C, N, root=0, force=force, hints=hints())
+                h.sync()
+                assert p.chosen == force
+                assert torch.equal(C, ref), (force, panels)
+        h.set_attr(emugemm.ATTR_ROWS_PANELS, 0)
+        # measured hints through the rows path: the same absmax and (one rank) the same rho as emugemm_sgemm
+        C = torch.empty((M, N), device="cuda")
+        p1, hn1 = h.sgemm_rows(M, N, K, A, K, B, N, C, N, hints=emugemm.EmuHints(-1, -1, 0, -1.0, 64))
+        p2, hn2 = h.sgemm(M, N, K, A, B, C, hints=emugemm.EmuHints(-1, -1, 0, -1.0, 64))
+        h.sync()
+        assert hn1.a_absmax == hn2.a_absmax and hn1.b_absmax == hn2.b_absmax
+        assert abs(hn1.rho - hn2.rho) <= 1e-5 * hn2.rho
+        assert p1.chosen == p2.chosen
+        # K-split with one rank: the FP64 partial rounded once
+        P = torch.empty((M, N), dtype=torch.float64, device="cuda")
+        h.partial_f64(M, N, K, A, K, B, N, P, emugemm.BF16X3, 1)
+        want = torch.empty((M, N), device="cuda")
+        h.reduce_f64(M, N, 1, P, want)
+        C = torch.full((M, N), float("nan"), device="cuda")
+        h.sgemm_ksplit(M, N, K, A, K, B, N, C, N, root=0, scheme=emugemm.BF16X3)
+        h.sync()
+        assert torch.equal(C, want)
+        h.comm_destroy()
 
 
 def _worker(rank, world, port, q):
@@ -38,36 +88,63 @@ def _worker(rank, world, port, q):
     import multigpu
 
     res = {}
-    g = torch.Generator(device="cuda").manual_seed(3)
-    M, N, K = 1024, 1536, 2048
-    A = torch.randn(M, K, device="cuda", generator=g)
-    B = torch.randn(K, N, device="cuda", generator=g)
+    hints = lambda: emugemm.EmuHints(1.0, 1.0, 0, 0.0, 0)  # noqa: E731
     with emugemm.Handle() as h:
-        ref = torch.empty(M, N, device="cuda")
-        h.sgemm(M, N, K, A, B, ref, force=emugemm.BF16X3, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
-        r0, r1 = multigpu.row_range(M, rank, world)
-        Bb = B.clone() if rank == 0 else torch.empty_like(B)
-        C_local = torch.empty(r1 - r0, N, device="cuda")
-        multigpu.row_sharded(A[r0:r1].contiguous(), Bb, C_local, src=0, panel=512, handle=h,
-                             scheme=emugemm.BF16X3)
+        multigpu.init_comm(h)
+        for case, (M, N, K, force) in enumerate([(1024, 1536, 2048, emugemm.BF16X3), (1001, 1300, 4100,
+                                                                                     emugemm.BF16X3),
+                                                (777, 2048, 3000, emugemm.FP16X3)]):
+            g = torch.Generator(device="cuda").manual_seed(3 + case)
+            A = torch.randn(M, K, device="cuda", generator=g)
+            B = torch.randn(K, N, device="cuda", generator=g)
+            ref = torch.empty(M, N, device="cuda")
+            h.sgemm(M, N, K, A, B, ref, force=force, hints=hints())
+            r0, r1 = h.comm_rows(M)
+            assert (r0, r1) == multigpu.row_range(M, rank, world)
+            Bb = B.clone() if rank == 0 else torch.full_like(B, float("nan"))
+            C_local = torch.full((r1 - r0, N), float("nan"), device="cuda")
+            for panels in (0, 5):
+                h.set_attr(emugemm.ATTR_ROWS_PANELS, panels)
+                h.sgemm_rows(M, N, K, A[r0:r1].contiguous(), K, Bb, N, C_local, N, root=0, force=force,
+                             hints=hints())
+                torch.cuda.synchronize()
+                res[f"rows_equal_{case}_{panels}"] = bool(torch.equal(C_local, ref[r0:r1]))
+            res[f"b_received_{case}"] = bool(torch.equal(Bb, B))
+        h.set_attr(emugemm.ATTR_ROWS_PANELS, 0)
+        # rho measured over both row blocks against the single-GPU estimate
+        M, N, K = 1024, 1024, 2048
+        g = torch.Generator(device="cuda").manual_seed(11)
+        A = torch.randn(M, K, device="cuda", generator=g)
+        B = torch.randn(K, N, device="cuda", generator=g)
+        rho1 = h.estimate_rho(M, N, K, A, B, 64)
+        r0, r1 = h.comm_rows(M)
+        C_local = torch.empty((r1 - r0, N), device="cuda")
+        _, hn = h.sgemm_rows(M, N, K, A[r0:r1].contiguous(), K, B if rank == 0 else None, N, C_local, N,
+                             hints=emugemm.EmuHints(-1, -1, 0, -1.0, 64))
         torch.cuda.synchronize()
-        # the panel GEMMs are column blocks of the same tensor-core kernel: identical bits
-        res["rows_equal"] = bool(torch.equal(C_local, ref[r0:r1]))
-        k0, k1 = multigpu.k_range(K, rank, world)
-        C = torch.empty(M, N, device="cuda")
-        multigpu.k_split(A[:, k0:k1].contiguous(), B[k0:k1].contiguous(), C, M=M, N=N, handle=h,
-                         scheme=emugemm.BF16X3, all_ranks=True)
+        res["rho_rel"] = abs(hn.rho - rho1) / rho1
+        # K split, C on every rank
+        M, N, K = 1024, 1536, 6000
+        g = torch.Generator(device="cuda").manual_seed(13)
+        A = torch.randn(M, K, device="cuda", generator=g)
+        B = torch.randn(K, N, device="cuda", generator=g)
+        k0, k1 = h.comm_krange(K)
+        assert (k0, k1) == multigpu.k_range(K, rank, world)
+        C = torch.full((M, N), float("nan"), device="cuda")
+        h.sgemm_ksplit(M, N, K, A[:, k0:k1].contiguous(), k1 - k0, B[k0:k1].contiguous(), N, C, N, root=-1,
+                       scheme=emugemm.BF16X3)
         torch.cuda.synchronize()
         R = A.double() @ B.double()
         res["ksplit_err"] = ((C.double() - R).norm() / R.norm()).item()
         res["pred"] = emugemm.lib().emugemm_model_err(emugemm.BF16X3, K, world)
+        h.comm_destroy()
     q.put((rank, res))
     dist.barrier()
     dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_gpu_drivers():
+def test_two_gpu_entry_points():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
@@ -82,5 +159,8 @@ def test_two_gpu_drivers():
     assert not alive
     out = dict(q.get() for _ in range(2))
     for r in (0, 1):
-        assert out[r]["rows_equal"], out
+        for k, v in out[r].items():
+            if k.startswith(("rows_equal", "b_received")):
+                assert v, (r, k, out)
+        assert out[r]["rho_rel"] < 1e-4, out
         assert out[r]["ksplit_err"] <= out[r]["pred"], out

@@ -151,3 +151,22 @@ def test_rank_leaving_makes_peer_fail_not_hang():
     assert not alive, "a rank hung after its peer left"
     res = dict(out)
     assert res.get(0, "").startswith("error"), out
+
+
+@pytest.mark.parametrize("M,world,N,K", [(16384, 2, 8192, 8192), (65536, 8, 8192, 8192), (32768, 8, 32768, 32768),
+                                         (1000, 3, 1300, 2100), (5, 2, 100, 64), (32768, 4, 32768, 8192)])
+def test_rows_panel_schedule(M, world, N, K):
+    """emugemm_rows_panels (the column panels of emugemm_sgemm_rows, computed alike on every rank): contiguous,
+    covering [0, N), whole 256-column tiles except the last, at most 16; a forced count gives equal panels."""
+    import emugemm
+
+    for forced in (0, 1, 3, 16):
+        p = emugemm.rows_panels(M, world, N, K, 148, forced)
+        assert 1 <= len(p) <= 16
+        assert p[0][0] == 0 and p[-1][1] == N
+        assert all(a[1] == b[0] for a, b in zip(p, p[1:]))
+        assert all(n0 % 256 == 0 and n1 > n0 for n0, n1 in p)
+        if forced:
+            assert len(p) == min(forced, -(-N // 256))
+    # the schedule is a function of the whole product, so every rank computes the same one
+    assert emugemm.rows_panels(M, world, N, K) == emugemm.rows_panels(M, world, N, K)
