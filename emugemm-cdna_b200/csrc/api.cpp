@@ -244,6 +244,12 @@ int tc_kernel_choice(Handle* h, int M, int N, long K, bool fp16) {
     return code;
 }
 
+// SMs the tensor-core kernels may spread over: all of them, unless a multi-GPU call leaves some to its collectives
+// (the grid only; the K split count, and with it every bit of C, follows the whole GPU).
+static int tc_grid_sms(const Handle* h) {
+    return h->tc_grid_sms > 0 && h->tc_grid_sms < h->num_sms ? h->tc_grid_sms : h->num_sms;
+}
+
 // bf16x3 / fp16x3 through the tensor-core kernel over pre-split slices. With a_reused (hints->a_is_reused) and
 // the same A (pointer, shape, leading dimension, scheme) as the split already held in the workspace, A is not
 // split again: the caller has declared A unchanged since that call. With a_only, only A's slices (and its fp16
@@ -262,7 +268,7 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
             part = (double*)ws_get(h, kWsSplitK, (size_t)splits * M * N * sizeof(double));
             if (!part) return EMUGEMM_STATUS_MEMORY_ERROR;
         }
-        const int e = launch_tc_fused(A, lda, B, ldb, M, N, K, C, ldc, C64, ldc64, h->err_dev, h->num_sms, h->stream,
+        const int e = launch_tc_fused(A, lda, B, ldb, M, N, K, C, ldc, C64, ldc64, h->err_dev, tc_grid_sms(h), h->stream,
                                       splits, part);
         if (e != (int)cudaErrorNotSupported) {
             if (e || splits <= 1) return from_cuda(e);
@@ -284,7 +290,7 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
         if (e) return from_cuda(e);
         ProfScope ps(h, kProfTcGemm);
         return from_cuda(launch_tc_fused_a(A, lda, b0, b1, M, N, (int)Np4, K, Kp4, KP4, C, ldc, C64, ldc64,
-                                           h->err_dev, h->num_sms, h->stream));
+                                           h->err_dev, tc_grid_sms(h), h->stream));
     }
     const bool pair = choice >= 2;
     const int BN = pair ? tc_pair_bn(fp16 ? 1 : 0) : tc_gemm_bn(fp16 ? 1 : 0);
@@ -342,7 +348,7 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
     t.fp16 = fp16 ? 1 : 0;
     t.row_exp = rexp; t.col_exp = cexp;
     t.err = h->err_dev;
-    t.num_sms = h->num_sms;
+    t.num_sms = tc_grid_sms(h);
     if (pair) {
         t.splits = h->pin_splits ? h->pin_splits : tc_split_count(Mp, Np, K, h->num_sms, h->tc_splitk);
         t.K = K;
@@ -532,6 +538,10 @@ emugemm_status_t emugemm_set_attr(emugemm_handle_t handle, int attr, long value)
             if (value < 0 || value > 16) return EMUGEMM_STATUS_INVALID_VALUE;
             h->rows_panels = (int)value;
             return EMUGEMM_STATUS_SUCCESS;
+        case EMUGEMM_ATTR_COMM_SMS:
+            if (value < 0 || value > 64 || (value & 1)) return EMUGEMM_STATUS_INVALID_VALUE;
+            h->comm_sms = (int)value;
+            return EMUGEMM_STATUS_SUCCESS;
     }
     return EMUGEMM_STATUS_INVALID_VALUE;
 }
@@ -545,6 +555,7 @@ emugemm_status_t emugemm_get_attr(emugemm_handle_t handle, int attr, long* value
         case EMUGEMM_ATTR_TC_SPLITK: *value = h->tc_splitk; return EMUGEMM_STATUS_SUCCESS;
         case EMUGEMM_ATTR_FP32_TILE: *value = h->fp32_tile; return EMUGEMM_STATUS_SUCCESS;
         case EMUGEMM_ATTR_ROWS_PANELS: *value = h->rows_panels; return EMUGEMM_STATUS_SUCCESS;
+        case EMUGEMM_ATTR_COMM_SMS: *value = h->comm_sms; return EMUGEMM_STATUS_SUCCESS;
     }
     return EMUGEMM_STATUS_INVALID_VALUE;
 }

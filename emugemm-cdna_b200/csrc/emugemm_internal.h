@@ -118,6 +118,8 @@ struct Handle {
     // multi-GPU state (multigpu.cpp): NCCL communicator, its stream and events; null until emugemm_comm_init
     void* mg = nullptr;
     int rows_panels = 0;            // EMUGEMM_ATTR_ROWS_PANELS: 0 = modelled schedule, n = n equal panels
+    int comm_sms = 0;               // EMUGEMM_ATTR_COMM_SMS: SMs the GEMMs of emugemm_sgemm_rows leave to NCCL
+    int tc_grid_sms = 0;            // while > 0: grid bound of the tensor-core kernels (set by emugemm_sgemm_rows)
 };
 
 // Profiler scope: records an event before and after the launches inside it when the handle profiles.

@@ -517,6 +517,7 @@ int launch_tc_fused(const float* A, long lda, const float* B, long ldb, int M, i
         cudaGetLastError();
         clusters = (num_sms > 0 ? num_sms : 148) / 2;
     }
+    if (num_sms > 0 && clusters > num_sms / 2) clusters = num_sms / 2;   // a caller that leaves SMs to other work
     if (clusters > tiles * p.splits) clusters = tiles * p.splits;
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     e = cudaLaunchKernelEx(&cfg, k_tc_fused, ta, tb, p);

@@ -459,6 +459,7 @@ int launch_pair_impl(const TcGemmArgs& a, void* stream) {
         cudaGetLastError();
         clusters = (a.num_sms > 0 ? a.num_sms : 148) / 2;
     }
+    if (a.num_sms > 0 && clusters > a.num_sms / 2) clusters = a.num_sms / 2;   // a caller that leaves SMs to other work
     if (clusters > tiles * p.splits) clusters = tiles * p.splits;
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     e = cudaLaunchKernelEx(&cfg, k_tc_gemm_pair<FP16>, tah, tal, tbh, tbl, p);

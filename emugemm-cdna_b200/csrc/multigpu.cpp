@@ -5,7 +5,7 @@
 //   emugemm_sgemm_rows    row blocks of A (and C) on the ranks, B held by one rank and broadcast in column panels on
 //                         a communication stream; the GEMM of panel j starts as soon as panel j has arrived, so the
 //                         broadcast of later panels runs under the GEMMs of earlier ones. C equals the single-GPU
-//                         emugemm_sgemm of the same rows bit for bit (same kernel and K split for every panel).
+//                         emugemm_sgemm of the whole product bit for bit (its kernel and K split in every panel).
 //   emugemm_sgemm_ksplit  K split over the ranks: every rank writes its partial product in FP64, NCCL sums the
 //                         partials in FP64, one rounding to FP32 follows.
 // NCCL is not linked: the library opens libnccl.so.2 when a communicator is first made, which resolves to the copy a
@@ -332,8 +332,9 @@ emugemm_status_t emugemm_sgemm_rows(emugemm_handle_t handle, int M, int N, long 
     }
 
     // Column panels of B (one panel when rho must be measured: the probe reads all of B at once).
-    const auto pan = want_rho ? emu::rows_panels(M, m->size, N, K, h->num_sms, 1)
-                              : emu::rows_panels(M, m->size, N, K, h->num_sms, h->rows_panels);
+    const int gemm_sms = (m->size > 1 && h->comm_sms > 0) ? h->num_sms - h->comm_sms : h->num_sms;
+    const auto pan = want_rho ? emu::rows_panels(M, m->size, N, K, gemm_sms, 1)
+                              : emu::rows_panels(M, m->size, N, K, gemm_sms, h->rows_panels);
     long wmax = 0;
     for (const auto& p : pan) wmax = std::max(wmax, p.second - p.first);
     float* stage = nullptr;
@@ -396,7 +397,9 @@ emugemm_status_t emugemm_sgemm_rows(emugemm_handle_t handle, int M, int N, long 
     if (out_plan) *out_plan = plan;
 
     // The GEMMs on the handle's stream: A's slices once, before the first panel arrives; then panel j as soon as it
-    // is there (the root reads its own B in place). Every panel runs the kernel and K split of the whole row block.
+    // is there (the root reads its own B in place). Every panel of every rank runs the tensor-core kernel and K split
+    // count chosen for the WHOLE M x N x K product, so C does not depend on the number of ranks: each rank's rows
+    // are those of the single-GPU emugemm_sgemm of the whole product, bit for bit.
     emugemm_status_t st = EMUGEMM_STATUS_SUCCESS;
     if (ml > 0 && N > 0) {
         if (K == 0) {
@@ -405,14 +408,15 @@ emugemm_status_t emugemm_sgemm_rows(emugemm_handle_t handle, int M, int N, long 
         } else {
             if (emu::is_tc(plan.chosen)) {
                 const bool fp16 = plan.chosen == EMU_SCHEME_FP16X3;
-                h->pin_tc_code = emu::tc_kernel_choice(h, ml, N, K, fp16);
-                h->pin_splits = emu::tc_split_count(emu::round_up(ml, 256), emu::round_up(N, 256), K, h->num_sms,
+                h->pin_tc_code = emu::tc_kernel_choice(h, M, N, K, fp16);
+                h->pin_splits = emu::tc_split_count(emu::round_up(M, 256), emu::round_up(N, 256), K, h->num_sms,
                                                     h->tc_splitk);
             }
             struct Unpin {
                 Handle* h;
-                ~Unpin() { h->pin_tc_code = 0; h->pin_splits = 0; }
+                ~Unpin() { h->pin_tc_code = 0; h->pin_splits = 0; h->tc_grid_sms = 0; }
             } unpin{h};
+            if (m->size > 1 && h->comm_sms > 0) h->tc_grid_sms = h->num_sms - h->comm_sms;
             st = emu::prepare_a(h, plan.chosen, ml, (int)wmax, K, A_local, lda);
             for (size_t j = 0; j < pan.size() && st == EMUGEMM_STATUS_SUCCESS; ++j) {
                 const long n0 = pan[j].first, w = pan[j].second - pan[j].first;

@@ -254,8 +254,11 @@ typedef enum {
                                      4 pair with A split into TMEM (3, 4: bf16x3 only; fp16x3 runs 2) */
     EMUGEMM_ATTR_TC_SPLITK = 1,   /* 0 auto, n >= 1: K splits of the CTA-pair kernels */
     EMUGEMM_ATTR_FP32_TILE = 2,   /* 0 auto, 16 (16 x 32), 32, 64, 128: tile of the FP32 SIMT kernel */
-    EMUGEMM_ATTR_ROWS_PANELS = 3  /* emugemm_sgemm_rows: 0 = the modelled panel schedule, 1..16 = that many equal
+    EMUGEMM_ATTR_ROWS_PANELS = 3, /* emugemm_sgemm_rows: 0 = the modelled panel schedule, 1..16 = that many equal
                                      column panels of B (the same value on every rank) */
+    EMUGEMM_ATTR_COMM_SMS = 4     /* emugemm_sgemm_rows: SMs (even, 0..64) its tensor-core GEMMs leave free for the
+                                     broadcast's NCCL kernels, so that neither waits for the other's SMs; C does
+                                     not change (only the GEMMs' grid does) */
 } emugemm_attr_t;
 /* INVALID_VALUE for an unknown attribute or a value outside the ranges above. */
 emugemm_status_t emugemm_set_attr(emugemm_handle_t handle, int attr, long value);
@@ -298,8 +301,9 @@ emugemm_status_t emugemm_comm_krange(emugemm_handle_t handle, long K, long* k0, 
    on its way. Hints are those of emugemm_sgemm, agreed on by the ranks: a_absmax < 0 is the maximum over all row
    blocks, b_absmax < 0 the root's scan, rho < 0 the Hutchinson estimate of the whole product (all of B first, then
    each rank's sums over its rows added up). The plan is emugemm_plan of the whole product, the same on every rank,
-   and each rank's C rows equal emugemm_sgemm's for those rows bit for bit (BF16X3, FP16X3, NATIVE_FP32). Returns
-   INVALID_VALUE without a communicator. Asynchronous on the handle's stream, like emugemm_sgemm. */
+   and every panel runs the tensor-core kernel and K split chosen for the whole product, so each rank's C rows equal
+   those rows of the single-GPU emugemm_sgemm of the whole product bit for bit, whatever the number of ranks (BF16X3,
+   FP16X3, NATIVE_FP32). Returns INVALID_VALUE without a communicator. Asynchronous on the handle's stream. */
 emugemm_status_t emugemm_sgemm_rows(emugemm_handle_t handle, int M, int N, long K, const float* A_local, long lda,
                                     float* B, long ldb, float* C_local, long ldc, int root,
                                     const emu_request_t* req, emu_hints_t* hints, emu_plan_t* out_plan);

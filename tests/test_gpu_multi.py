@@ -103,14 +103,16 @@ def _worker(rank, world, port, q):
             assert (r0, r1) == multigpu.row_range(M, rank, world)
             Bb = B.clone() if rank == 0 else torch.full_like(B, float("nan"))
             C_local = torch.full((r1 - r0, N), float("nan"), device="cuda")
-            for panels in (0, 5):
+            for panels, comm_sms in ((0, 0), (5, 0), (0, 8)):
                 h.set_attr(emugemm.ATTR_ROWS_PANELS, panels)
+                h.set_attr(emugemm.ATTR_COMM_SMS, comm_sms)    # a smaller GEMM grid: the same bits
                 h.sgemm_rows(M, N, K, A[r0:r1].contiguous(), K, Bb, N, C_local, N, root=0, force=force,
                              hints=hints())
                 torch.cuda.synchronize()
-                res[f"rows_equal_{case}_{panels}"] = bool(torch.equal(C_local, ref[r0:r1]))
+                res[f"rows_equal_{case}_{panels}_{comm_sms}"] = bool(torch.equal(C_local, ref[r0:r1]))
             res[f"b_received_{case}"] = bool(torch.equal(Bb, B))
         h.set_attr(emugemm.ATTR_ROWS_PANELS, 0)
+        h.set_attr(emugemm.ATTR_COMM_SMS, 0)
         # rho measured over both row blocks against the single-GPU estimate
         M, N, K = 1024, 1024, 2048
         g = torch.Generator(device="cuda").manual_seed(11)
