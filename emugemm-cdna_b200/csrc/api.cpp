@@ -265,7 +265,7 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
                                          : tc_split_count(round_up(M, 256), round_up(N, 256), K, h->num_sms, h->tc_splitk);
         double* part = nullptr;
         if (splits > 1) {
-            part = (double*)ws_get(h, kWsSplitK, (size_t)splits * M * N * sizeof(double));
+            part = (double*)ws_get(h, bank_slot(h, kWsSplitK), (size_t)splits * M * N * sizeof(double));
             if (!part) return EMUGEMM_STATUS_MEMORY_ERROR;
         }
         const int e = launch_tc_fused(A, lda, B, ldb, M, N, K, C, ldc, C64, ldc64, h->err_dev, tc_grid_sms(h), h->stream,
@@ -279,8 +279,8 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
     if (choice == 4 && (lda & 3) == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0) {
         const long Np4 = round_up(N, tc_fused_a_bn()), Kp4 = slice_kp(K), KP4 = slice_panel(Kp4);
         if (Np4 > 0x7fffffffL) return EMUGEMM_STATUS_INVALID_SIZE;
-        uint16_t* b0 = (uint16_t*)ws_get(h, kWsSplitB0, (size_t)Np4 * Kp4 * 2);
-        uint16_t* b1 = (uint16_t*)ws_get(h, kWsSplitB1, (size_t)Np4 * Kp4 * 2);
+        uint16_t* b0 = (uint16_t*)ws_get(h, bank_slot(h, kWsSplitB0), (size_t)Np4 * Kp4 * 2);
+        uint16_t* b1 = (uint16_t*)ws_get(h, bank_slot(h, kWsSplitB1), (size_t)Np4 * Kp4 * 2);
         if (!b0 || !b1) return EMUGEMM_STATUS_MEMORY_ERROR;
         int e = 0;
         {
@@ -298,14 +298,14 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
     if (Mp > 0x7fffffffL || Np > 0x7fffffffL || Kp > 0x7fffffffL) return EMUGEMM_STATUS_INVALID_SIZE;
     uint16_t* a0 = (uint16_t*)ws_get(h, kWsSplitA0, (size_t)Mp * Kp * 2);
     uint16_t* a1 = (uint16_t*)ws_get(h, kWsSplitA1, (size_t)Mp * Kp * 2);
-    uint16_t* b0 = (uint16_t*)ws_get(h, kWsSplitB0, (size_t)Np * Kp * 2);
-    uint16_t* b1 = (uint16_t*)ws_get(h, kWsSplitB1, (size_t)Np * Kp * 2);
+    uint16_t* b0 = (uint16_t*)ws_get(h, bank_slot(h, kWsSplitB0), (size_t)Np * Kp * 2);
+    uint16_t* b1 = (uint16_t*)ws_get(h, bank_slot(h, kWsSplitB1), (size_t)Np * Kp * 2);
     if (!a0 || !a1 || !b0 || !b1) return EMUGEMM_STATUS_MEMORY_ERROR;
     int* rexp = nullptr;
     int* cexp = nullptr;
     if (fp16) {
         rexp = (int*)ws_get(h, kWsScaleA, (size_t)M * 4);
-        cexp = (int*)ws_get(h, kWsScaleB, (size_t)N * 8);
+        cexp = (int*)ws_get(h, bank_slot(h, kWsScaleB), (size_t)N * 8);
         if (!rexp || !cexp) return EMUGEMM_STATUS_MEMORY_ERROR;
     }
     const int kind = fp16 ? 1 : 0;
@@ -338,7 +338,16 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
         // size the FP64 planes of the K splits now, so that no later panel grows the workspace (a reallocation
         // synchronises the stream)
         const int sp = !pair ? 1 : h->pin_splits ? h->pin_splits : tc_split_count(Mp, Np, K, h->num_sms, h->tc_splitk);
-        if (sp > 1 && !ws_get(h, kWsSplitK, (size_t)sp * M * N * sizeof(double))) return EMUGEMM_STATUS_MEMORY_ERROR;
+        for (int b = 0; b < 2; ++b) {   // both banks, for panel GEMMs on two streams
+            const int keep = h->bank;
+            h->bank = b;
+            const bool ok = ws_get(h, bank_slot(h, kWsSplitB0), (size_t)Np * Kp * 2) &&
+                            ws_get(h, bank_slot(h, kWsSplitB1), (size_t)Np * Kp * 2) &&
+                            (!fp16 || ws_get(h, bank_slot(h, kWsScaleB), (size_t)N * 8)) &&
+                            (sp <= 1 || ws_get(h, bank_slot(h, kWsSplitK), (size_t)sp * M * N * sizeof(double)));
+            h->bank = keep;
+            if (!ok) return EMUGEMM_STATUS_MEMORY_ERROR;
+        }
         return EMUGEMM_STATUS_SUCCESS;
     }
     TcGemmArgs t;
@@ -353,7 +362,7 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
         t.splits = h->pin_splits ? h->pin_splits : tc_split_count(Mp, Np, K, h->num_sms, h->tc_splitk);
         t.K = K;
         if (t.splits > 1) {
-            t.part64 = (double*)ws_get(h, kWsSplitK, (size_t)t.splits * M * N * sizeof(double));
+            t.part64 = (double*)ws_get(h, bank_slot(h, kWsSplitK), (size_t)t.splits * M * N * sizeof(double));
             if (!t.part64) return EMUGEMM_STATUS_MEMORY_ERROR;
         }
     }
@@ -403,7 +412,7 @@ static emugemm_status_t run_fp32(Handle* h, int M, int N, long K, const float* A
     f.ws64 = nullptr;
     size_t wsb = fp32_gemm_ws_bytes(f);
     if (wsb) {
-        f.ws64 = (double*)ws_get(h, kWsF64Acc, wsb);
+        f.ws64 = (double*)ws_get(h, bank_slot(h, kWsF64Acc), wsb);
         if (!f.ws64) return EMUGEMM_STATUS_MEMORY_ERROR;
     }
     ProfScope ps(h, kProfFp32Gemm);

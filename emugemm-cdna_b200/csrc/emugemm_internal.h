@@ -76,6 +76,8 @@ enum WsSlot {
     kWsSplitK,                      // FP64 partial planes of the split-K tensor-core GEMM
     kWsCommB,                       // emugemm_sgemm_rows: B's column panels as broadcast, panel after panel
     kWsCommP,                       // emugemm_sgemm_ksplit: the FP64 partial product and its sum over ranks
+    // bank 1 of the per-product scratch (Handle::bank), for a second panel GEMM running beside the first
+    kWsSplitB0b, kWsSplitB1b, kWsScaleBb, kWsSplitKb, kWsF64Accb,
     kWsCount
 };
 
@@ -120,7 +122,22 @@ struct Handle {
     int rows_panels = 0;            // EMUGEMM_ATTR_ROWS_PANELS: 0 = modelled schedule, n = n equal panels
     int comm_sms = 0;               // EMUGEMM_ATTR_COMM_SMS: SMs the GEMMs of emugemm_sgemm_rows leave to NCCL
     int tc_grid_sms = 0;            // while > 0: grid bound of the tensor-core kernels (set by emugemm_sgemm_rows)
+    int bank = 0;                   // 1: the per-product B scratch comes from the bank-1 slots (two GEMMs at once)
 };
+
+// Workspace slot of the current bank: the scratch a product writes besides A's slices (B's slices and column
+// exponents, split-K planes, FP64 chunk groups) is doubled, so that two panel GEMMs can run on two streams at once.
+inline int bank_slot(const Handle* h, int slot) {
+    if (!h->bank) return slot;
+    switch (slot) {
+        case kWsSplitB0: return kWsSplitB0b;
+        case kWsSplitB1: return kWsSplitB1b;
+        case kWsScaleB: return kWsScaleBb;
+        case kWsSplitK: return kWsSplitKb;
+        case kWsF64Acc: return kWsF64Accb;
+        default: return slot;
+    }
+}
 
 // Profiler scope: records an event before and after the launches inside it when the handle profiles.
 struct ProfScope {

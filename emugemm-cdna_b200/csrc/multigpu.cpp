@@ -71,7 +71,8 @@ struct Mg {
     ncclComm_t comm = nullptr;
     int rank = 0, size = 1;
     cudaStream_t stream = nullptr;                 // broadcasts of B's panels
-    cudaEvent_t ev_start = nullptr, ev_done = nullptr;
+    cudaStream_t stream2 = nullptr;                // every other panel GEMM, beside the handle's stream
+    cudaEvent_t ev_start = nullptr, ev_done = nullptr, ev_a = nullptr, ev_join = nullptr;
     cudaEvent_t ev_panel[kMaxRowPanels] = {};
     void* small = nullptr;                         // 256 bytes: hint values agreed on by the ranks
 };
@@ -102,11 +103,13 @@ void k_range(long K, int rank, int size, long* k0, long* k1) {
 
 // Column panels of B for emugemm_sgemm_rows, in units of 256 columns (the CTA-pair tile width), chosen by a model of
 // the pipeline so that every rank computes the same schedule from (M, ranks, N, K): panel j's broadcast ends at
-// sum_{i<=j} (latency + bytes_i / bandwidth) on the communication stream; its GEMM starts when both that broadcast
-// and the GEMM of panel j-1 have ended and takes ceil(tiles_j / SM pairs) waves of one tile time plus the split of
-// the panel. A first panel that is too wide leaves the GPU idle while it crosses NVLink; narrow panels waste
-// partial waves. The model's constants are round B200 figures: 1.45 PFLOP/s of slice products over 74 SM pairs,
-// 400 GB/s broadcast bandwidth, 25 us per collective, 5 TB/s for the split, 8 us per launch pair.
+// sum_{i<=j} (latency + bytes_i / bandwidth) on the communication stream; consecutive panel GEMMs run on two
+// streams, so the CTAs of panel j+1 fill the SMs the last partial wave of panel j leaves idle, and the GPU works
+// through the panels' tiles as one queue: panel j's tiles start once it has arrived and the tiles before it are
+// done, and take tiles_j / SM pairs tile times, plus the split of the panel. A wide first panel leaves the GPU idle
+// while it crosses NVLink; every further panel costs a collective's latency. The model's constants are round B200
+// figures: 1.45 PFLOP/s of slice products over 74 SM pairs, 400 GB/s broadcast bandwidth, 25 us per collective,
+// 5 TB/s for the split, 8 us per launch pair.
 std::vector<std::pair<long, long>> rows_panels(long M, int size, long N, long K, int num_sms, int forced) {
     std::vector<std::pair<long, long>> out;
     const long nc = (N + 255) / 256;
@@ -135,8 +138,8 @@ std::vector<std::pair<long, long>> rows_panels(long M, int size, long N, long K,
             if (at(c, p) >= inf) continue;
             for (long w = 1; c + w <= nc; ++w) {
                 const double arrive = (p + 1) * lat + (double)(c + w) * col_bytes / bw;
-                const double waves = std::ceil((double)(tiles_m * w) / (double)pairs);
-                const double end = std::max(at(c, p), arrive) + launch + waves * t_tile + w * split;
+                const double work = (double)(tiles_m * w) / (double)pairs * t_tile;
+                const double end = std::max(at(c, p), arrive + launch) + work + w * split + lat * 0.2;
                 if (end < at(c + w, p + 1)) {
                     at(c + w, p + 1) = end;
                     from[(c + w) * (P + 1) + p + 1] = (int)c;
@@ -177,6 +180,9 @@ void multigpu_release(Handle* h) {
     if (m->ev_start) cudaEventDestroy(m->ev_start);
     if (m->ev_done) cudaEventDestroy(m->ev_done);
     if (m->stream) cudaStreamDestroy(m->stream);
+    if (m->stream2) cudaStreamDestroy(m->stream2);
+    if (m->ev_a) cudaEventDestroy(m->ev_a);
+    if (m->ev_join) cudaEventDestroy(m->ev_join);
     if (m->small) cudaFree(m->small);
     delete m;
     h->mg = nullptr;
@@ -214,6 +220,9 @@ emugemm_status_t emugemm_comm_init(emugemm_handle_t handle, int nranks, int rank
     m->rank = rank;
     m->size = nranks;
     bool ok = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&m->stream2, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaEventCreateWithFlags(&m->ev_a, cudaEventDisableTiming) == cudaSuccess &&
+              cudaEventCreateWithFlags(&m->ev_join, cudaEventDisableTiming) == cudaSuccess &&
               cudaEventCreateWithFlags(&m->ev_start, cudaEventDisableTiming) == cudaSuccess &&
               cudaEventCreateWithFlags(&m->ev_done, cudaEventDisableTiming) == cudaSuccess &&
               cudaMalloc(&m->small, 256) == cudaSuccess;
@@ -412,22 +421,44 @@ emugemm_status_t emugemm_sgemm_rows(emugemm_handle_t handle, int M, int N, long 
                 h->pin_splits = emu::tc_split_count(emu::round_up(M, 256), emu::round_up(N, 256), K, h->num_sms,
                                                     h->tc_splitk);
             }
-            struct Unpin {
+            struct Restore {
                 Handle* h;
-                ~Unpin() { h->pin_tc_code = 0; h->pin_splits = 0; h->tc_grid_sms = 0; }
-            } unpin{h};
+                void* stream;
+                ~Restore() {
+                    h->pin_tc_code = 0; h->pin_splits = 0; h->tc_grid_sms = 0;
+                    h->stream = stream; h->bank = 0;
+                }
+            } restore{h, h->stream};
             if (m->size > 1 && h->comm_sms > 0) h->tc_grid_sms = h->num_sms - h->comm_sms;
             st = emu::prepare_a(h, plan.chosen, ml, (int)wmax, K, A_local, lda);
+            // odd panels on the second stream with the bank-1 scratch, after A's split
+            const bool two = pan.size() > 1;
+            if (st == EMUGEMM_STATUS_SUCCESS && two) {
+                e = (int)cudaEventRecord(m->ev_a, cs);
+                if (!e) e = (int)cudaStreamWaitEvent(m->stream2, m->ev_a, 0);
+                if (e) return emu::from_cuda(e);
+            }
             for (size_t j = 0; j < pan.size() && st == EMUGEMM_STATUS_SUCCESS; ++j) {
                 const long n0 = pan[j].first, w = pan[j].second - pan[j].first;
+                const bool odd = two && (j & 1);
+                cudaStream_t ps = odd ? m->stream2 : cs;
                 if (!is_root) {
-                    e = (int)cudaStreamWaitEvent(cs, m->ev_panel[j], 0);
+                    e = (int)cudaStreamWaitEvent(ps, m->ev_panel[j], 0);
                     if (e) return emu::from_cuda(e);
                 }
                 const float* Bp = is_root ? B + n0 : stage + (size_t)K * n0;
                 const long bld = is_root ? ldb : w;
+                h->stream = ps;
+                h->bank = odd ? 1 : 0;
                 st = emu::dispatch(h, plan.chosen, plan.chunks, ml, (int)w, K, A_local, lda, Bp, bld, C_local + n0, ldc,
                                    nullptr, 0, /*a_reused*/ true);
+                h->stream = cs;
+                h->bank = 0;
+            }
+            if (two) {
+                e = (int)cudaEventRecord(m->ev_join, m->stream2);
+                if (!e) e = (int)cudaStreamWaitEvent(cs, m->ev_join, 0);
+                if (e) return emu::from_cuda(e);
             }
         }
     }
