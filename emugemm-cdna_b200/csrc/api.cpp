@@ -551,6 +551,10 @@ emugemm_status_t emugemm_set_attr(emugemm_handle_t handle, int attr, long value)
             if (value < 0 || value > 64 || (value & 1)) return EMUGEMM_STATUS_INVALID_VALUE;
             h->comm_sms = (int)value;
             return EMUGEMM_STATUS_SUCCESS;
+        case EMUGEMM_ATTR_BCAST_NCCL:
+            if (value != 0 && value != 1) return EMUGEMM_STATUS_INVALID_VALUE;
+            h->bcast_nccl = (int)value;
+            return EMUGEMM_STATUS_SUCCESS;
     }
     return EMUGEMM_STATUS_INVALID_VALUE;
 }
@@ -565,6 +569,7 @@ emugemm_status_t emugemm_get_attr(emugemm_handle_t handle, int attr, long* value
         case EMUGEMM_ATTR_FP32_TILE: *value = h->fp32_tile; return EMUGEMM_STATUS_SUCCESS;
         case EMUGEMM_ATTR_ROWS_PANELS: *value = h->rows_panels; return EMUGEMM_STATUS_SUCCESS;
         case EMUGEMM_ATTR_COMM_SMS: *value = h->comm_sms; return EMUGEMM_STATUS_SUCCESS;
+        case EMUGEMM_ATTR_BCAST_NCCL: *value = h->bcast_nccl; return EMUGEMM_STATUS_SUCCESS;
     }
     return EMUGEMM_STATUS_INVALID_VALUE;
 }

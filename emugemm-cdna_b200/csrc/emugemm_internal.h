@@ -63,6 +63,7 @@ enum : unsigned {
     kErrTimeoutEpilogue = 4u,
     kErrTimeoutConvert = 8u,
     kErrTmemAlloc = 16u,
+    kErrTimeoutComm = 32u,          // a wait for another GPU's flag in emugemm_sgemm_rows gave up
 };
 
 // Workspace slots of a handle (grow-only, freed with the handle).
@@ -123,6 +124,7 @@ struct Handle {
     int comm_sms = 0;               // EMUGEMM_ATTR_COMM_SMS: SMs the GEMMs of emugemm_sgemm_rows leave to NCCL
     int tc_grid_sms = 0;            // while > 0: grid bound of the tensor-core kernels (set by emugemm_sgemm_rows)
     int bank = 0;                   // 1: the per-product B scratch comes from the bank-1 slots (two GEMMs at once)
+    int bcast_nccl = 0;             // EMUGEMM_ATTR_BCAST_NCCL: 1 = B by NCCL broadcast, 0 = copy engines (peer memory)
 };
 
 // Workspace slot of the current bank: the scratch a product writes besides A's slices (B's slices and column

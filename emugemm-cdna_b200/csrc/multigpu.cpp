@@ -12,6 +12,18 @@
 // host framework has already loaded, if any, so that the library and its caller use one NCCL. The communicator is
 // the library's own (emugemm_comm_unique_id / emugemm_comm_init), so it never shares a stream or a sequence of
 // collectives with the caller's.
+//
+// How B travels in emugemm_sgemm_rows. The panel GEMMs are persistent kernels with one CTA on every SM; NCCL's
+// broadcast kernels need SMs of their own (about 27 GB/s per CTA measured), so they either wait for the GEMMs or take
+// SMs from them. By default B therefore moves by COPY ENGINES over NVLink peer memory, which use no SM: every rank
+// maps the staging buffers of the others (CUDA IPC, set up once per size), and the ranks form a binary tree rooted
+// at `root`; each rank pulls panel j from its parent's staging buffer into its own with one cudaMemcpyAsync as soon
+// as the parent has it, so every node sends B at most twice. Arrival and release are 32-bit sequence flags in device
+// memory: one-warp kernels set them (a system-scope release store) and wait for them (bounded polls, which co-reside
+// with the GEMM's CTAs on an SM); a wait that runs out sets the handle's timeout bit, so emugemm_sync reports it.
+// The staging buffers alternate between two per call, and a parent reuses one only after its children have
+// released it. NCCL broadcasts remain the path when the ranks cannot map each other's memory, or on request.
+#include "device_utils.cuh"
 #include "emugemm_internal.h"
 
 #include <cuda_runtime.h>
@@ -35,6 +47,7 @@ struct NcclApi {
     decltype(&ncclBroadcast) broadcast = nullptr;
     decltype(&ncclAllReduce) all_reduce = nullptr;
     decltype(&ncclReduce) reduce = nullptr;
+    decltype(&ncclAllGather) all_gather = nullptr;
     decltype(&ncclGetErrorString) error_string = nullptr;
     bool ok = false;
 };
@@ -57,9 +70,10 @@ const NcclApi* nccl() {
         a.broadcast = reinterpret_cast<decltype(a.broadcast)>(dlsym(lib, "ncclBroadcast"));
         a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(lib, "ncclAllReduce"));
         a.reduce = reinterpret_cast<decltype(a.reduce)>(dlsym(lib, "ncclReduce"));
+        a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(lib, "ncclAllGather"));
         a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(lib, "ncclGetErrorString"));
         a.ok = a.get_unique_id && a.init_rank_config && a.destroy && a.broadcast && a.all_reduce && a.reduce &&
-               a.error_string;
+               a.all_gather && a.error_string;
         if (!a.ok) std::fprintf(stderr, "emugemm: libnccl.so.2 lacks a needed entry point\n");
     });
     return g_nccl.ok ? &g_nccl : nullptr;
@@ -75,7 +89,69 @@ struct Mg {
     cudaEvent_t ev_start = nullptr, ev_done = nullptr, ev_a = nullptr, ev_join = nullptr;
     cudaEvent_t ev_panel[kMaxRowPanels] = {};
     void* small = nullptr;                         // 256 bytes: hint values agreed on by the ranks
+    // copy-engine broadcast over peer memory
+    int p2p = -1;                                  // -1 not yet tried, 0 unavailable (NCCL), 1 in use
+    unsigned seq = 0;                              // emugemm_sgemm_rows calls so far (equal on every rank)
+    size_t stage_bytes = 0;
+    float* stage[2] = {};                          // this rank's staging buffers, mapped by the others
+    unsigned* flags = nullptr;                     // [kFlagArrive + 16 b + j] arrivals, [kFlagRelease + c] releases
+    std::vector<float*> peer_stage[2];             // the other ranks' staging buffers (by rank; null for this one)
+    std::vector<unsigned*> peer_flags;
 };
+
+constexpr int kFlagArrive = 0;                     // + 16 * buffer + panel: the sequence number of the panel's call
+constexpr int kFlagRelease = 32;                   // + child slot: the last call whose panels that child has pulled
+constexpr size_t kFlagBytes = 256;
+constexpr unsigned long long kCommWaitNs = 30000000000ull;   // a peer that has not arrived within 30 s has failed
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Waits until *flag has reached `want` (sequence numbers compared modulo 2^32), at most limit_ns.
+__global__ void k_wait_flag(const unsigned* flag, unsigned want, unsigned* err, unsigned long long limit_ns) {
+    if (threadIdx.x != 0) return;
+    const unsigned long long t0 = dev::globaltimer();
+    while ((int)(ld_acquire_sys(flag) - want) < 0) {
+        if (dev::globaltimer() - t0 > limit_ns) {
+            if (err) atomicOr(err, kErrTimeoutComm);
+            return;
+        }
+        __nanosleep(200);
+    }
+}
+
+// Publishes `v` in *flag after every earlier operation of the stream (the copy it announces) has completed.
+__global__ void k_set_flag(unsigned* flag, unsigned v) {
+    if (threadIdx.x != 0) return;
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
+}
+
+int wait_flag(const unsigned* flag, unsigned want, unsigned* err, cudaStream_t st) {
+    k_wait_flag<<<1, 32, 0, st>>>(flag, want, err, kCommWaitNs);
+    count_launch();
+    return (int)cudaGetLastError();
+}
+
+int set_flag(unsigned* flag, unsigned v, cudaStream_t st) {
+    k_set_flag<<<1, 32, 0, st>>>(flag, v);
+    count_launch();
+    return (int)cudaGetLastError();
+}
+
+void p2p_close(Mg* m) {
+    for (int b = 0; b < 2; ++b) {
+        for (float*& q : m->peer_stage[b])
+            if (q) cudaIpcCloseMemHandle(q), q = nullptr;
+        if (m->stage[b]) cudaFree(m->stage[b]), m->stage[b] = nullptr;
+    }
+    for (unsigned*& q : m->peer_flags)
+        if (q) cudaIpcCloseMemHandle(q), q = nullptr;
+    m->stage_bytes = 0;
+}
 
 Mg* mg_of(Handle* h) { return static_cast<Mg*>(h->mg); }
 
@@ -163,6 +239,102 @@ std::vector<std::pair<long, long>> rows_panels(long M, int size, long N, long K,
     return out;
 }
 
+// Makes (or grows to `bytes`) the staging buffers of the copy-engine broadcast and maps every other rank's; collective:
+// every rank calls it in the same emugemm_sgemm_rows call with the same size. Sets m->p2p to 1, or to 0 when some rank
+// could not map the others' memory (all ranks then use NCCL broadcasts). On return every rank's earlier transfers of
+// the old buffers have ended.
+emugemm_status_t p2p_setup(Handle* h, Mg* m, const NcclApi* n, size_t bytes) {
+    if (m->p2p == 0 || (m->p2p == 1 && m->stage_bytes >= bytes)) return EMUGEMM_STATUS_SUCCESS;
+    cudaStream_t cs = (cudaStream_t)h->stream;
+    // every rank's device idle before any buffer is replaced: local sync, then a collective both ways
+    if (cudaDeviceSynchronize() != cudaSuccess) return EMUGEMM_STATUS_INTERNAL_ERROR;
+    struct Rec { cudaIpcMemHandle_t st[2], fl; int ok; char pad[256 - 3 * sizeof(cudaIpcMemHandle_t) - sizeof(int)]; };
+    static_assert(sizeof(Rec) == 256, "record size");
+    if (m->stage_bytes > 0) {
+        // growing: the peers may still read this rank's old buffers until they, too, have drained
+        int* d = static_cast<int*>(m->small);
+        emugemm_status_t s = from_nccl(n->all_reduce(d, d, 1, ncclInt32, ncclSum, m->comm, cs));
+        if (s == EMUGEMM_STATUS_SUCCESS) s = from_cuda((int)cudaStreamSynchronize(cs));
+        if (s != EMUGEMM_STATUS_SUCCESS) return s;
+    }
+    Rec mine{};
+    int ok = 1;
+    const int P = m->size;
+    p2p_close(m);
+    if (!m->flags) {
+        if (cudaMalloc(&m->flags, kFlagBytes) != cudaSuccess || cudaMemset(m->flags, 0, kFlagBytes) != cudaSuccess) {
+            cudaGetLastError();
+            m->flags = nullptr;
+            ok = 0;
+        }
+    }
+    for (int b = 0; b < 2 && ok; ++b) {
+        void* q = nullptr;
+        if (cudaMalloc(&q, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            ok = 0;
+            break;
+        }
+        m->stage[b] = static_cast<float*>(q);
+    }
+    if (ok)
+        ok = cudaIpcGetMemHandle(&mine.st[0], m->stage[0]) == cudaSuccess &&
+             cudaIpcGetMemHandle(&mine.st[1], m->stage[1]) == cudaSuccess &&
+             cudaIpcGetMemHandle(&mine.fl, m->flags) == cudaSuccess;
+    cudaGetLastError();
+    mine.ok = ok;
+    void* dev = nullptr;
+    if (cudaMalloc(&dev, (size_t)(P + 1) * sizeof(Rec)) != cudaSuccess) {
+        cudaGetLastError();
+        return EMUGEMM_STATUS_MEMORY_ERROR;
+    }
+    std::vector<Rec> all(P);
+    emugemm_status_t s = from_cuda((int)cudaMemcpy(dev, &mine, sizeof mine, cudaMemcpyHostToDevice));
+    if (s == EMUGEMM_STATUS_SUCCESS)
+        s = from_nccl(n->all_gather(dev, static_cast<char*>(dev) + sizeof(Rec), sizeof(Rec), ncclUint8, m->comm, cs));
+    if (s == EMUGEMM_STATUS_SUCCESS)
+        s = from_cuda((int)cudaMemcpyAsync(all.data(), static_cast<char*>(dev) + sizeof(Rec), P * sizeof(Rec),
+                                           cudaMemcpyDeviceToHost, cs));
+    if (s == EMUGEMM_STATUS_SUCCESS) s = from_cuda((int)cudaStreamSynchronize(cs));
+    if (s != EMUGEMM_STATUS_SUCCESS) {
+        cudaFree(dev);
+        return s;
+    }
+    for (int r = 0; r < P; ++r) ok = ok && all[r].ok;
+    for (int b = 0; b < 2; ++b) m->peer_stage[b].assign(P, nullptr);
+    m->peer_flags.assign(P, nullptr);
+    for (int r = 0; r < P && ok; ++r) {
+        if (r == m->rank) continue;
+        void* q[3] = {};
+        const cudaIpcMemHandle_t* hs[3] = {&all[r].st[0], &all[r].st[1], &all[r].fl};
+        for (int i = 0; i < 3 && ok; ++i)
+            if (cudaIpcOpenMemHandle(&q[i], *hs[i], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                ok = 0;
+            }
+        m->peer_stage[0][r] = static_cast<float*>(q[0]);
+        m->peer_stage[1][r] = static_cast<float*>(q[1]);
+        m->peer_flags[r] = static_cast<unsigned*>(q[2]);
+    }
+    // every rank must take the same path: the minimum of the ranks' outcomes
+    int* d = static_cast<int*>(dev);
+    s = from_cuda((int)cudaMemcpy(d, &ok, sizeof ok, cudaMemcpyHostToDevice));
+    if (s == EMUGEMM_STATUS_SUCCESS) s = from_nccl(n->all_reduce(d, d, 1, ncclInt32, ncclMin, m->comm, cs));
+    if (s == EMUGEMM_STATUS_SUCCESS) s = from_cuda((int)cudaMemcpyAsync(&ok, d, sizeof ok, cudaMemcpyDeviceToHost, cs));
+    if (s == EMUGEMM_STATUS_SUCCESS) s = from_cuda((int)cudaStreamSynchronize(cs));
+    cudaFree(dev);
+    if (s != EMUGEMM_STATUS_SUCCESS) return s;
+    if (!ok) {
+        p2p_close(m);
+        m->p2p = 0;
+        std::fprintf(stderr, "emugemm: the ranks cannot map each other's memory; B travels by NCCL broadcast\n");
+        return EMUGEMM_STATUS_SUCCESS;
+    }
+    m->stage_bytes = bytes;
+    m->p2p = 1;
+    return EMUGEMM_STATUS_SUCCESS;
+}
+
 bool is_tc(emu_scheme_t s) {
     return s == EMU_SCHEME_BF16X3 || s == EMU_SCHEME_BF16X6 || s == EMU_SCHEME_FP16X3;
 }
@@ -175,6 +347,9 @@ void multigpu_release(Handle* h) {
     if (m->stream) cudaStreamSynchronize(m->stream);
     const NcclApi* n = nccl();
     if (m->comm && n) n->destroy(m->comm);
+    cudaDeviceSynchronize();   // no copy from or to a mapped buffer in flight
+    p2p_close(m);
+    if (m->flags) cudaFree(m->flags);
     for (cudaEvent_t e : m->ev_panel)
         if (e) cudaEventDestroy(e);
     if (m->ev_start) cudaEventDestroy(m->ev_start);
@@ -346,17 +521,36 @@ emugemm_status_t emugemm_sgemm_rows(emugemm_handle_t handle, int M, int N, long 
                               : emu::rows_panels(M, m->size, N, K, gemm_sms, h->rows_panels);
     long wmax = 0;
     for (const auto& p : pan) wmax = std::max(wmax, p.second - p.first);
+    // B's path: copy engines over peer memory (default, when every rank can map the others' memory) or NCCL
+    const bool use_p2p = m->size > 1 && !h->bcast_nccl && K > 0 && N > 0 &&
+                         emu::p2p_setup(h, m, n, (size_t)K * N * 4) == EMUGEMM_STATUS_SUCCESS && m->p2p == 1;
     float* stage = nullptr;
-    if (K > 0 && N > 0) {
+    // calls that move B by copy engines are numbered alike on every rank (use_p2p is the same on all of them)
+    const unsigned seq = use_p2p ? ++m->seq : 0u;
+    const int buf = (int)(seq & 1u);
+    if (use_p2p) {
+        stage = m->stage[buf];
+    } else if (K > 0 && N > 0) {
         stage = static_cast<float*>(emu::ws_get(h, emu::kWsCommB, (size_t)K * N * 4));
         if (!stage) return EMUGEMM_STATUS_MEMORY_ERROR;
     }
-    // The broadcasts start once earlier work on the handle's stream is done with the staging buffer (and the root's B
-    // is final); panel j is packed on the root (B's columns [n0, n1) made contiguous at stage + K*n0), broadcast,
-    // and, on the other ranks, copied into B's columns when the caller passed a B to receive it.
+    // The transfers start once earlier work on the handle's stream is done with the staging buffer (and the root's B
+    // is final); panel j is packed on the root (B's columns [n0, n1) made contiguous at stage + K*n0), moved to the
+    // other ranks, and there copied into B's columns when the caller passed a B to receive it.
     int e = (int)cudaEventRecord(m->ev_start, cs);
     if (!e) e = (int)cudaStreamWaitEvent(m->stream, m->ev_start, 0);
     if (e) return emu::from_cuda(e);
+    // the tree for this root: v = position after the root; parent (v - 1) / 2, children 2v + 1 and 2v + 2
+    const int P = m->size, v = (m->rank - root + P) % P;
+    const int parent = v > 0 ? ((v - 1) / 2 + root) % P : -1, slot = v > 0 ? (v - 1) & 1 : 0;
+    if (use_p2p && seq > 2) {
+        // this buffer was last filled two calls ago: wait until the children have pulled it
+        for (int c = 0; c < 2; ++c)
+            if (2 * v + 1 + c < P) {
+                e = emu::wait_flag(m->flags + emu::kFlagRelease + c, seq - 2, h->err_dev, m->stream);
+                if (e) return emu::from_cuda(e);
+            }
+    }
     for (size_t j = 0; j < pan.size() && K > 0; ++j) {
         const long n0 = pan[j].first, w = pan[j].second - pan[j].first;
         float* sp = stage + (size_t)K * n0;
@@ -364,12 +558,29 @@ emugemm_status_t emugemm_sgemm_rows(emugemm_handle_t handle, int M, int N, long 
             e = (int)cudaMemcpy2DAsync(sp, (size_t)w * 4, B + n0, (size_t)ldb * 4, (size_t)w * 4, (size_t)K,
                                        cudaMemcpyDeviceToDevice, m->stream);
         if (e) return emu::from_cuda(e);
-        emugemm_status_t s = emu::from_nccl(n->broadcast(sp, sp, (size_t)K * w, ncclFloat, root, m->comm, m->stream));
-        if (s != EMUGEMM_STATUS_SUCCESS) return s;
+        if (use_p2p) {
+            if (!is_root) {
+                e = emu::wait_flag(m->peer_flags[parent] + emu::kFlagArrive + 16 * buf + j, seq, h->err_dev, m->stream);
+                if (!e)
+                    e = (int)cudaMemcpyAsync(sp, m->peer_stage[buf][parent] + (size_t)K * n0, (size_t)K * w * 4,
+                                             cudaMemcpyDeviceToDevice, m->stream);
+            }
+            if (!e) e = emu::set_flag(m->flags + emu::kFlagArrive + 16 * buf + j, seq, m->stream);
+            if (e) return emu::from_cuda(e);
+        } else {
+            emugemm_status_t s =
+                emu::from_nccl(n->broadcast(sp, sp, (size_t)K * w, ncclFloat, root, m->comm, m->stream));
+            if (s != EMUGEMM_STATUS_SUCCESS) return s;
+        }
         if (!is_root && B)
             e = (int)cudaMemcpy2DAsync(B + n0, (size_t)ldb * 4, sp, (size_t)w * 4, (size_t)w * 4, (size_t)K,
                                        cudaMemcpyDeviceToDevice, m->stream);
         if (!e) e = (int)cudaEventRecord(m->ev_panel[j], m->stream);
+        if (e) return emu::from_cuda(e);
+    }
+    if (use_p2p && !is_root) {
+        // every panel pulled: the parent may refill this buffer in two calls' time
+        e = emu::set_flag(m->peer_flags[parent] + emu::kFlagRelease + slot, seq, m->stream);
         if (e) return emu::from_cuda(e);
     }
     e = (int)cudaEventRecord(m->ev_done, m->stream);

@@ -21,7 +21,7 @@ AUTO, NATIVE_FP32, FP32_CHUNKED, BF16X3, FP16X3, BF16X6 = range(6)
 SCHEME_NAMES = ["AUTO", "NATIVE_FP32", "FP32_CHUNKED", "BF16X3", "FP16X3", "BF16X6"]
 
 # emugemm_attr_t: per-handle kernel choices
-ATTR_TC_KERNEL, ATTR_TC_SPLITK, ATTR_FP32_TILE, ATTR_ROWS_PANELS, ATTR_COMM_SMS = 0, 1, 2, 3, 4
+ATTR_TC_KERNEL, ATTR_TC_SPLITK, ATTR_FP32_TILE, ATTR_ROWS_PANELS, ATTR_COMM_SMS, ATTR_BCAST_NCCL = 0, 1, 2, 3, 4, 5
 TC_KERNEL_CODES = {"auto": 0, "single": 1, "pair": 2, "fused": 3, "fusea": 4}
 
 STATUS = {

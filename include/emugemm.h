@@ -256,9 +256,12 @@ typedef enum {
     EMUGEMM_ATTR_FP32_TILE = 2,   /* 0 auto, 16 (16 x 32), 32, 64, 128: tile of the FP32 SIMT kernel */
     EMUGEMM_ATTR_ROWS_PANELS = 3, /* emugemm_sgemm_rows: 0 = the modelled panel schedule, 1..16 = that many equal
                                      column panels of B (the same value on every rank) */
-    EMUGEMM_ATTR_COMM_SMS = 4     /* emugemm_sgemm_rows: SMs (even, 0..64) its tensor-core GEMMs leave free for the
+    EMUGEMM_ATTR_COMM_SMS = 4,    /* emugemm_sgemm_rows: SMs (even, 0..64) its tensor-core GEMMs leave free for the
                                      broadcast's NCCL kernels, so that neither waits for the other's SMs; C does
                                      not change (only the GEMMs' grid does) */
+    EMUGEMM_ATTR_BCAST_NCCL = 5   /* emugemm_sgemm_rows: 0 = B travels by copy engines over peer memory (CUDA IPC,
+                                     a tree of pulls; NCCL when the ranks cannot map each other's memory), 1 = NCCL
+                                     broadcast (the same value on every rank) */
 } emugemm_attr_t;
 /* INVALID_VALUE for an unknown attribute or a value outside the ranges above. */
 emugemm_status_t emugemm_set_attr(emugemm_handle_t handle, int attr, long value);

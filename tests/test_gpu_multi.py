@@ -5,7 +5,8 @@
   rounded once, identical to emugemm_sgemm_partial_f64 + emugemm_reduce_f64.
 - Two ranks (one process per GPU; skipped unless two sm_100 GPUs are visible): each rank's C rows equal a
   single-GPU emugemm_sgemm of the whole product bit for bit, for bf16x3 and fp16x3 and for ragged shapes whose row
-  blocks differ by one row; a measured rho (hint -1) agrees with the single-GPU estimate; the K-split sits within
+  blocks differ by one row, with B moved by copy engines over peer memory and by NCCL, from either root, over
+  several calls in a row (the received B equals the root's); a measured rho (hint -1) agrees with the single-GPU estimate; the K-split sits within
   the bf16x3 model error against FP64. NVLS stays off (NCCL_NVLS_ENABLE=0).
 """
 from __future__ import annotations
@@ -101,18 +102,24 @@ def _worker(rank, world, port, q):
             h.sgemm(M, N, K, A, B, ref, force=force, hints=hints())
             r0, r1 = h.comm_rows(M)
             assert (r0, r1) == multigpu.row_range(M, rank, world)
-            Bb = B.clone() if rank == 0 else torch.full_like(B, float("nan"))
             C_local = torch.full((r1 - r0, N), float("nan"), device="cuda")
-            for panels, comm_sms in ((0, 0), (5, 0), (0, 8)):
+            # B by copy engines over peer memory (default) and by NCCL broadcast; several calls in a row, so the
+            # double-buffered staging and its release flags cycle; root 1 as well as root 0
+            for panels, comm_sms, nccl, root in ((0, 0, 0, 0), (5, 0, 0, 0), (3, 0, 0, 1), (0, 0, 0, 0),
+                                                 (0, 8, 1, 0), (5, 0, 1, 1), (7, 0, 0, 0)):
                 h.set_attr(emugemm.ATTR_ROWS_PANELS, panels)
                 h.set_attr(emugemm.ATTR_COMM_SMS, comm_sms)    # a smaller GEMM grid: the same bits
-                h.sgemm_rows(M, N, K, A[r0:r1].contiguous(), K, Bb, N, C_local, N, root=0, force=force,
+                h.set_attr(emugemm.ATTR_BCAST_NCCL, nccl)
+                Bb = B.clone() if rank == root else torch.full_like(B, float("nan"))
+                C_local.fill_(float("nan"))
+                h.sgemm_rows(M, N, K, A[r0:r1].contiguous(), K, Bb, N, C_local, N, root=root, force=force,
                              hints=hints())
-                torch.cuda.synchronize()
-                res[f"rows_equal_{case}_{panels}_{comm_sms}"] = bool(torch.equal(C_local, ref[r0:r1]))
-            res[f"b_received_{case}"] = bool(torch.equal(Bb, B))
+                assert h.sync_status() == 0
+                res[f"rows_equal_{case}_{panels}_{comm_sms}_{nccl}_{root}"] = bool(torch.equal(C_local, ref[r0:r1]))
+                res[f"b_received_{case}_{panels}_{nccl}_{root}"] = bool(torch.equal(Bb, B))
         h.set_attr(emugemm.ATTR_ROWS_PANELS, 0)
         h.set_attr(emugemm.ATTR_COMM_SMS, 0)
+        h.set_attr(emugemm.ATTR_BCAST_NCCL, 0)
         # rho measured over both row blocks against the single-GPU estimate
         M, N, K = 1024, 1024, 2048
         g = torch.Generator(device="cuda").manual_seed(11)
