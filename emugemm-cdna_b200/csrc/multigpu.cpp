@@ -21,8 +21,8 @@
 // as the parent has it, so every node sends B at most twice. Arrival and release are 32-bit sequence flags in device
 // memory: one-warp kernels set them (a system-scope release store) and wait for them (bounded polls, which co-reside
 // with the GEMM's CTAs on an SM); a wait that runs out sets the handle's timeout bit, so emugemm_sync reports it.
-// The staging buffers alternate between two per call, and a parent reuses one only after its children have
-// released it. NCCL broadcasts remain the path when the ranks cannot map each other's memory, or on request.
+// The staging buffers alternate between two per call, and a rank refills one only after every rank has released
+// the call that filled it last (which ranks pulled from it depended on that call's root). NCCL broadcasts remain the path when the ranks cannot map each other's memory, or on request.
 #include "device_utils.cuh"
 #include "emugemm_internal.h"
 
@@ -100,9 +100,12 @@ struct Mg {
 };
 
 constexpr int kFlagArrive = 0;                     // + 16 * buffer + panel: the sequence number of the panel's call
-constexpr int kFlagRelease = 32;                   // + child slot: the last call whose panels that child has pulled
-constexpr size_t kFlagBytes = 256;
-constexpr unsigned long long kCommWaitNs = 30000000000ull;   // a peer that has not arrived within 30 s has failed
+constexpr int kFlagRelease = 32;                   // + rank: the last call whose panels that rank has pulled
+constexpr int kMaxP2pRanks = 32;
+constexpr size_t kFlagBytes = 4 * (kFlagRelease + kMaxP2pRanks);
+constexpr unsigned long long kCommWaitNs = 10000000000ull;   // a peer that has not arrived within 10 s has failed
+
+struct PeerFlags { unsigned* p[kMaxP2pRanks]; };
 
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     unsigned v;
@@ -110,34 +113,43 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     return v;
 }
 
-// Waits until *flag has reached `want` (sequence numbers compared modulo 2^32), at most limit_ns.
-__global__ void k_wait_flag(const unsigned* flag, unsigned want, unsigned* err, unsigned long long limit_ns) {
+// Waits until flag[i] has reached `want` for every i < n except `skip` (sequence numbers compared modulo 2^32), all
+// within limit_ns.
+__global__ void k_wait_flags(const unsigned* flag, int n, int skip, unsigned want, unsigned* err,
+                             unsigned long long limit_ns) {
     if (threadIdx.x != 0) return;
     const unsigned long long t0 = dev::globaltimer();
-    while ((int)(ld_acquire_sys(flag) - want) < 0) {
-        if (dev::globaltimer() - t0 > limit_ns) {
-            if (err) atomicOr(err, kErrTimeoutComm);
-            return;
+    for (int i = 0; i < n; ++i) {
+        if (i == skip) continue;
+        while ((int)(ld_acquire_sys(flag + i) - want) < 0) {
+            if (dev::globaltimer() - t0 > limit_ns) {
+                if (err) atomicOr(err, kErrTimeoutComm);
+                return;
+            }
+            __nanosleep(200);
         }
-        __nanosleep(200);
     }
 }
 
-// Publishes `v` in *flag after every earlier operation of the stream (the copy it announces) has completed.
-__global__ void k_set_flag(unsigned* flag, unsigned v) {
+// Publishes `v` in *f.p[i] for every i < n that is not null, after every earlier operation of the stream (the copy
+// it announces) has completed.
+__global__ void k_set_flags(PeerFlags f, int n, unsigned v) {
     if (threadIdx.x != 0) return;
     __threadfence_system();
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
+    for (int i = 0; i < n; ++i)
+        if (f.p[i]) asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f.p[i]), "r"(v) : "memory");
 }
 
-int wait_flag(const unsigned* flag, unsigned want, unsigned* err, cudaStream_t st) {
-    k_wait_flag<<<1, 32, 0, st>>>(flag, want, err, kCommWaitNs);
+int wait_flags(const unsigned* flag, int n, int skip, unsigned want, unsigned* err, cudaStream_t st) {
+    k_wait_flags<<<1, 32, 0, st>>>(flag, n, skip, want, err, kCommWaitNs);
     count_launch();
     return (int)cudaGetLastError();
 }
 
 int set_flag(unsigned* flag, unsigned v, cudaStream_t st) {
-    k_set_flag<<<1, 32, 0, st>>>(flag, v);
+    PeerFlags f{};
+    f.p[0] = flag;
+    k_set_flags<<<1, 32, 0, st>>>(f, 1, v);
     count_launch();
     return (int)cudaGetLastError();
 }
@@ -245,6 +257,10 @@ std::vector<std::pair<long, long>> rows_panels(long M, int size, long N, long K,
 // the old buffers have ended.
 emugemm_status_t p2p_setup(Handle* h, Mg* m, const NcclApi* n, size_t bytes) {
     if (m->p2p == 0 || (m->p2p == 1 && m->stage_bytes >= bytes)) return EMUGEMM_STATUS_SUCCESS;
+    if (m->size > kMaxP2pRanks) {
+        m->p2p = 0;
+        return EMUGEMM_STATUS_SUCCESS;
+    }
     cudaStream_t cs = (cudaStream_t)h->stream;
     // every rank's device idle before any buffer is replaced: local sync, then a collective both ways
     if (cudaDeviceSynchronize() != cudaSuccess) return EMUGEMM_STATUS_INTERNAL_ERROR;
@@ -542,14 +558,12 @@ emugemm_status_t emugemm_sgemm_rows(emugemm_handle_t handle, int M, int N, long 
     if (e) return emu::from_cuda(e);
     // the tree for this root: v = position after the root; parent (v - 1) / 2, children 2v + 1 and 2v + 2
     const int P = m->size, v = (m->rank - root + P) % P;
-    const int parent = v > 0 ? ((v - 1) / 2 + root) % P : -1, slot = v > 0 ? (v - 1) & 1 : 0;
+    const int parent = v > 0 ? ((v - 1) / 2 + root) % P : -1;
     if (use_p2p && seq > 2) {
-        // this buffer was last filled two calls ago: wait until the children have pulled it
-        for (int c = 0; c < 2; ++c)
-            if (2 * v + 1 + c < P) {
-                e = emu::wait_flag(m->flags + emu::kFlagRelease + c, seq - 2, h->err_dev, m->stream);
-                if (e) return emu::from_cuda(e);
-            }
+        // this buffer was last filled two calls ago: wait until every rank has released that call (its pulls are
+        // done; which ranks pulled from this one depended on that call's root)
+        e = emu::wait_flags(m->flags + emu::kFlagRelease, P, m->rank, seq - 2, h->err_dev, m->stream);
+        if (e) return emu::from_cuda(e);
     }
     for (size_t j = 0; j < pan.size() && K > 0; ++j) {
         const long n0 = pan[j].first, w = pan[j].second - pan[j].first;
@@ -560,7 +574,8 @@ emugemm_status_t emugemm_sgemm_rows(emugemm_handle_t handle, int M, int N, long 
         if (e) return emu::from_cuda(e);
         if (use_p2p) {
             if (!is_root) {
-                e = emu::wait_flag(m->peer_flags[parent] + emu::kFlagArrive + 16 * buf + j, seq, h->err_dev, m->stream);
+                e = emu::wait_flags(m->peer_flags[parent] + emu::kFlagArrive + 16 * buf + j, 1, -1, seq, h->err_dev,
+                                    m->stream);
                 if (!e)
                     e = (int)cudaMemcpyAsync(sp, m->peer_stage[buf][parent] + (size_t)K * n0, (size_t)K * w * 4,
                                              cudaMemcpyDeviceToDevice, m->stream);
@@ -578,9 +593,14 @@ emugemm_status_t emugemm_sgemm_rows(emugemm_handle_t handle, int M, int N, long 
         if (!e) e = (int)cudaEventRecord(m->ev_panel[j], m->stream);
         if (e) return emu::from_cuda(e);
     }
-    if (use_p2p && !is_root) {
-        // every panel pulled: the parent may refill this buffer in two calls' time
-        e = emu::set_flag(m->peer_flags[parent] + emu::kFlagRelease + slot, seq, m->stream);
+    if (use_p2p) {
+        // every panel pulled (the root pulls none): tell every rank, each may refill its buffer in two calls' time
+        emu::PeerFlags f{};
+        for (int r = 0; r < P; ++r)
+            if (r != m->rank) f.p[r] = m->peer_flags[r] + emu::kFlagRelease + m->rank;
+        emu::k_set_flags<<<1, 32, 0, m->stream>>>(f, P, seq);
+        emu::count_launch();
+        e = (int)cudaGetLastError();
         if (e) return emu::from_cuda(e);
     }
     e = (int)cudaEventRecord(m->ev_done, m->stream);

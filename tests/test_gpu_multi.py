@@ -75,6 +75,14 @@ def test_one_rank_comm(cuda):
 
 
 def _worker(rank, world, port, q):
+    try:
+        _work(rank, world, port, q)
+    except BaseException as exc:  # noqa: BLE001 - reported to the parent instead of leaving it waiting
+        q.put((rank, {"error": repr(exc)}))
+        raise
+
+
+def _work(rank, world, port, q):
     import datetime
     import sys
 
@@ -166,7 +174,8 @@ def test_two_gpu_entry_points():
     for p in alive:
         p.kill()
     assert not alive
-    out = dict(q.get() for _ in range(2))
+    out = dict(q.get(timeout=30) for _ in range(2))
+    assert not any("error" in v for v in out.values()), out
     for r in (0, 1):
         for k, v in out[r].items():
             if k.startswith(("rows_equal", "b_received")):
