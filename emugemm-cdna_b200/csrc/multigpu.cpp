@@ -17,8 +17,9 @@
 // broadcast kernels need SMs of their own (about 27 GB/s per CTA measured), so they either wait for the GEMMs or take
 // SMs from them. By default B therefore moves by COPY ENGINES over NVLink peer memory, which use no SM: every rank
 // maps the staging buffers of the others (CUDA IPC, set up once per size), and the ranks form a binary tree rooted
-// at `root`; each rank pulls panel j from its parent's staging buffer into its own with one cudaMemcpyAsync as soon
-// as the parent has it, so every node sends B at most twice. Arrival and release are 32-bit sequence flags in device
+// at `root`; the root copies B into its buffer in one piece, and each other rank pulls panel j from its parent's
+// buffer into its own with one pitched cudaMemcpy2DAsync as soon as the parent has it, so every node sends B at
+// most twice. Arrival and release are 32-bit sequence flags in device
 // memory: one-warp kernels set them (a system-scope release store) and wait for them (bounded polls, which co-reside
 // with the GEMM's CTAs on an SM); a wait that runs out sets the handle's timeout bit, so emugemm_sync reports it.
 // The staging buffers alternate between two per call, and a rank refills one only after every rank has released
@@ -565,30 +566,48 @@ emugemm_status_t emugemm_sgemm_rows(emugemm_handle_t handle, int M, int N, long 
         e = emu::wait_flags(m->flags + emu::kFlagRelease, P, m->rank, seq - 2, h->err_dev, m->stream);
         if (e) return emu::from_cuda(e);
     }
+    // Staging layouts. Copy engines: B row-major (ld N) on every rank; the root fills its buffer with one contiguous
+    // copy (a pitched same-GPU copy beside its GEMMs cost them 0.23 ms at 8192^3, a contiguous one 0.05 ms) and
+    // announces every panel, and each other rank pulls panel j as a pitched copy over NVLink from its parent. NCCL:
+    // panel j contiguous at stage + K * n0 (a broadcast buffer must be contiguous), packed on the root.
+    if (use_p2p && is_root && K > 0 && N > 0) {
+        e = ldb == N ? (int)cudaMemcpyAsync(stage, B, (size_t)K * N * 4, cudaMemcpyDeviceToDevice, m->stream)
+                     : (int)cudaMemcpy2DAsync(stage, (size_t)N * 4, B, (size_t)ldb * 4, (size_t)N * 4, (size_t)K,
+                                              cudaMemcpyDeviceToDevice, m->stream);
+        if (!e) {
+            emu::PeerFlags f{};
+            for (size_t j = 0; j < pan.size(); ++j) f.p[j] = m->flags + emu::kFlagArrive + 16 * buf + j;
+            emu::k_set_flags<<<1, 32, 0, m->stream>>>(f, (int)pan.size(), seq);
+            emu::count_launch();
+            e = (int)cudaGetLastError();
+        }
+        if (e) return emu::from_cuda(e);
+    }
     for (size_t j = 0; j < pan.size() && K > 0; ++j) {
         const long n0 = pan[j].first, w = pan[j].second - pan[j].first;
-        float* sp = stage + (size_t)K * n0;
-        if (is_root)
-            e = (int)cudaMemcpy2DAsync(sp, (size_t)w * 4, B + n0, (size_t)ldb * 4, (size_t)w * 4, (size_t)K,
-                                       cudaMemcpyDeviceToDevice, m->stream);
-        if (e) return emu::from_cuda(e);
+        float* sp = use_p2p ? stage + n0 : stage + (size_t)K * n0;
+        const long sld = use_p2p ? N : w;
         if (use_p2p) {
             if (!is_root) {
                 e = emu::wait_flags(m->peer_flags[parent] + emu::kFlagArrive + 16 * buf + j, 1, -1, seq, h->err_dev,
                                     m->stream);
                 if (!e)
-                    e = (int)cudaMemcpyAsync(sp, m->peer_stage[buf][parent] + (size_t)K * n0, (size_t)K * w * 4,
-                                             cudaMemcpyDeviceToDevice, m->stream);
+                    e = (int)cudaMemcpy2DAsync(sp, (size_t)N * 4, m->peer_stage[buf][parent] + n0, (size_t)N * 4,
+                                               (size_t)w * 4, (size_t)K, cudaMemcpyDeviceToDevice, m->stream);
+                if (!e) e = emu::set_flag(m->flags + emu::kFlagArrive + 16 * buf + j, seq, m->stream);
+                if (e) return emu::from_cuda(e);
             }
-            if (!e) e = emu::set_flag(m->flags + emu::kFlagArrive + 16 * buf + j, seq, m->stream);
-            if (e) return emu::from_cuda(e);
         } else {
+            if (is_root)
+                e = (int)cudaMemcpy2DAsync(sp, (size_t)w * 4, B + n0, (size_t)ldb * 4, (size_t)w * 4, (size_t)K,
+                                           cudaMemcpyDeviceToDevice, m->stream);
+            if (e) return emu::from_cuda(e);
             emugemm_status_t s =
                 emu::from_nccl(n->broadcast(sp, sp, (size_t)K * w, ncclFloat, root, m->comm, m->stream));
             if (s != EMUGEMM_STATUS_SUCCESS) return s;
         }
         if (!is_root && B)
-            e = (int)cudaMemcpy2DAsync(B + n0, (size_t)ldb * 4, sp, (size_t)w * 4, (size_t)w * 4, (size_t)K,
+            e = (int)cudaMemcpy2DAsync(B + n0, (size_t)ldb * 4, sp, (size_t)sld * 4, (size_t)w * 4, (size_t)K,
                                        cudaMemcpyDeviceToDevice, m->stream);
         if (!e) e = (int)cudaEventRecord(m->ev_panel[j], m->stream);
         if (e) return emu::from_cuda(e);
@@ -677,8 +696,8 @@ emugemm_status_t emugemm_sgemm_rows(emugemm_handle_t handle, int M, int N, long 
                     e = (int)cudaStreamWaitEvent(ps, m->ev_panel[j], 0);
                     if (e) return emu::from_cuda(e);
                 }
-                const float* Bp = is_root ? B + n0 : stage + (size_t)K * n0;
-                const long bld = is_root ? ldb : w;
+                const float* Bp = is_root ? B + n0 : use_p2p ? stage + n0 : stage + (size_t)K * n0;
+                const long bld = is_root ? ldb : use_p2p ? N : w;
                 h->stream = ps;
                 h->bank = odd ? 1 : 0;
                 st = emu::dispatch(h, plan.chosen, plan.chunks, ml, (int)w, K, A_local, lda, Bp, bld, C_local + n0, ldc,
