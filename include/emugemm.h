@@ -157,9 +157,10 @@ emugemm_status_t emugemm_sgemm_ex(emugemm_handle_t handle,
 
 /* emugemm_sgemm on HOST buffers (no emugemm-cdna counterpart; its callers copy to the device themselves):
    A (MxK), B (KxN), C (MxN) row-major in host memory, pinned (cudaHostAlloc / cudaHostRegister) for the
-   copies to overlap. With every hint given (absmax >= 0, rho >= 0), A is copied to the device once and B and C
-   travel in column panels of about N/8 on two copy streams of the handle, each panel's GEMM starting as soon
-   as its panel of B has landed and its panel of C leaving while later panels of B arrive; A is split once.
+   copies to overlap. With every hint given (absmax >= 0, rho >= 0), B is copied to the device first in one piece,
+   then A and C travel in row panels of about M/8 on two copy streams of the handle (every copy contiguous), each
+   panel's GEMM starting as soon as its rows of A have landed and its rows of C leaving while later rows of A
+   arrive.
    Hints that ask for measurements (or NULL hints) copy all of A and B first and then run emugemm_sgemm.
    C is identical to emugemm_sgemm's for BF16X3, FP16X3 and NATIVE_FP32; FP32_CHUNKED keeps the same FMA
    chains, but its FP64 chunk groups follow the panel's tile count. Asynchronous on the handle's stream: C is

@@ -502,7 +502,7 @@ def test_fused_split_kernel_partial_f64(cuda, handle, variant):
 @pytest.mark.parametrize("force", [emugemm.BF16X3, emugemm.FP16X3, emugemm.NATIVE_FP32])
 @pytest.mark.parametrize("shape", [(1024, 2048, 512), (300, 520, 1000), (1, 1, 1), (257, 3000, 64)])
 def test_sgemm_host_matches_device(cuda, handle, force, shape):
-    """emugemm_sgemm_host (pinned host A, B, C; B and C in column panels overlapped with the GEMMs) gives the bits
+    """emugemm_sgemm_host (pinned host A, B, C; B first, A and C in row panels overlapped with the GEMMs) gives the bits
     of emugemm_sgemm on device copies of the same operands, with hints given (pipelined) and with NULL hints
     (copy everything, then the device path)."""
     torch = cuda
@@ -523,10 +523,10 @@ def test_sgemm_host_matches_device(cuda, handle, force, shape):
 @pytest.mark.parametrize("force", [emugemm.BF16X3, emugemm.FP16X3])
 def test_sgemm_host_long_k_matches_device(cuda, handle, force):
     """Few output tiles and a long K: the single call splits K over the SM pairs (bf16x3 in the fused kernel). The
-    host-buffer entry point runs column panels with fewer tiles each, but with the kernel and split count of the
+    host-buffer entry point runs row panels with fewer tiles each, but with the kernel and split count of the
     whole product, so its C has the same bits."""
     torch = cuda
-    M, N, K = 256, 1024, 24000
+    M, N, K = 1024, 256, 24000
     A = datagen.normal((M, K), 93)
     B = datagen.normal((K, N), 94)
     want, _, _ = run_sgemm(torch, handle, A, B, force=force, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
