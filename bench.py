@@ -82,8 +82,7 @@ def peaks():
 
 def tc_kernel_name(M: int, N: int, K: int, scheme: str) -> str:
     """The tensor-core kernel the library picks for this shape: EMUGEMM_TC_KERNEL, else the tile table's code, else
-    the built-in rule of the library (a copy of it);
-    fp16x3 has no fused variants."""
+    the built-in rule of the library (a copy of it); fp16x3 has no fused-A variant."""
     import emugemm
 
     fp16 = scheme == "fp16x3"
@@ -99,7 +98,10 @@ def tc_kernel_name(M: int, N: int, K: int, scheme: str) -> str:
                 code = 3
         else:
             code = 2 if ((K > 1024 or pair_tiles >= 512) if pair_tiles >= pairs else K >= 16384) else 1
-    if fp16 and code >= 3:
+            nck = -(-K // 128)
+            if code == 2 and pair_tiles < 16 and min(pairs // pair_tiles, nck // 8) > 1:
+                code = 3
+    if fp16 and code == 4:
         code = 2
     return {1: "k_tc_gemm", 2: "k_tc_gemm_pair", 3: "k_tc_fused",
             4: "k_tc_fused_a (+ k_split_cols of B)"}.get(code, "k_tc_gemm")

@@ -233,9 +233,15 @@ int tc_kernel_choice(Handle* h, int M, int N, long K, bool fp16) {
                 tc_split_count(round_up(M, 256), round_up(N, 256), K, h->num_sms, h->tc_splitk) > 1)
                 code = 3;
         }
-        else code = (pair_tiles >= pairs ? (K > 1024 || pair_tiles >= 512) : K >= 16384) ? 2 : 1;
+        else {
+            code = (pair_tiles >= pairs ? (K > 1024 || pair_tiles >= 512) : K >= 16384) ? 2 : 1;
+            // few tiles and K split over the SM pairs: as for bf16x3, the split in shared memory saves the split pass
+            if (code == 2 && pair_tiles < 16 &&
+                tc_split_count(round_up(M, 256), round_up(N, 256), K, h->num_sms, h->tc_splitk) > 1)
+                code = 3;
+        }
     }
-    if (fp16 && code >= 3) code = 2;
+    if (fp16 && code == 4) code = 2;   // fp16x3 has no A-in-TMEM kernel
     if (log_enabled()) {
         static const char* names[] = {"?", "single", "pair", "fused", "fusea"};
         std::fprintf(stderr, "emugemm: tensor-core kernel=%s (%s) M=%d N=%d K=%ld\n", names[code], fp16 ? "fp16x3" : "bf16x3",
@@ -259,8 +265,8 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
                                bool a_only = false) {
     const int choice = tc_kernel_choice(h, M, N, K, fp16);
     if (a_only && (choice == 3 || choice == 4)) return EMUGEMM_STATUS_SUCCESS;   // these split A in the kernel
-    if (choice == 3) {
-        ProfScope ps(h, kProfTcGemm);
+    if (choice == 3 && (lda & 3) == 0 && (ldb & 3) == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(B) & 15) == 0) {
         const int splits = h->pin_splits ? h->pin_splits
                                          : tc_split_count(round_up(M, 256), round_up(N, 256), K, h->num_sms, h->tc_splitk);
         double* part = nullptr;
@@ -268,8 +274,22 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
             part = (double*)ws_get(h, bank_slot(h, kWsSplitK), (size_t)splits * M * N * sizeof(double));
             if (!part) return EMUGEMM_STATUS_MEMORY_ERROR;
         }
+        int* rexp = nullptr;
+        int* cexp = nullptr;
+        if (fp16) {
+            // the scale exponents of the split, made by the same scans as on the pre-split path
+            rexp = (int*)ws_get(h, kWsScaleA, (size_t)M * 4);
+            cexp = (int*)ws_get(h, bank_slot(h, kWsScaleB), (size_t)N * 8);
+            if (!rexp || !cexp) return EMUGEMM_STATUS_MEMORY_ERROR;
+            h->a_key = Handle::ASplitKey();   // the row exponents are rewritten below
+            ProfScope ps(h, kProfScan);
+            int e = launch_row_exponents(A, M, K, lda, rexp, h->stream);
+            if (!e) e = launch_col_exponents(B, K, N, ldb, cexp, reinterpret_cast<unsigned*>(cexp + N), h->stream);
+            if (e) return from_cuda(e);
+        }
+        ProfScope ps(h, kProfTcGemm);
         const int e = launch_tc_fused(A, lda, B, ldb, M, N, K, C, ldc, C64, ldc64, h->err_dev, tc_grid_sms(h), h->stream,
-                                      splits, part);
+                                      splits, part, fp16 ? 1 : 0, rexp, cexp);
         if (e != (int)cudaErrorNotSupported) {
             if (e || splits <= 1) return from_cuda(e);
             return from_cuda(launch_reduce_f64(part, splits, M, N, (long)M * N, C, ldc, C64, ldc64, h->stream));

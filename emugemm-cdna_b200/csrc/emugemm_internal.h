@@ -234,12 +234,15 @@ int tc_gemm_bn(int fp16);   // output tile width of the bf16x3 (0) / fp16x3 (1) 
 // k_tc_gemm2.cu: the same product on CTA pairs (cta_group::2); needs Mp % 256 == 0.
 int launch_tc_gemm_pair(const TcGemmArgs& a, void* stream);
 int tc_pair_bn(int fp16);
-// k_tc_fused.cu: bf16x3 with the split fused into the CTA-pair GEMM (FP32 tiles by TMA, no slices in HBM).
+// k_tc_fused.cu: bf16x3 / fp16x3 with the split fused into the CTA-pair GEMM (FP32 tiles by TMA, no slices in HBM).
 // splits / part64: K splits on 128-K chunk boundaries with FP64 partial planes, as for launch_tc_gemm_pair.
 // Returns cudaErrorNotSupported unless lda, ldb are multiples of 4 and A, B are 16-byte aligned.
+// fp16: the scaled fp16x3 form (row_exp / col_exp: the exponents of launch_row_exponents / launch_col_exponents),
+// bit-identical to launch_tc_gemm_pair over the pre-split fp16 slices.
 int launch_tc_fused(const float* A, long lda, const float* B, long ldb, int M, int N, long K, float* C, long ldc,
                     double* C64, long ldc64, unsigned* err, int num_sms, void* stream, int splits = 1,
-                    double* part64 = nullptr);
+                    double* part64 = nullptr, int fp16 = 0, const int* row_exp = nullptr,
+                    const int* col_exp = nullptr);
 // k_tc_fused_a.cu: bf16x3 on CTA pairs with A split in the kernel into TMEM and B's slices pre-split (b_hi, b_lo:
 // Np x Kp in K panels of KP, Np a multiple of tc_fused_a_bn()). cudaErrorNotSupported unless lda % 4 == 0 and A is
 // 16-byte aligned.

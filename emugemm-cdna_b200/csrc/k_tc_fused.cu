@@ -1,4 +1,12 @@
-// k_tc_fused.cu - bf16x3 emulated SGEMM with the hi/lo split fused into the GEMM (CTA pairs, cta_group::2).
+// k_tc_fused.cu - bf16x3 and fp16x3 emulated SGEMM with the hi/lo split fused into the GEMM (CTA pairs,
+// cta_group::2).
+//
+// fp16x3 (FP16 = true): the converters split x * 2^-e (e: the row exponent of A's row, the column exponent of B's
+// column, both from the exponent scans of k_split.cu) with the fp16 rule hi = RNE_f16(x'), lo = RNE_f16((x' - hi) *
+// 2048), exactly as k_split.cu does; the MMAs of a 64-K chunk (two k-blocks, both stages held) run in the order of
+// the fp16 pair kernel (k_tc_gemm2.cu): the cross products lo*hi and hi*lo of all four k16 steps, then the first
+// hi*hi scaling the accumulator by 2^-11 on the way in, then the other hi*hi; the store undoes 2^(e_row + e_col).
+// So its C is bit-identical to the pre-split fp16 pair kernel's, and the slices never exist in HBM.
 //
 // The pre-split path (k_split.cu + k_tc_gemm*.cu) writes the bf16 slices of A and B to HBM and reads them back.
 // Here TMA loads the caller's FP32 tiles straight into a shared-memory staging ring, converter warps split them
@@ -29,6 +37,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace emu {
@@ -69,7 +78,9 @@ static_assert(kBfA == kBfB, "each lo slice sits kBfA bytes after its hi slice");
 constexpr int kAccCols = kBN;
 constexpr int kHalf = kBN / 2;
 constexpr int kSmemBytes = kF32Stages * kF32Stage + kBfStages * kBfStage + 1024 + 512;
-constexpr uint32_t kIdesc = idesc_f16(2 * kBM, kBN, true);
+// k-blocks per accumulator: bf16x3 promotes every 128 values of K, fp16x3 every 64 (as the pair kernels do)
+template <bool FP16>
+constexpr int chunk_kb() { return FP16 ? 64 / kBK : kChunkKB; }
 
 struct CtlF {
     uint64_t f32_full[kF32Stages];
@@ -92,6 +103,7 @@ struct KParamsF {
     double* C64; long ldc64;
     double* part;      // splits > 1: FP64 partial planes [splits][M][N]
     unsigned* err;
+    const int* row_exp; const int* col_exp;   // fp16x3: scale exponents of A's rows and B's columns
 };
 
 // Work unit u (tile x K split): the tile, the split and its k-block range [kb0, kb1).
@@ -151,11 +163,40 @@ __device__ __forceinline__ void split8(const float (&x)[8], uint4& hi, uint4& lo
     lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
+// The same, fp16 slices of x * 2^-e: hi = RNE_f16(x'), lo = RNE_f16((x' - hi) * 2048), the rule of the split pass.
+__device__ __forceinline__ void split8_f16(const float (&x)[8], int e, uint4& hi, uint4& lo) {
+    // x * 2^-e equals ldexpf(x, -e) (one correctly rounded result) when 2^-e is a normal float
+    const bool mul = e >= -127 && e <= 126;
+    const float s = __int_as_float((127 - (mul ? e : 0)) << 23);
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float x0 = mul ? x[2 * j] * s : ldexpf(x[2 * j], -e);
+        const float x1 = mul ? x[2 * j + 1] * s : ldexpf(x[2 * j + 1], -e);
+        const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+        const __half l0 = __float2half_rn((x0 - __half2float(h0)) * 2048.0f);
+        const __half l1 = __float2half_rn((x1 - __half2float(h1)) * 2048.0f);
+        h[j] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+        l[j] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// x * 2^e rounded once to float, for the fp16x3 store of a row whose 2^e is not a normal float (as in k_tc_gemm2.cu)
+__device__ __forceinline__ float scale_pow2_exact(float x, int e) {
+    e = min(max(e, -1022), 1023);
+    return __double2float_rn((double)x * __longlong_as_double((long long)(e + 1023) << 52));
+}
+
 // byte offset of 16-byte chunk `c` of row `r` in a K-major tile with 64-byte rows and the 64-byte swizzle
 __device__ __forceinline__ uint32_t sw64(int r, int c) { return (uint32_t)(r * 64 + ((c ^ ((r >> 1) & 3)) << 4)); }
 
+template <bool FP16>
 __global__ void __launch_bounds__(kThreads, 1)
     k_tc_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, KParamsF p) {
+    constexpr int kChunk = chunk_kb<FP16>();
+    constexpr uint32_t kIdesc = idesc_f16(2 * kBM, kBN, !FP16);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* f32 = smem;
@@ -241,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int u = pair; u < num_units && ok; u += num_pairs) {
                     int t, sp, kbb, kbe;
                     unit_of_f(p, num_tiles, u, t, sp, kbb, kbe);
-                    for (int kb0 = kbb; kb0 < kbe && ok; kb0 += kChunkKB, ++ch) {
+                    for (int kb0 = kbb; kb0 < kbe && ok; kb0 += kChunk, ++ch) {
                         const int b = (int)(ch & 1);
                         const uint32_t bph = (uint32_t)((ch >> 1) & 1);
                         if (!mbar_wait_cluster(&ctl->tmem_empty[b], bph ^ 1u, abort, p.err, kErrTimeoutMma)) {
@@ -250,7 +291,55 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         tc_fence_after();
                         const uint32_t d = tmem_base + (uint32_t)(b * kAccCols);
-                        const int kb1 = min(kbe, kb0 + kChunkKB);
+                        const int kb1 = min(kbe, kb0 + kChunk);
+                        if (FP16) {
+                            // both k-blocks of the 64-K chunk: cross products of all k16 steps, then hi*hi, the
+                            // first of which scales the accumulator by 2^-11 (the fp16 pair kernel's order)
+                            uint32_t st[2] = {0u, 0u};
+                            int s_of[2] = {0, 0};
+                            const int nkb = kb1 - kb0;
+                            for (int i = 0; i < nkb; ++i) {
+                                const long itk = it + i;
+                                s_of[i] = (int)(itk % kBfStages);
+                                const uint32_t ph = (uint32_t)((itk / kBfStages) & 1);
+                                if (!mbar_wait_cluster(&ctl->bf_full[s_of[i]], ph, abort, p.err, kErrTimeoutMma)) {
+                                    ok = false;
+                                    break;
+                                }
+                                st[i] = smem_u32(bf + s_of[i] * kBfStage);
+                            }
+                            if (!ok) break;
+                            tc_fence_after();
+#pragma unroll
+                            for (int i = 0; i < 2; ++i) {
+                                if (i >= nkb) break;
+                                const uint64_t a_hi = sdesc_kmajor(st[i], 64), a_lo = sdesc_kmajor(st[i] + kBfA, 64);
+                                const uint64_t b_hi = sdesc_kmajor(st[i] + 2 * kBfA, 64);
+                                const uint64_t b_lo = sdesc_kmajor(st[i] + 2 * kBfA + kBfB, 64);
+#pragma unroll
+                                for (int ks = 0; ks < kBK / 16; ++ks) {
+                                    const uint64_t adv = (uint64_t)(ks * 32) >> 4;
+                                    mma_f16_ss_pair(d, a_lo + adv, b_hi + adv, kIdesc, (i != 0 || ks != 0) ? 1u : 0u);
+                                    mma_f16_ss_pair(d, a_hi + adv, b_lo + adv, kIdesc, 1u);
+                                }
+                            }
+#pragma unroll
+                            for (int i = 0; i < 2; ++i) {
+                                if (i >= nkb) break;
+                                const uint64_t a_hi = sdesc_kmajor(st[i], 64);
+                                const uint64_t b_hi = sdesc_kmajor(st[i] + 2 * kBfA, 64);
+#pragma unroll
+                                for (int ks = 0; ks < kBK / 16; ++ks) {
+                                    const uint64_t adv = (uint64_t)(ks * 32) >> 4;
+                                    if (i == 0 && ks == 0) mma_f16_ss_pair_scale11(d, a_hi, b_hi, kIdesc);
+                                    else mma_f16_ss_pair(d, a_hi + adv, b_hi + adv, kIdesc, 1u);
+                                }
+                            }
+                            for (int i = 0; i < nkb; ++i) mma_commit_pair_both(&ctl->bf_empty[s_of[i]], (uint16_t)0x3);
+                            it += nkb;
+                            mma_commit_pair_both(&ctl->tmem_full[b], (uint16_t)0x3);
+                            continue;
+                        }
                         for (int kb = kb0; kb < kb1; ++kb, ++it) {
                             const int s = (int)(it % kBfStages);
                             const uint32_t ph = (uint32_t)((it / kBfStages) & 1);
@@ -296,8 +385,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             long it = 0;
             bool ok = true;
             for (int u = pair; u < num_units && ok; u += num_pairs) {
-                int t, sp, kbb, kbe;
+                int t, sp, kbb, kbe, mb2, nb;
                 unit_of_f(p, num_tiles, u, t, sp, kbb, kbe);
+                tile_coords_f(t, p.num_m2, p.num_n, mb2, nb);
+                const int a_row0 = mb2 * 2 * kBM + (int)rank * kBM;   // this CTA's first row of A
+                const int b_col0 = nb * kBN + (int)rank * kBNH;       // and first column of B
                 for (int kb = kbb; kb < kbe; ++kb, ++it) {
                     const int s = (int)(it % kF32Stages);
                     const uint32_t ph = (uint32_t)((it / kF32Stages) & 1);
@@ -316,6 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int i0 = 0; i0 < kPer; i0 += kBatch) {
                         float x[kBatch][8];
                         uint32_t dst[kBatch];   // offset of the hi chunk in the stage; lo is kBfA further
+                        int ex[kBatch];         // fp16x3: the item's scale exponent
 #pragma unroll
                         for (int i = 0; i < kBatch; ++i) {
                             const int item = ct + (i0 + i) * kConvThreads;
@@ -328,12 +421,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 x[i][0] = u.x; x[i][1] = u.y; x[i][2] = u.z; x[i][3] = u.w;
                                 x[i][4] = v.x; x[i][5] = v.y; x[i][6] = v.z; x[i][7] = v.w;
                                 dst[i] = sw64(r, g);
+                                ex[i] = (FP16 && a_row0 + r < p.M) ? __ldg(p.row_exp + a_row0 + r) : 0;
                             } else {
                                 const int i2 = item - 512;
                                 const int r = i2 & (kBNH - 1), g = i2 >> 7;   // column n of this CTA's B, k-group
 #pragma unroll
                                 for (int j = 0; j < 8; ++j) x[i][j] = fb[(8 * g + j) * kBNH + r];
                                 dst[i] = (uint32_t)(2 * kBfA) + sw64(r, g);
+                                ex[i] = (FP16 && b_col0 + r < p.N) ? __ldg(p.col_exp + b_col0 + r) : 0;
                             }
                         }
 #pragma unroll
@@ -341,7 +436,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const int item = ct + (i0 + i) * kConvThreads;
                             if (i0 + i >= kPer || item >= 1024) continue;
                             uint4 hv, lv;
-                            split8(x[i], hv, lv);
+                            if (FP16) split8_f16(x[i], ex[i], hv, lv);
+                            else split8(x[i], hv, lv);
                             *reinterpret_cast<uint4*>(ob + dst[i]) = hv;
                             *reinterpret_cast<uint4*>(ob + dst[i] + kBfA) = lv;
                         }
@@ -378,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             int t, sp, kbb, kbe, mb2, nb;
             unit_of_f(p, num_tiles, u, t, sp, kbb, kbe);
             tile_coords_f(t, p.num_m2, p.num_n, mb2, nb);
-            const int nchunks = (kbe - kbb + kChunkKB - 1) / kChunkKB;
+            const int nchunks = (kbe - kbb + kChunk - 1) / kChunk;
             float sum[kHalf];
 #pragma unroll
             for (int j = 0; j < kHalf; ++j) sum[j] = 0.f;
@@ -405,30 +501,50 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int m = mb2 * 2 * kBM + row_in_tile;
             if (m < p.M) {
                 const int n0 = nb * kBN + col0;
-                if (p.splits > 1) {
-                    double* crow = p.part + ((size_t)sp * p.M + m) * p.N;
-#pragma unroll
-                    for (int j = 0; j < kHalf; ++j)
-                        if (n0 + j < p.N) crow[n0 + j] = (double)sum[j];
-                } else if (p.C64) {
-                    double* crow = p.C64 + (size_t)m * p.ldc64;
-#pragma unroll
-                    for (int j = 0; j < kHalf; ++j)
-                        if (n0 + j < p.N) crow[n0 + j] = (double)sum[j];
-                } else {
-                    float* crow = p.C + (size_t)m * p.ldc;
-                    const bool vec = (n0 + kHalf <= p.N) && ((p.ldc & 3) == 0) &&
-                                     ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
-                    if (vec) {
-                        float4* c4 = reinterpret_cast<float4*>(crow + n0);
-#pragma unroll
-                        for (int j = 0; j < kHalf / 4; ++j)
-                            c4[j] = make_float4(sum[4 * j], sum[4 * j + 1], sum[4 * j + 2], sum[4 * j + 3]);
-                    } else {
+                auto store_row = [&](auto&& val) {
+                    if (p.splits > 1) {
+                        double* crow = p.part + ((size_t)sp * p.M + m) * p.N;
 #pragma unroll
                         for (int j = 0; j < kHalf; ++j)
-                            if (n0 + j < p.N) crow[n0 + j] = sum[j];
+                            if (n0 + j < p.N) crow[n0 + j] = (double)val(j);
+                    } else if (p.C64) {
+                        double* crow = p.C64 + (size_t)m * p.ldc64;
+#pragma unroll
+                        for (int j = 0; j < kHalf; ++j)
+                            if (n0 + j < p.N) crow[n0 + j] = (double)val(j);
+                    } else {
+                        float* crow = p.C + (size_t)m * p.ldc;
+                        const bool vec = (n0 + kHalf <= p.N) && ((p.ldc & 3) == 0) &&
+                                         ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
+                        if (vec) {
+                            float4* c4 = reinterpret_cast<float4*>(crow + n0);
+#pragma unroll
+                            for (int j = 0; j < kHalf / 4; ++j)
+                                c4[j] = make_float4(val(4 * j), val(4 * j + 1), val(4 * j + 2), val(4 * j + 3));
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < kHalf; ++j)
+                                if (n0 + j < p.N) crow[n0 + j] = val(j);
+                        }
                     }
+                };
+                if (!FP16) {
+                    store_row([&](int j) { return sum[j]; });
+                } else {
+                    // undo the split's 2^-(e_row + e_col): one exact multiply while 2^e is a normal float, the exact
+                    // double form for a row where it is not (as the fp16 pair kernel stores); columns past N read
+                    // exponent 0 and are not stored
+                    const int e_row = p.row_exp[m];
+                    const int* cexp = p.col_exp + n0;
+                    bool normal = true;
+                    store_row([&](int j) {
+                        const int e = e_row + (n0 + j < p.N ? cexp[j] : 0);
+                        const int ec = min(max(e, -126), 127);
+                        normal = normal && (e == ec);
+                        return sum[j] * __int_as_float((ec + 127) << 23);
+                    });
+                    if (!normal)
+                        store_row([&](int j) { return scale_pow2_exact(sum[j], e_row + (n0 + j < p.N ? cexp[j] : 0)); });
                 }
             }
         }
@@ -449,7 +565,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // aligned A, B (TMA). Returns cudaErrorNotSupported when those do not hold, so the caller can pre-split instead.
 int launch_tc_fused(const float* A, long lda, const float* B, long ldb, int M, int N, long K, float* C, long ldc,
                     double* C64, long ldc64, unsigned* err, int num_sms, void* stream, int splits,
-                    double* part64) {
+                    double* part64, int fp16, const int* row_exp, const int* col_exp) {
+    if (fp16 && (!row_exp || !col_exp)) return (int)cudaErrorInvalidValue;
     if ((lda & 3) || (ldb & 3) || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
         return (int)cudaErrorNotSupported;
     PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
@@ -475,7 +592,8 @@ int launch_tc_fused(const float* A, long lda, const float* B, long ldb, int M, i
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return (int)cudaErrorInvalidValue;
     }
-    cudaError_t e = cudaFuncSetAttribute(k_tc_fused, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    auto kern = fp16 ? k_tc_fused<true> : k_tc_fused<false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return (int)e;
     KParamsF p;
     p.M = M;
@@ -497,6 +615,8 @@ int launch_tc_fused(const float* A, long lda, const float* B, long ldb, int M, i
     p.C64 = C64;
     p.ldc64 = ldc64;
     p.err = err;
+    p.row_exp = row_exp;
+    p.col_exp = col_exp;
     const int tiles = p.num_m2 * p.num_n;
 
     cudaLaunchConfig_t cfg = {};
@@ -512,7 +632,7 @@ int launch_tc_fused(const float* A, long lda, const float* B, long ldb, int M, i
     cfg.numAttrs = 1;
     cfg.gridDim = dim3(2, 1, 1);
     int clusters = 0;
-    e = cudaOccupancyMaxActiveClusters(&clusters, k_tc_fused, &cfg);
+    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
     if (e != cudaSuccess || clusters <= 0) {
         cudaGetLastError();
         clusters = (num_sms > 0 ? num_sms : 148) / 2;
@@ -520,7 +640,7 @@ int launch_tc_fused(const float* A, long lda, const float* B, long ldb, int M, i
     if (num_sms > 0 && clusters > num_sms / 2) clusters = num_sms / 2;   // a caller that leaves SMs to other work
     if (clusters > tiles * p.splits) clusters = tiles * p.splits;
     cfg.gridDim = dim3(2 * clusters, 1, 1);
-    e = cudaLaunchKernelEx(&cfg, k_tc_fused, ta, tb, p);
+    e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
     count_launch();
     if (e != cudaSuccess) return (int)e;
     return (int)cudaGetLastError();

@@ -610,3 +610,54 @@ def test_peak_probe(cuda, handle):
     assert 2000 < r["copy_gbs"] < 8000
     # the handle stays usable after the probe
     assert handle.absmax(dev(cuda, np.ones(16, np.float32)), 16) == 1.0
+
+
+@pytest.mark.parametrize("splits", [1, None, 5])
+@pytest.mark.parametrize("shape", [(256, 256, 128), (260, 516, 1004), (1024, 768, 2048), (384, 264, 96), (1, 1, 1),
+                                   (33, 68, 129), (256, 256, 40000), (260, 500, 20000), (300, 264, 9000)])
+@pytest.mark.parametrize("gen", ["normal", "wide_range"])
+def test_fused_fp16x3_matches_presplit_pair(cuda, handle, splits, shape, gen):
+    """fp16x3 with the scaled split fused into the CTA-pair GEMM (FP32 tiles by TMA, x * 2^-e split into fp16 hi/lo in
+    shared memory, the pair kernel's MMA order within each 64-K chunk, 2^e undone at the store) gives the bits of the
+    pre-split fp16 pair kernel, with the same K splits (1, the built-in count, or 5); and within the accumulation bound
+    of the exact scaled slice products."""
+    torch = cuda
+    M, N, K = shape
+    if gen == "normal":
+        A = datagen.normal((M, K), 170 + M)
+        B = datagen.normal((K, N), 171 + N)
+    else:
+        A = datagen.wide_range((M, K), 172 + M, emax=20)
+        B = datagen.wide_range((K, N), 173 + N, emax=20)
+    if splits is not None:
+        handle.set_kernels(splitk=splits)
+    out = {}
+    for v in ("pair", "fused"):
+        handle.set_kernels(tc_kernel=v)
+        handle.profile_begin()
+        C, p, _ = run_sgemm(torch, handle, A, B, force=emugemm.FP16X3, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+        prof = handle.profile_end()
+        assert p.chosen == emugemm.FP16X3
+        out[v] = (C, prof["split"][1])
+    assert np.isfinite(out["fused"][0]).all()
+    assert np.array_equal(out["fused"][0], out["pair"][0])
+    assert out["fused"][1] == (0 if (K % 4 == 0 and N % 4 == 0) else 1)   # no split pass when the fused kernel ran
+    R = oracle.gemm_f64(A, B)
+    d = np.linalg.norm(out["fused"][0].astype(np.float64) - oracle.slice_product(A, B, kind=1)) / np.linalg.norm(R)
+    assert d <= _accum_bound(K)
+
+
+def test_fused_fp16x3_is_the_builtin_choice_for_few_tiles_and_long_k(cuda, handle):
+    """256 x 256 x 65536 fp16x3: one pair tile, K split over the SM pairs; the built-in choice is now the fused kernel
+    (no split pass), with the bits of the pre-split pair kernel at the same split count."""
+    torch = cuda
+    M, N, K = 256, 256, 65536
+    A = datagen.uniform((M, K), 181)
+    B = datagen.uniform((K, N), 182)
+    handle.profile_begin()
+    C, _, _ = run_sgemm(torch, handle, A, B, force=emugemm.FP16X3, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+    prof = handle.profile_end()
+    assert prof["split"][1] == 0
+    handle.set_kernels(tc_kernel="pair")
+    Cp, _, _ = run_sgemm(torch, handle, A, B, force=emugemm.FP16X3, hints=emugemm.EmuHints(1, 1, 0, 0, 0))
+    assert np.array_equal(C, Cp)
