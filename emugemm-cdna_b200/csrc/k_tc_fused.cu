@@ -67,7 +67,11 @@ constexpr int kBK = 32;                             // k-block (64-byte rows of 
 constexpr int kChunkKB = 128 / kBK;                 // promotion every 128 values of K
 constexpr int kGroupM = 8;
 constexpr int kF32Stages = 3;
-constexpr int kBfStages = 3;
+// bf16 stages: 3 for bf16x3; 4 for fp16x3, whose MMA issuer holds the two stages of a 64-K chunk at once (with 3 the
+// converters could run only one stage ahead of it)
+constexpr int kBfStagesMax = 4;
+template <bool FP16>
+constexpr int bf_stages() { return FP16 ? 4 : 3; }
 constexpr int kF32A = kBM * kBK * 4;                // 16 KB
 constexpr int kF32B = kBK * kBNH * 4;               // 16 KB
 constexpr int kF32Stage = kF32A + kF32B;
@@ -77,7 +81,9 @@ constexpr int kBfStage = 2 * kBfA + 2 * kBfB;       // 32 KB
 static_assert(kBfA == kBfB, "each lo slice sits kBfA bytes after its hi slice");
 constexpr int kAccCols = kBN;
 constexpr int kHalf = kBN / 2;
-constexpr int kSmemBytes = kF32Stages * kF32Stage + kBfStages * kBfStage + 1024 + 512;
+template <bool FP16>
+constexpr int smem_bytes() { return kF32Stages * kF32Stage + bf_stages<FP16>() * kBfStage + 1024 + 512; }
+static_assert(smem_bytes<true>() <= 232448, "shared memory per CTA");
 // k-blocks per accumulator: bf16x3 promotes every 128 values of K, fp16x3 every 64 (as the pair kernels do)
 template <bool FP16>
 constexpr int chunk_kb() { return FP16 ? 64 / kBK : kChunkKB; }
@@ -85,8 +91,8 @@ constexpr int chunk_kb() { return FP16 ? 64 / kBK : kChunkKB; }
 struct CtlF {
     uint64_t f32_full[kF32Stages];
     uint64_t f32_empty[kF32Stages];
-    uint64_t bf_full[kBfStages];     // leader: its converter warps arrive; the peer's deliver 16 bytes each
-    uint64_t bf_empty[kBfStages];    // both: leader's commit
+    uint64_t bf_full[kBfStagesMax];  // leader: its converter warps arrive; the peer's deliver 16 bytes each
+    uint64_t bf_empty[kBfStagesMax]; // both: leader's commit
     uint64_t tmem_full[2];
     uint64_t tmem_empty[2];
     uint64_t drain;
@@ -173,11 +179,11 @@ __device__ __forceinline__ void split8_f16(const float (&x)[8], int e, uint4& hi
     for (int j = 0; j < 4; ++j) {
         const float x0 = mul ? x[2 * j] * s : ldexpf(x[2 * j], -e);
         const float x1 = mul ? x[2 * j + 1] * s : ldexpf(x[2 * j + 1], -e);
-        const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
-        const __half l0 = __float2half_rn((x0 - __half2float(h0)) * 2048.0f);
-        const __half l1 = __float2half_rn((x1 - __half2float(h1)) * 2048.0f);
-        h[j] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-        l[j] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+        const __half2 hh = __floats2half2_rn(x0, x1);   // low half: x0
+        const float2 hf = __half22float2(hh);
+        const __half2 ll = __floats2half2_rn((x0 - hf.x) * 2048.0f, (x1 - hf.y) * 2048.0f);
+        h[j] = *reinterpret_cast<const uint32_t*>(&hh);
+        l[j] = *reinterpret_cast<const uint32_t*>(&ll);
     }
     hi = make_uint4(h[0], h[1], h[2], h[3]);
     lo = make_uint4(l[0], l[1], l[2], l[3]);
@@ -196,6 +202,7 @@ template <bool FP16>
 __global__ void __launch_bounds__(kThreads, 1)
     k_tc_fused(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, KParamsF p) {
     constexpr int kChunk = chunk_kb<FP16>();
+    constexpr int kBfStages = bf_stages<FP16>();
     constexpr uint32_t kIdesc = idesc_f16(2 * kBM, kBN, !FP16);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -593,7 +600,8 @@ int launch_tc_fused(const float* A, long lda, const float* B, long ldb, int M, i
             return (int)cudaErrorInvalidValue;
     }
     auto kern = fp16 ? k_tc_fused<true> : k_tc_fused<false>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    const int smem = fp16 ? smem_bytes<true>() : smem_bytes<false>();
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return (int)e;
     KParamsF p;
     p.M = M;
@@ -626,7 +634,7 @@ int launch_tc_fused(const float* A, long lda, const float* B, long ldb, int M, i
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = (cudaStream_t)stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
