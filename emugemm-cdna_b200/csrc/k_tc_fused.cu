@@ -169,24 +169,32 @@ __device__ __forceinline__ void split8(const float (&x)[8], uint4& hi, uint4& lo
     lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-// The same, fp16 slices of x * 2^-e: hi = RNE_f16(x'), lo = RNE_f16((x' - hi) * 2048), the rule of the split pass.
-__device__ __forceinline__ void split8_f16(const float (&x)[8], int e, uint4& hi, uint4& lo) {
-    // x * 2^-e equals ldexpf(x, -e) (one correctly rounded result) when 2^-e is a normal float
-    const bool mul = e >= -127 && e <= 126;
-    const float s = __int_as_float((127 - (mul ? e : 0)) << 23);
+// The same, fp16 slices of x' = x * 2^-e: hi = RNE_f16(x'), lo = RNE_f16((x' - hi) * 2048), the rule of the split
+// pass. x * 2^-e is one multiply by the normal float 2^-e, which equals ldexpf(x, -e) (both one correctly rounded
+// result); only an item whose 2^-e is not a normal float (a row or column of values below about 2^-112) takes ldexpf.
+__device__ __forceinline__ void split8_f16_scaled(const float (&xs)[8], uint4& hi, uint4& lo) {
     uint32_t h[4], l[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        const float x0 = mul ? x[2 * j] * s : ldexpf(x[2 * j], -e);
-        const float x1 = mul ? x[2 * j + 1] * s : ldexpf(x[2 * j + 1], -e);
-        const __half2 hh = __floats2half2_rn(x0, x1);   // low half: x0
+        const __half2 hh = __floats2half2_rn(xs[2 * j], xs[2 * j + 1]);   // low half: the lower k
         const float2 hf = __half22float2(hh);
-        const __half2 ll = __floats2half2_rn((x0 - hf.x) * 2048.0f, (x1 - hf.y) * 2048.0f);
+        const __half2 ll = __floats2half2_rn((xs[2 * j] - hf.x) * 2048.0f, (xs[2 * j + 1] - hf.y) * 2048.0f);
         h[j] = *reinterpret_cast<const uint32_t*>(&hh);
         l[j] = *reinterpret_cast<const uint32_t*>(&ll);
     }
     hi = make_uint4(h[0], h[1], h[2], h[3]);
     lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+__device__ __forceinline__ void split8_f16(float (&x)[8], int e, uint4& hi, uint4& lo) {
+    if (e >= -127 && e <= 126) {
+        const float sc = __int_as_float((127 - e) << 23);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[j] *= sc;
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[j] = ldexpf(x[j], -e);
+    }
+    split8_f16_scaled(x, hi, lo);
 }
 
 // x * 2^e rounded once to float, for the fp16x3 store of a row whose 2^e is not a normal float (as in k_tc_gemm2.cu)
