@@ -396,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t lead_slot = mapa_shared(smem_u32(&ctl->sig_dst[cw][0]), 0);
             const uint32_t sig_src = smem_u32(&ctl->sig_src[0]);
             constexpr int kPer = (1024 + kConvThreads - 1) / kConvThreads;   // items per thread and k-block
-            constexpr int kBatch = FP16 ? 2 : 3;                             // items loaded before any is stored
+            constexpr int kBatch = 3;                                        // items loaded before any is stored
             long it = 0;
             bool ok = true;
             for (int u = pair; u < num_units && ok; u += num_pairs) {
