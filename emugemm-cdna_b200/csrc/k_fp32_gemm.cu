@@ -326,27 +326,28 @@ __global__ void __launch_bounds__(kThr) k_fp32_gemm_cp(Params p) {
 }
 
 // 16 x 32 tiles for products whose output has too few elements to give every SM a 32 x 32 tile (C3: M = N = 256,
-// 65536 chains, c = 1). 64 threads: two warps, each a 16 x 16 block of the tile; a thread runs a 4 x 2 block of chains,
-// rows ty, ty + 4, ty + 8, ty + 12 of the warp's 16 (ty = lane / 8) and columns 2 tx, 2 tx + 1 of its 16 (tx = lane % 8).
-// The 128 CTAs put one warp on 256 of the 592 SM sub-partitions, each with 8 independent chains: enough to issue an FMA
-// every cycle through the 4-cycle FMA latency.
+// 65536 chains, c = 1). 128 threads, each running a 2 x 2 block of chains, so the CTA grid covers 128 SMs (the 32
+// tile: 64) with one warp per SM sub-partition.
 //
-// Shared-memory delivery: per four k a thread reads each of its four rows of A as one float4 along k, and the eight lanes
-// of a row quad read the same address (a broadcast; the four quads sit in four different bank groups, rows being 68
-// floats apart); per k it reads its two columns of B as a float2, the four row quads of the warp reading the same 64
-// bytes. That is two 128-byte wavefronts per warp for every 8 FMAs per thread. (The previous form, 2 x 2 chains per
-// thread and 128 threads, needed one wavefront per 2 FMAs and ran the FMA pipe at 23 %.) The stage is 64 deep. Same
-// chains (k ascending per element), same FP64 folds and the same VEC conditions as k_fp32_gemm_cp.
+// What bounds every FP32 SIMT tile here is shared-memory delivery, not the FMA pipe: an SM serves one 128-byte
+// wavefront per clock (one float per lane of a warp) while it can issue four FFMA warp-instructions, and a thread
+// with a TM x TN block of chains needs TM + TN floats per k for TM * TN FMAs. The FMA pipe can therefore be at most
+// TM * TN / (TM + TN) / 4 busy: 0.25 for 2 x 2, 0.5 for 4 x 4, 1 for 8 x 8 (ncu: the 1 x 4 form of this kernel
+// ran with the L1/shared pipe 97 % busy and the FMA pipe at 24 %). Few output elements force small blocks.
+//
+// Per four k a thread reads each of its two rows of A as one float4 along k (rows padded by 4 floats) and, per k,
+// its two columns of B as one float2: 16 wavefronts per 16 FMAs per warp. The stage is 64 deep. Same chains (k
+// ascending per element), same FP64 folds and the same VEC conditions as k_fp32_gemm_cp.
 template <int STAGES>
-__global__ void __launch_bounds__(64) k_fp32_narrow(Params p) {
+__global__ void __launch_bounds__(128) k_fp32_narrow(Params p) {
     constexpr int BK = 64, BKP = BK + 4, TR = 16, TC = 32;
-    constexpr int A_CH = TR * BK / 4, CH = A_CH + BK * TC / 4, CPT = CH / 64;
-    static_assert(CH % 64 == 0, "copies per thread");
+    constexpr int A_CH = TR * BK / 4, CH = A_CH + BK * TC / 4, CPT = CH / 128;
+    static_assert(CH % 128 == 0, "copies per thread");
     extern __shared__ __align__(16) float narrow_smem[];
     auto As = reinterpret_cast<float (*)[TR][BKP]>(narrow_smem);                       // [stage][m][k], rows padded
     auto Bs = reinterpret_cast<float (*)[BK][TC]>(narrow_smem + STAGES * TR * BKP);    // [stage][k][n]
-    const int tid = threadIdx.x, lane = tid & 31, wn = (tid >> 5) * 16;
-    const int tx = lane & 7, ty = lane >> 3;
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;               // rows 2*ty, 2*ty+1; columns 2*tx, 2*tx+1
     const int m0 = blockIdx.y * TR, n0 = blockIdx.x * TC;
     const int g = blockIdx.z;
     const int c_first = g * p.cpg;
@@ -362,7 +363,7 @@ __global__ void __launch_bounds__(64) k_fp32_narrow(Params p) {
             const long k = kbeg + kt * BK;
 #pragma unroll
             for (int c = 0; c < CPT; ++c) {
-                const int f = tid + c * 64;
+                const int f = tid + c * 128;
                 if (f < A_CH) {
                     const int r = f / (BK / 4), q = f % (BK / 4);
                     const int m = m0 + r;
@@ -381,9 +382,7 @@ __global__ void __launch_bounds__(64) k_fp32_narrow(Params p) {
                 }
             }
         };
-        float acc[4][2];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = 0.f;
+        float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
         for (int kt = 0; kt < STAGES - 1; ++kt) {
             if (kt < nkb) issue(kt);
             cp_async_commit();
@@ -396,18 +395,17 @@ __global__ void __launch_bounds__(64) k_fp32_narrow(Params p) {
             const int st = (int)(kt % STAGES);
 #pragma unroll
             for (int k4 = 0; k4 < BK / 4; ++k4) {
-                float4 a[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) a[i] = *reinterpret_cast<const float4*>(&As[st][ty + 4 * i][k4 * 4]);
+                const float4 a0 = *reinterpret_cast<const float4*>(&As[st][2 * ty][k4 * 4]);
+                const float4 a1 = *reinterpret_cast<const float4*>(&As[st][2 * ty + 1][k4 * 4]);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    const float2 b = *reinterpret_cast<const float2*>(&Bs[st][k4 * 4 + kk][wn + tx * 2]);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float x = kk == 0 ? a[i].x : kk == 1 ? a[i].y : kk == 2 ? a[i].z : a[i].w;
-                        acc[i][0] = __fmaf_rn(x, b.x, acc[i][0]);
-                        acc[i][1] = __fmaf_rn(x, b.y, acc[i][1]);
-                    }
+                    const float2 b = *reinterpret_cast<const float2*>(&Bs[st][k4 * 4 + kk][tx * 2]);
+                    const float x0 = kk == 0 ? a0.x : kk == 1 ? a0.y : kk == 2 ? a0.z : a0.w;
+                    const float x1 = kk == 0 ? a1.x : kk == 1 ? a1.y : kk == 2 ? a1.z : a1.w;
+                    acc[0][0] = __fmaf_rn(x0, b.x, acc[0][0]);
+                    acc[0][1] = __fmaf_rn(x0, b.y, acc[0][1]);
+                    acc[1][0] = __fmaf_rn(x1, b.x, acc[1][0]);
+                    acc[1][1] = __fmaf_rn(x1, b.y, acc[1][1]);
                 }
             }
             __syncthreads();
@@ -415,12 +413,12 @@ __global__ void __launch_bounds__(64) k_fp32_narrow(Params p) {
         cp_async_wait<0>();
         const bool first = (ci == c_first), last = (ci == c_last - 1);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int m = m0 + ty + 4 * i;
+        for (int i = 0; i < 2; ++i) {
+            const int m = m0 + 2 * ty + i;
             if (m >= p.M) continue;
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-                const int n = n0 + wn + tx * 2 + j;
+                const int n = n0 + tx * 2 + j;
                 if (n >= p.N) continue;
                 const size_t wi = (size_t)m * p.N + n;
                 const double s = first ? (double)acc[i][j] : Wg[wi] + (double)acc[i][j];
@@ -555,12 +553,12 @@ int launch_fp32_gemm(const Fp32GemmArgs& a, void* stream) {
         if (vec) k_fp32_gemm_cp<32, 8><<<grid, kThr, 0, st>>>(p);
         else launch_cfg<32, 2, false>(p, grid, st);
     } else if (s.bm == 16) {
-        constexpr int kNarrowStages = 4;   // 50 KB
+        constexpr int kNarrowStages = 4;   // 50 KB: four CTAs per SM
         const int smem = kNarrowStages * (16 * 68 + 64 * 32) * (int)sizeof(float);
         cudaError_t e = cudaFuncSetAttribute(k_fp32_narrow<kNarrowStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              smem);
         if (e != cudaSuccess) return (int)e;
-        k_fp32_narrow<kNarrowStages><<<grid, 64, smem, st>>>(p);
+        k_fp32_narrow<kNarrowStages><<<grid, 128, smem, st>>>(p);
     } else {
         return (int)cudaErrorInvalidValue;
     }
