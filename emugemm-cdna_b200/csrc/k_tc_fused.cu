@@ -405,6 +405,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tile_coords_f(t, p.num_m2, p.num_n, mb2, nb);
                 const int a_row0 = mb2 * 2 * kBM + (int)rank * kBM;   // this CTA's first row of A
                 const int b_col0 = nb * kBN + (int)rank * kBNH;       // and first column of B
+                // fp16x3: a thread converts the same items (row or column, k-group) in every k-block of the unit, so
+                // their scale exponents are loaded once per unit (a load per item and k-block stalled the converters)
+                int exq[kPer];
+#pragma unroll
+                for (int i = 0; i < kPer; ++i) {
+                    const int item = ct + i * kConvThreads;
+                    int e = 0;
+                    if (FP16 && item < 1024) {
+                        if (item < 512) {
+                            const int m = a_row0 + (item >> 2);
+                            e = m < p.M ? __ldg(p.row_exp + m) : 0;
+                        } else {
+                            const int n = b_col0 + ((item - 512) & (kBNH - 1));
+                            e = n < p.N ? __ldg(p.col_exp + n) : 0;
+                        }
+                    }
+                    exq[i] = e;
+                }
                 for (int kb = kbb; kb < kbe; ++kb, ++it) {
                     const int s = (int)(it % kF32Stages);
                     const uint32_t ph = (uint32_t)((it / kF32Stages) & 1);
@@ -436,14 +454,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 x[i][0] = u.x; x[i][1] = u.y; x[i][2] = u.z; x[i][3] = u.w;
                                 x[i][4] = v.x; x[i][5] = v.y; x[i][6] = v.z; x[i][7] = v.w;
                                 dst[i] = sw64(r, g);
-                                ex[i] = (FP16 && a_row0 + r < p.M) ? __ldg(p.row_exp + a_row0 + r) : 0;
+                                ex[i] = exq[i0 + i];
                             } else {
                                 const int i2 = item - 512;
                                 const int r = i2 & (kBNH - 1), g = i2 >> 7;   // column n of this CTA's B, k-group
 #pragma unroll
                                 for (int j = 0; j < 8; ++j) x[i][j] = fb[(8 * g + j) * kBNH + r];
                                 dst[i] = (uint32_t)(2 * kBfA) + sw64(r, g);
-                                ex[i] = (FP16 && b_col0 + r < p.N) ? __ldg(p.col_exp + b_col0 + r) : 0;
+                                ex[i] = exq[i0 + i];
                             }
                         }
 #pragma unroll
