@@ -571,12 +571,22 @@ emugemm_status_t emugemm_sgemm_rows(emugemm_handle_t handle, int M, int N, long 
     // announces every panel, and each other rank pulls panel j as a pitched copy over NVLink from its parent. NCCL:
     // panel j contiguous at stage + K * n0 (a broadcast buffer must be contiguous), packed on the root.
     if (use_p2p && is_root && K > 0 && N > 0) {
+        // the first panel alone first (a small pitched copy), so that the other ranks start without waiting for all
+        // of B; then B in one piece, which writes the first panel's bytes again with the same values
+        const bool first_alone = pan.size() > 1;
+        if (first_alone) {
+            const long w0 = pan[0].second - pan[0].first;
+            e = (int)cudaMemcpy2DAsync(stage, (size_t)N * 4, B, (size_t)ldb * 4, (size_t)w0 * 4, (size_t)K,
+                                       cudaMemcpyDeviceToDevice, m->stream);
+            if (!e) e = emu::set_flag(m->flags + emu::kFlagArrive + 16 * buf, seq, m->stream);
+            if (e) return emu::from_cuda(e);
+        }
         e = ldb == N ? (int)cudaMemcpyAsync(stage, B, (size_t)K * N * 4, cudaMemcpyDeviceToDevice, m->stream)
                      : (int)cudaMemcpy2DAsync(stage, (size_t)N * 4, B, (size_t)ldb * 4, (size_t)N * 4, (size_t)K,
                                               cudaMemcpyDeviceToDevice, m->stream);
         if (!e) {
             emu::PeerFlags f{};
-            for (size_t j = 0; j < pan.size(); ++j) f.p[j] = m->flags + emu::kFlagArrive + 16 * buf + j;
+            for (size_t j = first_alone ? 1 : 0; j < pan.size(); ++j) f.p[j] = m->flags + emu::kFlagArrive + 16 * buf + j;
             emu::k_set_flags<<<1, 32, 0, m->stream>>>(f, (int)pan.size(), seq);
             emu::count_launch();
             e = (int)cudaGetLastError();
