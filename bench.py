@@ -68,6 +68,7 @@ def parse():
     ap.add_argument("--no-ksplit", action="store_true", help="skip the K-split sub-record of the square workload")
     ap.add_argument("--no-check", action="store_true", help="skip the correctness check after the timed region")
     ap.add_argument("--no-sustained", action="store_true", help="skip the 2 s sustained-clock run after a short one")
+    ap.add_argument("--no-clocks", action="store_true", help="no nvidia-smi clock sampling during the timed region")
     return ap.parse_args()
 
 
@@ -518,7 +519,7 @@ def ours(args) -> None:
     # One sampler process, on rank 0, for every GPU of the job. It is started (and has delivered its first sample)
     # before the barrier, so that every rank leaves the barrier and starts its clock together: a rank that starts
     # timing while another still waits for its sampler measures that wait inside its first collective.
-    with ClockSampler(range(world) if world > 1 else [local], enabled=(rank == 0)) as clk:
+    with ClockSampler(range(world) if world > 1 else [local], enabled=(rank == 0 and not args.no_clocks)) as clk:
         torch.cuda.synchronize()
         if dist is not None:
             dist.barrier()
