@@ -602,7 +602,7 @@ def ours(args) -> None:
     # dominant kernel: the tensor-core 3-product GEMM (3 * 2 * m * n * k tensor FLOPs per rank and step), the FP32
     # SIMT GEMM (2 * m * n * k) for the chunked workload, the skinny probe products (4 * P * K * (M + N)) for rho
     if wl == "chunked" or (wl == "longk" and args.scheme == "native"):
-        kern_key, kern_name, bound = "fp32_gemm", "k_fp32_gemm / k_fp32_gemm_cp / k_fp32_narrow (+ k_reduce_f64)", "fp32"
+        kern_key, kern_name, bound = "fp32_gemm", "k_fp32_gemm / k_fp32_gemm_cp / k_fp32_pipe / k_fp32_pipe_cp (+ k_reduce_f64)", "fp32"
         rank_tensor_flop = 2.0 * m_loc * N * k_loc
     elif wl == "rho":
         kern_key, kern_name, bound = "rho", "rho probe (k_omega, k_skinny_cp x2, k_combine[_sq], k_final)", "fp32"

@@ -393,10 +393,10 @@ static emugemm_status_t run_tc(Handle* h, int M, int N, long K, const float* A, 
     return from_cuda(launch_reduce_f64(t.part64, t.splits, M, N, (long)M * N, C, ldc, C64, ldc64, h->stream));
 }
 
-// FP32 SIMT tile code for a shape: `forced` (the handle's EMUGEMM_ATTR_FP32_TILE: 16, 32, 64 or 128; 0 = choose) wins,
+// FP32 SIMT tile code for a shape: `forced` (the handle's EMUGEMM_ATTR_FP32_TILE, a code of fp32_tile_code_ok; 0 = choose) wins,
 // then the tile table's code (looked up at the chunk length), else 0 (the built-in choice of launch_fp32_gemm).
 static int fp32_tile_choice(int M, int N, long K, int chunks, int forced) {
-    if (forced == 16 || forced == 32 || forced == 64 || forced == 128) return forced;
+    if (fp32_tile_code_ok(forced)) return forced;
     return lookup_tile(M, N, K / (chunks < 1 ? 1 : chunks), 0).fp32_bm;
 }
 
@@ -418,7 +418,7 @@ static int env_tc_splitk() {
 static int env_fp32_tile() {
     const char* v = std::getenv("EMUGEMM_FP32_TILE");
     const int t = v ? std::atoi(v) : 0;
-    return (t == 16 || t == 32 || t == 64 || t == 128) ? t : 0;
+    return fp32_tile_code_ok(t) ? t : 0;
 }
 
 static emugemm_status_t run_fp32(Handle* h, int M, int N, long K, const float* A, long lda, const float* B, long ldb,
@@ -430,6 +430,7 @@ static emugemm_status_t run_fp32(Handle* h, int M, int N, long K, const float* A
     f.chunks = chunks < 1 ? 1 : chunks;
     f.num_sms = h->num_sms;
     f.bm = fp32_tile_choice(M, N, K, f.chunks, h->fp32_tile);
+    f.err = h->err_dev;
     f.ws64 = nullptr;
     size_t wsb = fp32_gemm_ws_bytes(f);
     if (wsb) {
@@ -560,8 +561,7 @@ emugemm_status_t emugemm_set_attr(emugemm_handle_t handle, int attr, long value)
             h->tc_splitk = (int)value;
             return EMUGEMM_STATUS_SUCCESS;
         case EMUGEMM_ATTR_FP32_TILE:
-            if (value != 0 && value != 16 && value != 32 && value != 64 && value != 128)
-                return EMUGEMM_STATUS_INVALID_VALUE;
+            if (value != 0 && !emu::fp32_tile_code_ok(value)) return EMUGEMM_STATUS_INVALID_VALUE;
             h->fp32_tile = (int)value;
             return EMUGEMM_STATUS_SUCCESS;
         case EMUGEMM_ATTR_ROWS_PANELS:

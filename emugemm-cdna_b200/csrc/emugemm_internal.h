@@ -50,7 +50,7 @@ struct TileChoice {
     int tc_variant;     // tensor-core kernel: 0 = built-in choice, 1 = single-CTA, 2 = CTA pair (cta_group::2),
                         // 3 = CTA pair with the split fused in, 4 = CTA pair with A split into TMEM in the
                         // kernel and B pre-split (3 and 4: bf16x3 only)
-    int fp32_bm;        // FP32 SIMT tile: 0 = auto, 32, 64 or 128 (square), 16 (16 x 32, k_fp32_narrow)
+    int fp32_bm;        // FP32 SIMT tile: 0 = auto, else a code of fp32_tile_code_ok
 };
 TileChoice lookup_tile(int M, int N, long K, int dtype /*0 fp32, 1 bf16, 2 fp16*/);
 
@@ -64,6 +64,7 @@ enum : unsigned {
     kErrTimeoutConvert = 8u,
     kErrTmemAlloc = 16u,
     kErrTimeoutComm = 32u,          // a wait for another GPU's flag in emugemm_sgemm_rows gave up
+    kErrTimeoutFp32 = 64u,          // a wait for a TMA k-block in the FP32 SIMT kernel gave up
 };
 
 // Workspace slots of a handle (grow-only, freed with the handle).
@@ -261,8 +262,14 @@ struct Fp32GemmArgs {
     int chunks;
     double* ws64;                // G x M x N FP64 partials when G > 1
     int num_sms;
-    int bm;                      // 0 = auto, else a tile code (16, 32, 64, 128)
+    int bm;                      // 0 = auto, else a tile code (fp32_tile_code_ok)
+    unsigned* err = nullptr;     // device error word for the bounded waits (may be null)
 };
+// FP32 SIMT tile codes: 32, 64, 128 (square tiles), 16 and 3264 (16 x 32 and 32 x 64, the register-pipelined
+// k_fp32_pipe).
+inline bool fp32_tile_code_ok(long t) {
+    return t == 16 || t == 32 || t == 64 || t == 128 || t == 3264;
+}
 int fp32_gemm_groups(const Fp32GemmArgs& a);   // G chosen for this shape
 size_t fp32_gemm_ws_bytes(const Fp32GemmArgs& a);
 int launch_fp32_gemm(const Fp32GemmArgs& a, void* stream);

@@ -105,7 +105,7 @@ TileChoice lookup_tile(int M, int N, long K, int dtype) {
     if (M <= 0 || N <= 0 || K <= 0) return t;
     int v = lookup_raw(M, N, K, dtype);
     if (dtype == 0) {
-        if (v == 16 || v == 32 || v == 64 || v == 128) t.fp32_bm = v;
+        if (fp32_tile_code_ok(v)) t.fp32_bm = v;
     } else {
         if (v >= 1 && v <= 4) t.tc_variant = v;
     }

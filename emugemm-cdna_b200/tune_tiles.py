@@ -4,7 +4,7 @@ bench/gen_tune_table.cpp: offline, resumable, shardable, header written once und
 For every (M, N, K, dtype) of the grid it times the candidate kernels through the C ABI and appends one row
     arch,cuda_version,M,N,K,dtype,tile,best_ms,default_ms,gain
 where `tile` is the winner (bf16/fp16: 1 = single-CTA, 2 = CTA pair, 3 = fused split, 4 = A split into TMEM;
-fp32: SIMT tile 16 (16 x 32), 32, 64 or 128),
+fp32: SIMT tile 16 (16 x 32), 32, 64, 128 or 3264 (32 x 64)),
 `default_ms` the built-in choice's time and `gain` = default_ms / best_ms. Rows already present for a key are
 skipped, so an interrupted run resumes; --shard i/n takes every n-th shape starting at i (one process per GPU).
 --dtypes restricts the grid; --replace first drops the table's rows of those dtypes, so that they are measured

@@ -246,7 +246,7 @@ emugemm_status_t emugemm_noalloc_sync(void* stream);
 
 /* Per-handle kernel choices (no emugemm-cdna counterpart; there rocBLAS picks the kernel). Every handle starts
    from the process environment, read when the handle is created: EMUGEMM_TC_KERNEL ("single", "pair", "fused",
-   "fusea"), EMUGEMM_TC_SPLITK (a count >= 1) and EMUGEMM_FP32_TILE (16, 32, 64, 128); unset means 0, the tile
+   "fusea"), EMUGEMM_TC_SPLITK (a count >= 1) and EMUGEMM_FP32_TILE (16, 32, 64, 128, 3264); unset means 0, the tile
    table's choice and then the built-in one. A handle's setting changes only that handle's later calls. The K split
    count changes the order of the FP64 partial sums, so two handles with different settings may differ in the last
    bits of C; each setting on its own is deterministic. */
@@ -254,7 +254,8 @@ typedef enum {
     EMUGEMM_ATTR_TC_KERNEL = 0,   /* 0 auto, 1 single CTA, 2 CTA pair, 3 pair with the split fused in,
                                      4 pair with A split into TMEM (3, 4: bf16x3 only; fp16x3 runs 2) */
     EMUGEMM_ATTR_TC_SPLITK = 1,   /* 0 auto, n >= 1: K splits of the CTA-pair kernels */
-    EMUGEMM_ATTR_FP32_TILE = 2,   /* 0 auto, 16 (16 x 32), 32, 64, 128: tile of the FP32 SIMT kernel */
+    EMUGEMM_ATTR_FP32_TILE = 2,   /* 0 auto, 16 (16 x 32), 32, 64, 128, 3264 (32 x 64): tile of the FP32 SIMT
+                                     kernel */
     EMUGEMM_ATTR_ROWS_PANELS = 3, /* emugemm_sgemm_rows: 0 = the modelled panel schedule, 1..16 = that many equal
                                      column panels of B (the same value on every rank) */
     EMUGEMM_ATTR_COMM_SMS = 4,    /* emugemm_sgemm_rows: SMs (even, 0..64) its tensor-core GEMMs leave free for the

@@ -111,14 +111,17 @@ def test_chunked_fp32_bitexact(cuda, handle, shape, chunks):
     assert np.array_equal(C.cpu().numpy(), want.astype(np.float32))
 
 
-@pytest.mark.parametrize("tile", [16, 32, 64, 128])
+@pytest.mark.parametrize("tile", [16, 3264, 32, 64, 128])
 @pytest.mark.parametrize("shape,chunks", [((256, 256, 8192), 1), ((256, 256, 8192), 4), ((100, 36, 1000), 3),
-                                          ((33, 20, 260), 1), ((64, 130, 500), 2)])
+                                          ((33, 20, 260), 1), ((64, 130, 500), 2), ((64, 64, 1000), 2),
+                                          ((48, 96, 4104), 3)])
 def test_fp32_tiles_bitexact(cuda, handle, tile, shape, chunks):
-    """Every FP32 SIMT tile (EMUGEMM_ATTR_FP32_TILE: 16 = the 16 x 32 narrow kernel, 32 / 64 / 128 square) runs the same
-    chains and FP64 folds: bit-exact against the oracle with the group split the library reports. Ragged M, N not
-    a multiple of 32, chunk lengths not a multiple of 64; N = 130 is not a multiple of 4, so the narrow kernel falls
-    back to the 32 tile there."""
+    """Every FP32 SIMT tile (EMUGEMM_ATTR_FP32_TILE: 16 / 3264 = the 16 x 32 and 32 x 64 tiles of the register-pipelined
+    kernel, fed by cp.async and by TMA; 32 / 64 / 128 square) runs the same chains and FP64 folds: bit-exact against the oracle
+    with the group split the library reports. Ragged M, N not a multiple of 32, chunk lengths not a multiple of 64
+    (chunks that end inside a k-block: the TMA-fed kernel must stop there although the block holds the next chunk's
+    values); N = 130 is not a multiple of 4 and K = 1000 in 3 chunks gives chunk lengths that are not, so the kernels
+    that copy 16-byte pieces fall back to the 32 tile there."""
     torch = cuda
     handle.set_kernels(fp32_tile=tile)
     M, N, K = shape
