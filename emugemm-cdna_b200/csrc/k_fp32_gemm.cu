@@ -337,9 +337,10 @@ __global__ void __launch_bounds__(kThr) k_fp32_gemm_cp(Params p) {
 // Register-pipelined chains for products with few chains per SM sub-partition (C3: M = N = 256 holds 65536 chains,
 // one warp of 2 x 2 chains per sub-partition of 128 SMs). BM x BN tile, TM x TN chains per thread, (BM/TM) x (BN/TN)
 // threads, a STAGES-deep ring of 64-deep k-blocks. Two loaders, two kernels with the same k-loop:
-// - k_fp32_pipe (32 x 64 tiles, 4 x 4 chains): TMA. One thread issues a k-block (two 32-deep boxes of A's rows with
-//   the 128-byte swizzle, one 64-row box of B) completing on the stage's mbarrier. It runs the c = 4 and c = 16 products
-//   at 28.9 and 34.4 TFLOP/s against 17.5 and 29.4 for the 32 and 64 square tiles (cp.async rings).
+// - k_fp32_pipe (32 x 64 tiles with 4 x 4 chains; 128 x 128 tiles with 8 x 8): TMA. One thread issues a k-block (two
+//   32-deep boxes of A's rows with the 128-byte swizzle, one 64-row box of B) completing on the stage's mbarrier. It
+//   runs the c = 4 and c = 16 products at 28.9 and 34.4 TFLOP/s against 17.5 and 29.4 for the 32 and 64 square tiles
+//   (cp.async rings), and NATIVE 8192^3 at 51.4 against 44.5 for the register-staged 128 tile.
 // - k_fp32_pipe_cp (16 x 32 tiles, 2 x 2 chains): per-thread 16-byte cp.async copies whose source pointers are set
 //   once per chunk, A's rows padded to 68 floats. Its warp has the least slack (four chains per thread): the c = 1
 //   product runs at 14.1 TFLOP/s; the TMA form of the same tile ran at 12.2, and the earlier cp.async kernel with two
@@ -375,7 +376,14 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN)) k_fp32_pipe(const __gri
     constexpr int TX = BN / TN, TY = BM / TM;
     constexpr int A_STAGE = BM * BK, B_STAGE = BK * BN;   // floats
     constexpr uint32_t STAGE_BYTES = (A_STAGE + B_STAGE) * 4;
-    static_assert(TX % 8 == 0 && TY % 8 == 0 && (TN == 2 || TN == 4), "warp layout");
+    static_assert(TX % 8 == 0 && TY % 8 == 0 && (TN == 2 || TN == 4 || TN == 8), "warp layout");
+    constexpr int CW = TN == 8 ? BN / 2 : 4;   // TN = 8: a thread's columns come in two groups of four, BN/2 apart
+    // TN = 8 (8 x 8 chains): B is read at its use, not PF steps ahead (four k of B would be 32 more registers per
+    // fragment set); then the last PF steps of a k-block still read its B after the barrier, so a stage is refilled
+    // one k-block later (LA k-blocks in flight instead of STAGES - 1).
+    constexpr bool BJIT = TN == 8;
+    constexpr int LA = BJIT ? STAGES - 2 : STAGES - 1;
+    static_assert(LA >= 1, "k-blocks in flight");
     static_assert(PF >= 1 && STEPS % NF == 0 && STAGES >= 2, "fragment ring");
     static_assert(BM % 8 == 0 && BM <= 256 && BN * 4 % 16 == 0 && BN <= 256, "TMA boxes");
     extern __shared__ __align__(16) unsigned char pipe_raw[];
@@ -404,7 +412,7 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN)) k_fp32_pipe(const __gri
 
     struct Frag {
         float4 a[TM];
-        float b[4][TN];
+        float b[BJIT ? 1 : 4][TN];
     };
     // Step s of a k-block covers k = 4s .. 4s+3: A half s / 8, 16-byte piece s % 8 of each 128-byte row, stored at
     // piece (s % 8) ^ (row % 8). A thread's rows i*TY + ty all have row % 8 = ty % 8 (TY is a multiple of 8), so the
@@ -418,13 +426,16 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN)) k_fp32_pipe(const __gri
         for (int i = 0; i < TM; ++i) f.a[i] = *reinterpret_cast<const float4*>(a_row + i * TY * 32);
         const float* b_st = Bs + st * B_STAGE;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
+        for (int kk = 0; kk < (BJIT ? 0 : 4); ++kk) {
             if (TN == 2) {
                 const float2 v = *reinterpret_cast<const float2*>(b_st + (s * 4 + kk) * BN + tx * 2);
                 f.b[kk][0] = v.x; f.b[kk][1] = v.y;
             } else {
-                const float4 v = *reinterpret_cast<const float4*>(b_st + (s * 4 + kk) * BN + tx * 4);
-                f.b[kk][0] = v.x; f.b[kk][1] = v.y; f.b[kk][2] = v.z; f.b[kk][3] = v.w;
+#pragma unroll
+                for (int h = 0; h < TN / 4; ++h) {
+                    const float4 v = *reinterpret_cast<const float4*>(b_st + (s * 4 + kk) * BN + h * CW + tx * 4);
+                    f.b[kk][4 * h] = v.x; f.b[kk][4 * h + 1] = v.y; f.b[kk][4 * h + 2] = v.z; f.b[kk][4 * h + 3] = v.w;
+                }
             }
         }
     };
@@ -456,7 +467,7 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN)) k_fp32_pipe(const __gri
         for (int i = 0; i < TM; ++i)
 #pragma unroll
             for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
-        for (int kt = 0; kt < STAGES - 1 && kt < nkb; ++kt) issue_block(kt);
+        for (int kt = 0; kt < LA && kt < nkb; ++kt) issue_block(kt);
         wait_block(0);
         Frag fr[NF];
 #pragma unroll
@@ -464,8 +475,9 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN)) k_fp32_pipe(const __gri
         for (long kt = 0; kt < nkb; ++kt) {
             const int st = (int)((ring + kt) % STAGES);
             const bool more = kt + 1 < nkb;
-            // refills the stage of k-block kt - 1: every thread issued its last read of it before the previous barrier
-            if (kt + STAGES - 1 < nkb) issue_block(kt + STAGES - 1);
+            // refills the stage of k-block kt + LA - STAGES (kt - 1, or kt - 2 when B is read at its use): every thread
+            // issued its last read of it before the previous barrier
+            if (kt + LA < nkb) issue_block(kt + LA);
             const long left = kend - (kbeg + kt * BK);
             // one k-block; GUARD: the chunk ends inside it and only its first vs steps run (a separate copy of the
             // unrolled loop, so full k-blocks carry no per-step test)
@@ -487,11 +499,22 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN)) k_fp32_pipe(const __gri
                         const Frag& f = fr[s % NF];
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk) {
+                            float bj[TN];
+#pragma unroll
+                            for (int j = 0; j < TN; ++j) bj[j] = BJIT ? 0.f : f.b[BJIT ? 0 : kk][j];
+                            if (BJIT) {
+                                const float* b_row = Bs + st * B_STAGE + (s * 4 + kk) * BN + tx * 4;
+#pragma unroll
+                                for (int h = 0; h < TN / 4; ++h) {
+                                    const float4 v = *reinterpret_cast<const float4*>(b_row + h * CW);
+                                    bj[4 * h] = v.x; bj[4 * h + 1] = v.y; bj[4 * h + 2] = v.z; bj[4 * h + 3] = v.w;
+                                }
+                            }
 #pragma unroll
                             for (int i = 0; i < TM; ++i) {
                                 const float av = kk == 0 ? f.a[i].x : kk == 1 ? f.a[i].y : kk == 2 ? f.a[i].z : f.a[i].w;
 #pragma unroll
-                                for (int j = 0; j < TN; ++j) acc[i][j] = __fmaf_rn(av, f.b[kk][j], acc[i][j]);
+                                for (int j = 0; j < TN; ++j) acc[i][j] = __fmaf_rn(av, bj[j], acc[i][j]);
                             }
                         }
                     }
@@ -508,7 +531,7 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN)) k_fp32_pipe(const __gri
             if (m >= p.M) continue;
 #pragma unroll
             for (int j = 0; j < TN; ++j) {
-                const int n = n0 + tx * TN + j;
+                const int n = n0 + (TN == 2 ? tx * 2 + j : (j / 4) * CW + tx * 4 + (j % 4));
                 if (n >= p.N) continue;
                 const size_t wi = (size_t)m * p.N + n;
                 const double s = first ? (double)acc[i][j] : Wg[wi] + (double)acc[i][j];
@@ -722,8 +745,10 @@ static int groups_for(int ce, long tiles, int sms, int per_sm = 2) {
 // that a product with few output tiles and few chunks (M = N = 256, c = 1) spreads its FMA chains over more SMs.
 // No chain changes with the tile.
 // The 16-byte copies of the cp.async kernels need 16-byte aligned rows and K, N and the chunk length multiples of 4.
+// (TMA coordinates are 32-bit: K below 2^31 - 64.)
 static bool vec_ok(const Fp32GemmArgs& a, long kc) {
     return (a.lda % 4 == 0) && (a.ldb % 4 == 0) && (a.N % 4 == 0) && (a.K % 4 == 0) && (kc % 4 == 0) &&
+           a.K < (1L << 31) - 64 &&
            ((reinterpret_cast<uintptr_t>(a.A) & 15) == 0) && ((reinterpret_cast<uintptr_t>(a.B) & 15) == 0);
 }
 
@@ -852,8 +877,16 @@ int launch_fp32_gemm(const Fp32GemmArgs& a, void* stream) {
     tile_dims(s.bm, bm, bn);
     dim3 grid((unsigned)((a.N + bn - 1) / bn), (unsigned)((a.M + bm - 1) / bm), (unsigned)s.G);
     if (s.bm == 128) {
-        if (vec) launch_cfg<128, 8, true>(p, grid, st);
-        else launch_cfg<128, 8, false>(p, grid, st);
+        // 16-byte aligned operands: the TMA-fed k_fp32_pipe with 8 x 8 chains per thread (NATIVE 8192^3 at 51.4
+        // TFLOP/s against 44.5 for the register-staged k_fp32_gemm, and ahead at 1024^3 to 4096^3 as well); else, or
+        // without TMA, k_fp32_gemm. Same chains either way.
+        PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+        if (vec && tc_get_encode(&enc)) {
+            cudaError_t e = launch_pipe<128, 128, 8, 8, 3, 1>(a, p, grid, st);
+            if (e != cudaSuccess) return (int)e;
+        } else {
+            launch_cfg<128, 8, false>(p, grid, st);
+        }
     } else if (s.bm == 64) {
         if (vec) k_fp32_gemm_cp<64, 5><<<grid, kThr, 0, st>>>(p);
         else launch_cfg<64, 4, false>(p, grid, st);
