@@ -20,7 +20,7 @@ static const ChunkStep kRefChunkSteps[] = {{1, 1.00}, {4, 1.05}, {16, 1.95}, {64
 
 // B200 chunk cost of the FP32 kernel here (4096 x 4096 x 65536, time at c / time at c = 1): the chunk loop stays
 // inside one kernel and only adds an FP64 accumulate per chunk: 1.006 (c=4), 1.032 (16), 1.120 (64), 1.468 (256).
-static const ChunkStep kB200ChunkSteps[] = {{1, 1.00}, {4, 1.01}, {16, 1.04}, {64, 1.13}, {256, 1.48}};
+static const ChunkStep kB200ChunkSteps[] = {{1, 1.00}, {4, 1.07}, {16, 1.16}, {64, 1.26}, {256, 1.61}};
 
 static const ModelConsts kRefMI250 = {
     "ref_mi250",
@@ -43,19 +43,23 @@ static const ModelConsts kRefMI250 = {
 //            of 128-long tensor-core partial sums; the FP32 running sum adds ~2e-9 sqrt(K)
 //   fp16x3   2.1e-7 at short K growing as ~1.6e-9 sqrt(K) (8.4e-7 at K = 262144)
 //   bf16x6   runs the bf16x3 kernel (as a forced BF16X6 does in the reference), so it gets bf16x3's numbers
-// Speed ratios: 8192^3 kernel time of the FP32 SIMT kernel (the NATIVE_FP32 path, 44.5 TFLOPS) over that of
-// the tensor-core kernel (bf16x3 11.7x, fp16x3 6.7x), rounded down; hbm_bps is the split's effective rate.
+// Speed ratios: 8192^3 kernel time of the FP32 SIMT kernel (the NATIVE_FP32 path, 51.4 TFLOPS) over that of
+// the tensor-core kernel (bf16x3 10.5x, fp16x3 8.6x), rounded down; hbm_bps is the split's effective rate (5.74e12
+// B/s, rounded down); chunk costs are FP32_CHUNKED times at 4096 x 4096 x 65536 over c = 1, rounded up. The error
+// constants a_lowp and a_fp16x3 keep the fits of the earlier run (2.98e-9, 1.63e-9): the latest run's few-tile
+// products split K over the SM pairs and grew less with K (2.52e-9, 0), but products whose tiles fill the GPU are
+// not split.
 // fp16x3 scales each row of A and column of B by a power of two before splitting, so its range test only
 // excludes zero and non-finite magnitudes. The measurements and raw fits are in calibration_b200.json.
 static const ModelConsts kB200 = {
     "b200",
     /*a_fp32*/ 2.02e-8, /*a_lowp*/ 3.0e-9, /*a_fp16x3*/ 1.7e-9,
     /*floor_bf16x3*/ 4.6e-6, /*floor_fp16x3*/ 2.6e-7, /*floor_bf16x6*/ 4.6e-6,
-    /*spd_bf16x3*/ 10.0, /*spd_fp16x3*/ 6.0, /*spd_bf16x6*/ 10.0,
+    /*spd_bf16x3*/ 10.0, /*spd_fp16x3*/ 8.0, /*spd_bf16x6*/ 10.0,
     /*fp16_max*/ INFINITY, /*fp16_min*/ 0.0f,
     kB200ChunkSteps, 5, /*chunk_cost_beyond*/ 2.0,
     /*max_chunks*/ 256,
-    /*hbm_bps*/ 4.3e12, /*fp32_flops*/ 44.5e12,
+    /*hbm_bps*/ 5.7e12, /*fp32_flops*/ 51.4e12,
     /*overhead bytes per input element: native, chunked (scan), emulated (scan + split), fp16x3 (+ exponent
       scan)*/ 0.0, 4.0, 12.0, 20.0,
     /*rho_ref_coef*/ 0.64,
