@@ -42,16 +42,15 @@ struct Params {
     unsigned* err;      // the handle's error word (bounded waits of k_fp32_pipe)
 };
 
-// kBKf: values of K per shared-memory stage (16; a 64-deep stage for the 32 tile measured slower: its
-// unrolled k-loop ran at 64 registers with spills).
-template <int BM, int BN, int TM, int TN, bool VEC, int kBKf>
+// The register-staged kernel, for operands the 16-byte copies of the other kernels cannot take (rows not 16-byte
+// aligned, or K, N or the chunk length not a multiple of 4): scalar global loads staged through registers into
+// double-buffered shared memory. kBKf: values of K per shared-memory stage (16; a 64-deep stage for the 32 tile
+// measured slower: its unrolled k-loop ran at 64 registers with spills).
+template <int BM, int BN, int TM, int TN, int kBKf>
 __global__ void __launch_bounds__(kThr) k_fp32_gemm(Params p) {
     __shared__ __align__(16) float As[2][kBKf][BM];
     __shared__ __align__(16) float Bs[2][kBKf][BN];
     constexpr int HM = TM / 2, HN = TN / 2;
-    constexpr int A_F4 = BM * kBKf / 4, B_F4 = BN * kBKf / 4;   // float4s per k-block tile
-    constexpr int A_VEC = (A_F4 + kThr - 1) / kThr;             // float4 per thread (the last may be idle)
-    constexpr int B_VEC = (B_F4 + kThr - 1) / kThr;
     constexpr int A_SC = (BM * kBKf + kThr - 1) / kThr;         // scalars per thread
     constexpr int B_SC = (BN * kBKf + kThr - 1) / kThr;
     static_assert(16 * TM == BM && 16 * TN == BN, "tile shape");
@@ -66,83 +65,39 @@ __global__ void __launch_bounds__(kThr) k_fp32_gemm(Params p) {
     float acc[TM][TN];
     double* Wg = p.W ? p.W + (size_t)g * p.M * p.N : nullptr;
 
-    float ra[VEC ? A_VEC * 4 : A_SC];
-    float rb[VEC ? B_VEC * 4 : B_SC];
+    float ra[A_SC];
+    float rb[B_SC];
 
     auto load_global = [&](long kb, long kend) {
-        if (VEC) {
 #pragma unroll
-            for (int j = 0; j < A_VEC; ++j) {
-                const int f = tid + j * kThr;
-                const int row = f / (kBKf / 4), kq = f % (kBKf / 4);
-                const int m = m0 + row;
-                const long k = kb + kq * 4;
-                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (f < A_F4 && m < p.M && k < kend)
-                    v = __ldg(reinterpret_cast<const float4*>(p.A + (size_t)m * p.lda + k));
-                ra[4 * j] = v.x; ra[4 * j + 1] = v.y; ra[4 * j + 2] = v.z; ra[4 * j + 3] = v.w;
-            }
+        for (int j = 0; j < A_SC; ++j) {
+            const int f = tid + j * kThr;
+            const int row = f / kBKf, kk = f % kBKf;
+            const int m = m0 + row;
+            const long k = kb + kk;
+            ra[j] = (f < BM * kBKf && m < p.M && k < kend) ? __ldg(p.A + (size_t)m * p.lda + k) : 0.f;
+        }
 #pragma unroll
-            for (int j = 0; j < B_VEC; ++j) {
-                const int f = tid + j * kThr;
-                const int kk = f / (BN / 4), nq = f % (BN / 4);
-                const long k = kb + kk;
-                const int n = n0 + nq * 4;
-                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (f < B_F4 && k < kend && n < p.N)
-                    v = __ldg(reinterpret_cast<const float4*>(p.B + (size_t)k * p.ldb + n));
-                rb[4 * j] = v.x; rb[4 * j + 1] = v.y; rb[4 * j + 2] = v.z; rb[4 * j + 3] = v.w;
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < A_SC; ++j) {
-                const int f = tid + j * kThr;
-                const int row = f / kBKf, kk = f % kBKf;
-                const int m = m0 + row;
-                const long k = kb + kk;
-                ra[j] = (f < BM * kBKf && m < p.M && k < kend) ? __ldg(p.A + (size_t)m * p.lda + k) : 0.f;
-            }
-#pragma unroll
-            for (int j = 0; j < B_SC; ++j) {
-                const int f = tid + j * kThr;
-                const int kk = f / BN, nn = f % BN;
-                const long k = kb + kk;
-                const int n = n0 + nn;
-                rb[j] = (f < BN * kBKf && k < kend && n < p.N) ? __ldg(p.B + (size_t)k * p.ldb + n) : 0.f;
-            }
+        for (int j = 0; j < B_SC; ++j) {
+            const int f = tid + j * kThr;
+            const int kk = f / BN, nn = f % BN;
+            const long k = kb + kk;
+            const int n = n0 + nn;
+            rb[j] = (f < BN * kBKf && k < kend && n < p.N) ? __ldg(p.B + (size_t)k * p.ldb + n) : 0.f;
         }
     };
     auto store_smem = [&](int buf) {
-        if (VEC) {
 #pragma unroll
-            for (int j = 0; j < A_VEC; ++j) {
-                const int f = tid + j * kThr;
-                const int row = f / (kBKf / 4), kq = f % (kBKf / 4);
-                if (f >= A_F4) continue;
+        for (int j = 0; j < A_SC; ++j) {
+            const int f = tid + j * kThr;
+            if (f >= BM * kBKf) continue;
+            As[buf][f % kBKf][f / kBKf] = ra[j];
+        }
 #pragma unroll
-                for (int e = 0; e < 4; ++e) As[buf][kq * 4 + e][row] = ra[4 * j + e];
-            }
-#pragma unroll
-            for (int j = 0; j < B_VEC; ++j) {
-                const int f = tid + j * kThr;
-                const int kk = f / (BN / 4), nq = f % (BN / 4);
-                if (f >= B_F4) continue;
-                *reinterpret_cast<float4*>(&Bs[buf][kk][nq * 4]) =
-                    make_float4(rb[4 * j], rb[4 * j + 1], rb[4 * j + 2], rb[4 * j + 3]);
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < A_SC; ++j) {
-                const int f = tid + j * kThr;
-                if (f >= BM * kBKf) continue;
-                As[buf][f % kBKf][f / kBKf] = ra[j];
-            }
-#pragma unroll
-            for (int j = 0; j < B_SC; ++j) {
-                const int f = tid + j * kThr;
-                if (f >= BN * kBKf) continue;
-                Bs[buf][f / BN][f % BN] = rb[j];
-            }
+        for (int j = 0; j < B_SC; ++j) {
+            const int f = tid + j * kThr;
+            if (f >= BN * kBKf) continue;
+            Bs[buf][f / BN][f % BN] = rb[j];
         }
     };
 
@@ -207,12 +162,13 @@ __global__ void __launch_bounds__(kThr) k_fp32_gemm(Params p) {
 }
 
 // 32 x 32 and 64 x 64 tiles (2 x 2 / 4 x 4 chains per thread) with the operands streamed through a cp.async ring,
-// for products with few output tiles (C3: M = N = 256) and mid-size ones. (At the 128 tile the register-staged
-// k_fp32_gemm stays: the ring version measured 41.8 against 44.5 TFLOP/s at 8192^3.) A register-staged k-block of prefetch left
+// for products with few output tiles (C3: M = N = 256) and mid-size ones. (At the 128 tile a ring of this kind measured
+// 41.8 against 44.5 TFLOP/s for k_fp32_gemm at 8192^3; the TMA-fed k_fp32_pipe replaced both there, 51.4.) A
+// register-staged k-block of prefetch left
 // the global-load latency exposed on every k-block when a thread has few FMAs per loaded value; the ring keeps
 // STAGES - 1 k-blocks of 16 in flight. Shared tiles keep the global layouts (A [m][k], B [k][n]): per four k a
 // thread reads its TM rows of A as float4 along k and, per k, its TM columns of B as one vector, then runs the
-// same chains (k ascending per element) with the same FP64 folds as k_fp32_gemm. Needs the VEC conditions
+// same chains (k ascending per element) with the same FP64 folds as k_fp32_gemm. Needs the vec_ok conditions
 // (16-byte aligned rows, K, N and the chunk length multiples of 4), so no 16-byte copy straddles a bound.
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc, bool valid) {
     const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
@@ -358,7 +314,7 @@ __global__ void __launch_bounds__(kThr) k_fp32_gemm_cp(Params p) {
 // the last k-block of a chunk that ends inside K holds the next chunk's values past the chunk end: that block runs a
 // copy of the unrolled loop that stops at the chunk end (chunk lengths are multiples of 4; full k-blocks carry no
 // per-step test; cp.async fills past the chunk end with zeros). Same chains (k ascending per element), same FP64 folds
-// and the same VEC conditions as k_fp32_gemm_cp.
+// and the same vec_ok conditions as k_fp32_gemm_cp.
 struct PipeMaps {
     CUtensorMap a;   // A: x = k, y = row; box 32 x BM, 128-byte swizzle
     CUtensorMap b;   // B: x = column, y = k; box BN x 64
@@ -795,12 +751,12 @@ Shape shape_of(const Fp32GemmArgs& a) {
     return s;
 }
 
-template <int BM, int TM, bool VEC>
+template <int BM, int TM>
 void launch_cfg(const Params& p, dim3 grid, cudaStream_t st) {
-    k_fp32_gemm<BM, BM, TM, TM, VEC, 16><<<grid, kThr, 0, st>>>(p);
+    k_fp32_gemm<BM, BM, TM, TM, 16><<<grid, kThr, 0, st>>>(p);
 }
 
-// A: x = k (32-deep boxes, 128-byte swizzle), y = row; B: x = column, y = k (64-deep boxes). Needs the VEC conditions
+// A: x = k (32-deep boxes, 128-byte swizzle), y = row; B: x = column, y = k (64-deep boxes). Needs the vec_ok conditions
 // (16-byte aligned operands, leading dimensions multiples of 4), which shape_of checks before choosing these tiles.
 template <int BM, int BN, int TM, int TN, int STAGES, int PF>
 cudaError_t launch_pipe(const Fp32GemmArgs& a, const Params& p, dim3 grid, cudaStream_t st) {
@@ -885,14 +841,14 @@ int launch_fp32_gemm(const Fp32GemmArgs& a, void* stream) {
             cudaError_t e = launch_pipe<128, 128, 8, 8, 3, 1>(a, p, grid, st);
             if (e != cudaSuccess) return (int)e;
         } else {
-            launch_cfg<128, 8, false>(p, grid, st);
+            launch_cfg<128, 8>(p, grid, st);
         }
     } else if (s.bm == 64) {
         if (vec) k_fp32_gemm_cp<64, 5><<<grid, kThr, 0, st>>>(p);
-        else launch_cfg<64, 4, false>(p, grid, st);
+        else launch_cfg<64, 4>(p, grid, st);
     } else if (s.bm == 32) {
         if (vec) k_fp32_gemm_cp<32, 8><<<grid, kThr, 0, st>>>(p);
-        else launch_cfg<32, 2, false>(p, grid, st);
+        else launch_cfg<32, 2>(p, grid, st);
     } else if (s.bm == 16) {
         cudaError_t e = launch_pipe_cp<16, 32, 2, 2, 4, 3>(p, grid, st);
         if (e != cudaSuccess) return (int)e;
