@@ -29,8 +29,13 @@ __device__ __forceinline__ void split_f16(float x, uint16_t& hi, uint16_t& lo) {
     lo = __half_as_ushort(l);
 }
 
-// x * 2^-e, exact for the exponents used here (a power-of-two scale of a normal float).
-__device__ __forceinline__ float scale_pow2(float x, int e) { return ldexpf(x, -e); }
+// x * 2^-e rounded once (exact unless the result leaves the normal range). When 2^-e is itself a normal float this is
+// one multiply by it, which gives the same correctly rounded result as ldexpf(x, -e) without its range handling (the
+// split ran at 0.29 ms at 8192^2 with ldexpf on every element); other e take ldexpf.
+__device__ __forceinline__ float scale_pow2(float x, int e) {
+    if (e >= -127 && e <= 126) return x * __int_as_float((127 - e) << 23);
+    return ldexpf(x, -e);
+}
 
 __global__ void k_split_bf16_elem(const float* __restrict__ X, size_t n, uint16_t* __restrict__ hi,
                                   uint16_t* __restrict__ lo) {
