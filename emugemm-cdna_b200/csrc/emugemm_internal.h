@@ -265,8 +265,7 @@ struct Fp32GemmArgs {
     int bm;                      // 0 = auto, else a tile code (fp32_tile_code_ok)
     unsigned* err = nullptr;     // device error word for the bounded waits (may be null)
 };
-// FP32 SIMT tile codes: 32, 64, 128 (square tiles), 16 and 3264 (16 x 32 and 32 x 64, the register-pipelined
-// k_fp32_pipe).
+// FP32 SIMT tile codes: 32, 64, 128 (square tiles), 16 (16 x 32, k_fp32_pipe_cp) and 3264 (32 x 64, k_fp32_pipe).
 inline bool fp32_tile_code_ok(long t) {
     return t == 16 || t == 32 || t == 64 || t == 128 || t == 3264;
 }
