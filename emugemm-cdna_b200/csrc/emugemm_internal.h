@@ -151,6 +151,10 @@ struct ProfScope {
 
 void* ws_get(Handle* h, int slot, size_t bytes);
 void count_launch(unsigned n = 1);
+// Testing hook (emugemm_test_stall_next_launches): true for each of the next n launches of a kernel that has one (the
+// single-CTA tensor-core kernel, the TMA-fed FP32 kernel), which then gives up a 1 ms wait on a barrier nothing
+// arrives on.
+bool take_test_stall();
 
 // ---------------------------------------------------------------------------------------------------
 // api.cpp internals shared with multigpu.cpp

@@ -40,6 +40,7 @@ struct Params {
     int cpg;            // chunks per group
     int G;
     unsigned* err;      // the handle's error word (bounded waits of k_fp32_pipe)
+    int stall;          // test hook (k_fp32_pipe): after k-block 0 lands every thread waits 1 ms on a barrier nothing arrives on
 };
 
 // The register-staged kernel, for operands the 16-byte copies of the other kernels cannot take (rows not 16-byte
@@ -322,7 +323,7 @@ struct PipeMaps {
 
 template <int BM, int BN>
 constexpr int pipe_smem_bytes(int stages) {   // alignment slack, A and B stages, mbarriers
-    return 1024 + stages * (BM * 64 + 64 * BN) * 4 + stages * 8;
+    return 1024 + stages * (BM * 64 + 64 * BN) * 4 + (stages + 1) * 8;
 }
 
 template <int BM, int BN, int TM, int TN, int STAGES, int PF>
@@ -357,8 +358,10 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN)) k_fp32_pipe(const __gri
     const int c_first = g * p.cpg;
     const int c_last = min(p.ce, c_first + p.cpg);
     double* Wg = p.W ? p.W + (size_t)g * p.M * p.N : nullptr;
+    uint64_t* const never = full + STAGES;   // the test hook's barrier: nothing arrives on it
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) dev::mbar_init(&full[s], 1);
+        dev::mbar_init(never, 1);
         abort_flag = 0;
         dev::fence_mbar_init();
         dev::prefetch_tmap(&maps.a);
@@ -397,14 +400,16 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN)) k_fp32_pipe(const __gri
     };
     long ring = 0;   // ring index of the current chunk's k-block 0 (k-blocks run through the stages in order)
     bool ok = true;  // false after a wait gave up: the kernel runs on over whatever the ring holds, and reports
+    long issued = 0;  // thread 0: k-blocks issued (none after one of its own waits gave up)
 
     for (int ci = c_first; ci < c_last; ++ci) {
         const long kbeg = (long)ci * p.kc;
         const long kend = min(p.K, kbeg + p.kc);
         const long nkb = (kend - kbeg + BK - 1) / BK;
         auto issue_block = [&](long kt) {   // by thread 0, k-blocks in order
-            if (tid == 0) {
+            if (tid == 0 && ok) {   // thread 0 waited for every earlier k-block of this stage itself
                 const long q = ring + kt;
+                issued = q + 1;
                 const int st = (int)(q % STAGES);
                 const int k = (int)(kbeg + kt * BK);
                 dev::mbar_arrive_expect_tx(&full[st], STAGE_BYTES);
@@ -425,6 +430,9 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN)) k_fp32_pipe(const __gri
             for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
         for (int kt = 0; kt < LA && kt < nkb; ++kt) issue_block(kt);
         wait_block(0);
+        // test hook: with the first k-blocks issued, every thread gives up a 1 ms wait on a barrier nothing arrives on
+        if (p.stall && ring == 0 && !dev::mbar_wait_for(never, 0, &abort_flag, p.err, kErrTimeoutFp32, 1000000ull))
+            ok = false;
         Frag fr[NF];
 #pragma unroll
         for (int s = 0; s < PF; ++s) load_frag(fr[s], (int)(ring % STAGES), s);
@@ -500,11 +508,12 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN)) k_fp32_pipe(const __gri
             }
         }
     }
-    // After a wait gave up, the loads still in flight land before the CTA's shared memory is released: thread 0
-    // waits (bounded, ignoring the abort flag) for the last k-block issued into each stage.
+    // After a wait gave up, no k-block is issued any more, and the loads still in flight land before the CTA's shared
+    // memory is released: thread 0 waits (bounded, ignoring the abort flag) for the last k-block issued into each
+    // stage.
     if (!ok && tid == 0) {
         int no_abort = 0;
-        for (long q = ring > STAGES ? ring - STAGES : 0; q < ring; ++q)
+        for (long q = issued > STAGES ? issued - STAGES : 0; q < issued; ++q)
             dev::mbar_wait(&full[q % STAGES], (uint32_t)((q / STAGES) & 1), &no_abort, nullptr, 0);
     }
 }
@@ -787,7 +796,9 @@ cudaError_t launch_pipe(const Fp32GemmArgs& a, const Params& p, dim3 grid, cudaS
     auto kern = k_fp32_pipe<BM, BN, TM, TN, STAGES, PF>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    kern<<<grid, (BM / TM) * (BN / TN), smem, st>>>(maps, p);
+    Params q = p;
+    q.stall = take_test_stall() ? 1 : 0;
+    kern<<<grid, (BM / TM) * (BN / TN), smem, st>>>(maps, q);
     return cudaSuccess;
 }
 
@@ -826,6 +837,7 @@ int launch_fp32_gemm(const Fp32GemmArgs& a, void* stream) {
     p.M = a.M; p.N = a.N; p.K = a.K;
     p.kc = s.kc; p.ce = s.ce; p.cpg = s.cpg; p.G = s.G;
     p.err = a.err;
+    p.stall = 0;
     if ((s.G > 1 || s.ce > 1) && !a.ws64) return (int)cudaErrorInvalidValue;
     const bool vec = vec_ok(a, s.kc);
     cudaStream_t st = (cudaStream_t)stream;

@@ -391,9 +391,7 @@ int launch_impl(const TcGemmArgs& a, void* stream) {
     p.row_exp = a.row_exp;
     p.col_exp = a.col_exp;
     p.err = a.err;
-    p.stall_chunk = -1;
-    for (int n = g_stall_launches.load(); n > 0;)
-        if (g_stall_launches.compare_exchange_weak(n, n - 1)) { p.stall_chunk = 1; break; }
+    p.stall_chunk = take_test_stall() ? 1 : -1;
     const int tiles = p.num_m * p.num_n;
     int grid = a.num_sms > 0 ? a.num_sms : 148;
     if (grid > tiles) grid = tiles;
@@ -416,6 +414,14 @@ int launch_tc_gemm(const TcGemmArgs& a, void* stream) {
     return a.fp16 ? launch_impl<true>(a, stream) : launch_impl<false>(a, stream);
 }
 
+}  // namespace emu
+
+namespace emu {
+bool take_test_stall() {
+    for (int n = g_stall_launches.load(); n > 0;)
+        if (g_stall_launches.compare_exchange_weak(n, n - 1)) return true;
+    return false;
+}
 }  // namespace emu
 
 extern "C" void emugemm_test_stall_next_launches(int n) { emu::g_stall_launches.store(n < 0 ? 0 : n); }

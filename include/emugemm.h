@@ -277,8 +277,10 @@ int emugemm_fp32_groups_tile(int M, int N, long K, int chunks, int num_sms, int 
    tensor-core kernel, from any entry point, make their MMA issuer wait before its second 128-K chunk on a
    barrier that nothing arrives on, with a 1 ms limit; the wait gives up and the kernel unwinds as after any
    timed-out wait (loads and MMAs in flight drained, TMEM freed, the timeout bit set in the error word), leaving
-   that launch's C incomplete. emugemm_sync (or emugemm_noalloc_sync) then returns EMUGEMM_STATUS_TIMEOUT. No
-   fault, trap or hang is involved; n = 0 cancels. */
+   that launch's C incomplete. The TMA-fed FP32 SIMT kernel (32 x 64 and 128 x 128 tiles) takes the hook the same
+   way: its threads give up such a wait once the first k-blocks are issued, no further k-block is loaded, the loads in
+   flight land before it exits, and its output is not meaningful. emugemm_sync (or emugemm_noalloc_sync) then
+   returns EMUGEMM_STATUS_TIMEOUT. No fault, trap or hang is involved; n = 0 cancels. */
 void emugemm_test_stall_next_launches(int n);
 
 /* ---- several GPUs of one node: one process (and one handle) per GPU, NCCL between them ---------------------------
