@@ -3,7 +3,7 @@ bench/gen_tune_table.cpp: offline, resumable, shardable, header written once und
 
 For every (M, N, K, dtype) of the grid it times the candidate kernels through the C ABI and appends one row
     arch,cuda_version,M,N,K,dtype,tile,best_ms,default_ms,gain
-where `tile` is the winner (bf16/fp16: 1 = single-CTA, 2 = CTA pair, 3 = fused split, 4 = A split into TMEM;
+where `tile` is the winner (bf16/fp16: 1 = single-CTA, 2 = CTA pair, 3 = fused split, 4 = A split into TMEM (bf16);
 fp32: SIMT tile 16 (16 x 32), 32, 64, 128 or 3264 (32 x 64)),
 `default_ms` the built-in choice's time and `gain` = default_ms / best_ms. Rows already present for a key are
 skipped, so an interrupted run resumes; --shard i/n takes every n-th shape starting at i (one process per GPU).
@@ -91,7 +91,7 @@ def tune_shape(h, M, N, K, dtype, reps):
 
     if dtype == "fp32":
         # time each SIMT tile by loading a one-row table per candidate
-        for tile in (128, 64, 32, 16):
+        for tile in (128, 64, 3264, 32, 16):
             tmp = pathlib.Path(f"/tmp/emugemm_tile_{os.getpid()}.csv")
             tmp.write_text(HEADER + f"{arch()},probe,{M},{N},{K},fp32,{tile},0,0,1\n")
             emugemm.lib().emugemm_init(str(tmp).encode())
@@ -100,7 +100,7 @@ def tune_shape(h, M, N, K, dtype, reps):
         emugemm.lib().emugemm_shutdown()
     else:
         kernels = (((1, "single"), (2, "pair"), (3, "fused"), (4, "fusea")) if dtype == "bf16"
-                   else ((1, "single"), (2, "pair")))
+                   else ((1, "single"), (2, "pair"), (3, "fused")))
         for tile, name in kernels:
             h.set_kernels(tc_kernel=name)
             res[tile] = timed()
