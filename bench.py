@@ -208,6 +208,17 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm), "window": window}
 
 
+def tensor_peak(ms_total: float, clocks: dict, burst: float, sustained: float) -> tuple[float, str]:
+    """The bf16 peak a tensor-core kernel's rate is compared with. A timed loop of more than half a second, or one
+    whose clock samples show the power cap holding the SM clock below 90 % of its maximum, runs under the power cap:
+    the sustained peak. Otherwise (a sw_power_cap flag seen at the full clock included) the burst peak."""
+    capped = ("sw_power_cap" in clocks.get("reasons", []) and clocks.get("sm_mhz") is not None
+              and bool(clocks.get("sm_max_mhz")) and clocks["sm_mhz"] < 0.9 * clocks["sm_max_mhz"])
+    if ms_total > 500.0 or capped:
+        return sustained, "bf16_tflops_sustained"
+    return burst, "bf16_tflops"
+
+
 def cpu_threads() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -615,15 +626,8 @@ def ours(args) -> None:
     launches_per_step = max(1, gemm_n // max(1, prof_steps))
     tensor_tflops = (rank_tensor_flop / launches_per_step / (gemm_avg * 1e-3) / 1e12) if gemm_n else None
     burst, sustained, hbm, src = peaks()
-    # a timed loop of more than half a second, or one whose clock samples show the power cap holding the SM clock
-    # below 90 % of its maximum, runs under the power cap: compare with the sustained peak (a sw_power_cap flag
-    # seen at the full clock leaves the burst peak)
     clocks = clk.summary()
-    capped = ("sw_power_cap" in clocks["reasons"] and clocks.get("sm_mhz") is not None
-              and clocks.get("sm_max_mhz") and clocks["sm_mhz"] < 0.9 * clocks["sm_max_mhz"])
-    long_loop = ms_total > 500.0 or bool(capped)
-    peak = sustained if long_loop else burst
-    peak_name = "bf16_tflops_sustained" if long_loop else "bf16_tflops"
+    peak, peak_name = tensor_peak(ms_total, clocks, burst, sustained)
     peak_source = f"{peak_name} ({src})"
     peak_probe = None
     if bound == "fp32":
