@@ -396,7 +396,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t lead_slot = mapa_shared(smem_u32(&ctl->sig_dst[cw][0]), 0);
             const uint32_t sig_src = smem_u32(&ctl->sig_src[0]);
             constexpr int kPer = (1024 + kConvThreads - 1) / kConvThreads;   // items per thread and k-block
-            constexpr int kBatch = 3;                                        // items loaded before any is stored
+            // items loaded before any is stored: 3 for bf16x3; 1 for fp16x3, whose split holds more registers per item
+            // (fewer spills: the long-K fp16x3 GEMM 0.212 -> 0.206 ms)
+            constexpr int kBatch = FP16 ? 1 : 3;
             long it = 0;
             bool ok = true;
             for (int u = pair; u < num_units && ok; u += num_pairs) {
